@@ -1,0 +1,315 @@
+"""Benchmark: the DeepSeek-V3-style Q4_K MoE layer (256 routed + 1 shared SwiGLU experts, hidden 7168,
+intermediate 2048, sigmoid group-limited top-8 routing, 8192 bf16 tokens) on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ck|reference]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
+
+One step = one MoE layer forward over all 8192 tokens (route, permute, grouped gate/up GEMM with
+SwiGLU, grouped down GEMM, combine; at N > 1 the experts are sharded 256/N per GPU and the token
+rows cross NVLink with NCCL all-to-alls).  Inputs are seeded synthetic tensors of the configuration's
+shapes and distributions; the weights (6.37 GB) are far larger than L2, so no flush is needed.
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "Q4_K MoE-layer tokens/s + weight-stream HBM GB/s at 1/2/4/8 B200 vs roofline"
+WORKLOAD = "dsv3-moe-layer: 256 routed + 1 shared Q4_K SwiGLU experts, hidden 7168, inter 2048, top-8 of 4/8 groups"
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(spec, w, tokens=2):
+    """The oracle (fp64 C restatement of the reference's Form recipes) on a bounded sample: `tokens`
+    whole tokens of the layer, one per host thread."""
+    from oracle import oracle as O
+    cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
+                    spec.topk_groups, spec.wscale)
+    toks = np.arange(tokens)
+    t0 = time.perf_counter()
+    O.moe_layer(cfg, w, w["x"], toks, nthreads=tokens)
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": tokens, "kind": "port",
+            "sample": f"{tokens} tokens of the layer end to end (router over 256 experts, 8 routed + 1 shared "
+                      f"SwiGLU experts, combine) on the oracle, one token per thread, {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    """The reference arm: the reference path's CPU implementation on the host cores, same workload."""
+    from coherence_kernel_b200 import workloads
+    if rank != 0:
+        return
+    spec = workloads.MOE_DSV3
+    nthreads = min(os.cpu_count() or 1, 16)
+    # only the experts the sampled tokens touch are needed; generate the full set lazily by id
+    probe = workloads.make_moe(spec, workloads.MOE_DSV3_TOKENS, seed=0, experts=[])
+    from oracle import oracle as O
+    cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
+                    spec.topk_groups, spec.wscale)
+    toks = np.arange(nthreads)
+    ids, _, _ = O.moe_route(cfg, probe["router"], probe["bias"], probe["x"][:nthreads], nthreads=nthreads)
+    used = sorted(set(ids.reshape(-1).tolist()))
+    sub = workloads.make_moe(spec, workloads.MOE_DSV3_TOKENS, seed=0, experts=used)
+    # place the touched experts at their ids in sparse full-size arrays is wasteful; remap instead
+    remap = {e: i for i, e in enumerate(used)}
+    mb = spec.matrix_bytes
+    full = {}
+    for k in ("gate", "up", "down"):
+        arr = np.zeros(spec.n_experts * mb, dtype=np.uint8)
+        for e in used:
+            arr[e * mb:(e + 1) * mb] = sub[k][remap[e] * mb:(remap[e] + 1) * mb]
+        full[k] = arr
+    for k in ("s_gate", "s_up", "s_down", "router", "bias", "x"):
+        full[k] = sub[k]
+    times = []
+    for _ in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        O.moe_layer(cfg, full, full["x"], toks, nthreads=nthreads)
+        times.append(time.perf_counter() - t0)
+    dt = sum(times[args.warmup:]) / max(1, args.steps)
+    value = nthreads / dt
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": workloads.MOE_DSV3_TOKENS,
+                       "sample_tokens_per_step": int(nthreads)},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                             "sample": f"{nthreads} tokens of the layer per step, one per host thread"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ck", choices=["ck", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from coherence_kernel_b200 import _lib, workloads
+    from coherence_kernel_b200.moe import ExpertParallelMoE, MoELayer
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    spec = workloads.MOE_DSV3
+    T_all = workloads.MOE_DSV3_TOKENS
+    T = T_all // world
+    el = spec.n_experts // world
+    experts = list(range(rank * el, (rank + 1) * el))
+    w = workloads.make_moe(spec, T_all, seed=0, experts=experts)
+    dev = torch.device("cuda", local)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    x_host = w["x"][rank * T:(rank + 1) * T]
+    x = t(x_host.view(np.int16))
+    wg, wu, wd = t(w["gate"]), t(w["up"]), t(w["down"])
+    sg, su, sd = t(w["s_gate"]), t(w["s_up"]), t(w["s_down"])
+    router, bias = t(w["router"]), t(w["bias"])
+    if world == 1:
+        layer = MoELayer(spec, wg, wu, wd, sg, su, sd, router, bias, max_tokens=T)
+    else:
+        layer = ExpertParallelMoE(spec, wg, wu, wd, sg, su, sd, router, bias, max_tokens=T)
+    out = torch.empty((T, spec.hidden), dtype=torch.bfloat16, device=dev)
+    ids = torch.empty((T, spec.nsel), dtype=torch.int32, device=dev)
+    wts = torch.empty((T, spec.nsel), dtype=torch.float32, device=dev)
+    counts = torch.empty(spec.n_experts, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    # per-step CUDA events between the layer's kernels (the dominant kernel is timed on its stream)
+    evs = []
+
+    def marks_factory():
+        rec = {}
+
+        def mark(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            rec[name] = e
+        return rec, mark
+
+    def step(record):
+        if world == 1:
+            rec, mark = marks_factory()
+            layer.forward_steps(x, out, ids, wts, counts, marks=mark if record else None)
+            if record:
+                evs.append(rec)
+        else:
+            layer.forward(x, out=out)
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    if world == 1:
+        layer.status(T)
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        m = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    ms_step = ms / args.steps
+    tokens_per_s = T_all / (ms_step / 1e3)
+
+    hbm, tc_burst, tc_sust, peak_src = peaks()
+    weight_bytes = (spec.n_experts + spec.n_shared) * 3 * spec.matrix_bytes
+    A = T * spec.nsel
+    roof = None
+    if world == 1 and evs:
+        gu = [r["permute"].elapsed_time(r["gate_up"]) for r in evs]
+        dn = [r["gate_up"].elapsed_time(r["down"]) for r in evs]
+        gu_ms = sum(gu) / len(gu)
+        flops_gu = 2.0 * (A + spec.n_shared * T) * 2 * spec.inter * spec.hidden
+        ach = flops_gu / (gu_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_sust, "unit": "TFLOP/s",
+                "frac": round(ach / tc_sust, 4), "traffic": None,
+                "kernel": "k_gemm_q4k<1> (grouped gate/up GEMM + SwiGLU)", "peak_source": f"{peak_src} sustained",
+                "kernel_ms": round(gu_ms, 4), "down_ms": round(sum(dn) / len(dn), 4),
+                "step_split_ms": {k: round(sum(r[b].elapsed_time(r[k]) for r in evs) / len(evs), 4)
+                                  for b, k in (("start", "route"), ("route", "permute"), ("permute", "gate_up"),
+                                               ("gate_up", "down"), ("down", "combine"))}}
+
+    # end to end through the public call: pinned host tokens in, host output back, every step
+    e2e = None
+    if world == 1:
+        xh = torch.from_numpy(np.ascontiguousarray(x_host.view(np.int16))).pin_memory()
+        oh = torch.empty((T, spec.hidden), dtype=torch.bfloat16).pin_memory()
+        xd = torch.empty_like(x)
+        for i in range(args.warmup + args.steps):
+            if i == args.warmup:
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            xd.copy_(xh, non_blocking=True)
+            layer(xd, out=out, ids=ids, wts=wts, counts=counts)
+            oh.copy_(out, non_blocking=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / args.steps
+        e2e = {"value": T_all / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(xh.numel() * 2),
+               "d2h_bytes_per_step": int(oh.numel() * 2), "ms_per_step": round(e_ms, 4)}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(spec, {k: w[k] for k in w}, tokens=2) if len(experts) == spec.n_experts else None
+        launches_per_step = 9 if world == 1 else 9 + 4 * spec.n_shared
+        line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": WORKLOAD, "tokens": T_all, "tokens_per_gpu": T,
+                           "experts_per_gpu": el, "parallelism": f"ep{world}" if world > 1 else "single",
+                           "l2": "weights 6.37 GB >> 126 MB L2 (no flush needed)"},
+                "weight_stream_gbs": round(weight_bytes / (ms_step / 1e3) / 1e9, 1),
+                "algorithmic_tflops": round(T_all * spec.flops_per_token() / (ms_step / 1e3) / 1e12, 1),
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "gpu_launches": launches_per_step * args.steps}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

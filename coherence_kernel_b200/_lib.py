@@ -1,0 +1,105 @@
+"""ctypes binding of libck_b200.so (the C ABI in include/ck_b200.h and include/fk_cuda_carrier.h).
+
+The library is the product: there is no fallback.  If it is missing or cannot be loaded the
+import of any op raises, loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libck_b200.so")
+
+_p = ctypes.c_void_p
+_u32 = ctypes.c_uint32
+_u64 = ctypes.c_uint64
+_i32 = ctypes.c_int
+_f = ctypes.c_float
+_ll = ctypes.c_longlong
+_sz = ctypes.c_size_t
+
+
+class MoeConfig(ctypes.Structure):
+    """ck_moe_config (include/ck_b200.h)."""
+    _fields_ = [("hidden", _u32), ("inter", _u32), ("n_experts", _u32), ("n_shared", _u32), ("nsel", _u32),
+                ("mode", _u32), ("ngroups", _u32), ("topk_groups", _u32), ("wscale", _f), ("tau", _f)]
+
+
+# name -> (restype, argtypes); every symbol include/*.h declares
+SIGNATURES = {
+    "ck_last_error": (ctypes.c_char_p, []),
+    "ck_device_ok": (_i32, []),
+    "ck_q8_0_dequant_f32": (_i32, [_p, _p, _u64, _u64, _p]),
+    "ck_q4k_dequant_f32": (_i32, [_p, _p, _u64, _u64, _p]),
+    "ck_q4k_dequant_bf16": (_i32, [_p, _p, _u64, _u64, _p]),
+    "ck_q8_0_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
+    "ck_q4k_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
+    "ck_matvec_ordered_f32": (_i32, [_i32, _p, _p, _p, _u32, _u32, _p]),
+    "ck_q4k_matmul_batch_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
+    "ck_q4k_gemm_workspace_bytes": (_sz, [_u32]),
+    "ck_q4k_gemm_bf16": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p, _sz, _p]),
+    "ck_f16_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
+    "ck_route_softmax_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _i32, _p]),
+    "ck_route_dsv4_f32": (_i32, [_p, _p, _p, _p, _u32, _u32, _f, _u32, _p]),
+    "ck_scale_f32": (_i32, [_p, _p, _f, _u32, _p]),
+    "ck_axpy_f32": (_i32, [_p, _p, _f, _u32, _p]),
+    "ck_swiglu_f32": (_i32, [_p, _p, _p, _u32, _f, _f, _p]),
+    "ck_moe_workspace_bytes": (_sz, [ctypes.POINTER(MoeConfig), _u32]),
+    "ck_moe_layer_bf16": (_i32, [ctypes.POINTER(MoeConfig), _p, _u32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                 _p, _sz, _p]),
+    "ck_moe_layer_status": (_i32, [ctypes.POINTER(MoeConfig), _u32, _p, _p]),
+    "ck_moe_route": (_i32, [ctypes.POINTER(MoeConfig), _p, _u32, _p, _p, _p, _p, _p, _p, _p]),
+    "ck_moe_permute_workspace_bytes": (_sz, [_u32, _u32, _u32]),
+    "ck_moe_max_tiles": (_u32, [_u32, _u32, _u32, _u32]),
+    "ck_moe_permute": (_i32, [_p, _p, _p, _u32, _u32, _u32, _u32, _u32, _i32, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "ck_moe_expert_gemm": (_i32, [_i32, _p, _p, _p, _p, _u64, _u32, _p, _u32, _p, _u32, _p, _p, _p, _u32, _u32, _u32,
+                                  _i32, _p, _p]),
+    "ck_moe_combine": (_i32, [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _i32, _p, _p, _p]),
+    "ck_token_tiles": (_i32, [_p, _p, _u32, _p]),
+    "ck_gather_rows": (_i32, [_p, _p, _p, _u32, _u32, _p]),
+    # the handle door
+    "fk_metal_pipeline_external": (_ll, [ctypes.c_char_p, _ll, ctypes.c_char_p, _ll]),
+    "fk_metal_buf_alloc_external": (_ll, [_ll]),
+    "fk_metal_buf_from_file_external": (_ll, [ctypes.c_char_p, _ll, _ll, _ll]),
+    "fk_metal_buf_write_external": (_ll, [_ll, _ll, ctypes.c_char_p, _ll]),
+    "fk_metal_enqueue_external": (_ll, [_ll, ctypes.c_char_p, _ll, _ll]),
+    "fk_metal_sync_external": (_ll, []),
+    "fk_metal_buf_read_external": (_ll, [_ll, _ll, _ll, ctypes.c_char_p, _ll]),
+    "fk_metal_status_external": (_ll, [ctypes.c_char_p, _ll]),
+    "fk_metal_batch_concurrent_external": (_ll, []),
+    "fk_metal_buf_free_external": (_ll, [_ll]),
+    "fk_metal_submit_external": (_ll, []),
+    "fk_metal_fence_wait_external": (_ll, [_ll]),
+    "fk_metal_matvec_fixture_external": (_ll, [ctypes.c_char_p, _ll]),
+    "fk_metal_matvec_f32_external": (_ll, [ctypes.c_char_p, _ll, ctypes.c_char_p, _ll, ctypes.c_char_p, _ll,
+                                           ctypes.c_char_p, _ll]),
+}
+
+_lib = None
+
+
+class CKError(RuntimeError):
+    pass
+
+
+def load():
+    """Load libck_b200.so; raise if it is absent (build it with ``python -m coherence_kernel_b200.build``)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise CKError(f"{LIB_PATH} is missing: the CUDA kernels are not built "
+                          "(python -m coherence_kernel_b200.build)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str = ""):
+    if rc != 0:
+        msg = load().ck_last_error().decode(errors="replace")
+        raise CKError(f"{what or 'ck call'} failed ({rc}): {msg}")

@@ -1,0 +1,327 @@
+// api.cu -- the extern "C" entry points declared in include/ck_b200.h.
+#include "../../include/ck_b200.h"
+#include "ck_common.cuh"
+#include "ck_launch.h"
+
+#include <stdio.h>
+#include <string.h>
+
+namespace {
+thread_local char g_err[512] = "none";
+
+int fail(int rc, const char *what) {
+    if (rc == 0) return 0;
+    const char *why = rc > 0 ? cudaGetErrorString((cudaError_t)rc)
+                             : rc == CK_ESHAPE ? "unsupported shape"
+                             : rc == CK_EARG ? "bad argument"
+                             : rc == CK_ETIMEOUT ? "device wait timed out"
+                             : rc == CK_ENODEV ? "no device / driver entry point"
+                                                : "error";
+    snprintf(g_err, sizeof(g_err), "%s: %s (%d)", what, why, rc);
+    return rc;
+}
+inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+inline size_t al(size_t b) { return (b + 255) & ~(size_t)255; }
+
+struct MoeWs {
+    float *logits;
+    uint32_t *flags;
+    void *perm_ws;
+    uint16_t *xp;
+    float *row_w;
+    int32_t *pair_pos;
+    int4 *tiles;
+    int32_t *ntiles;
+    uint16_t *h;
+    uint16_t *y;
+    int *err;
+    size_t total;
+};
+
+ck::PermuteParams perm_params(const ck_moe_config *c, uint32_t ntok) {
+    ck::PermuteParams p;
+    p.ntok = ntok;
+    p.nsel = c->nsel;
+    p.n_experts = c->n_experts;
+    p.n_shared = c->n_shared;
+    p.hidden = c->hidden;
+    p.bn = 256;
+    p.weight_in_mid = c->mode == 4 ? 1 : 0;
+    return p;
+}
+
+MoeWs moe_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
+    MoeWs w;
+    const size_t A = (size_t)ntok * c->nsel, XR = A + ntok, R = A + (size_t)c->n_shared * ntok;
+    const uint32_t mt = ck_moe_max_tiles(ntok, c->nsel, c->n_experts, c->n_shared);
+    uint8_t *b = (uint8_t *)base;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { uint8_t *p = b ? b + o : nullptr; o += al(bytes); return p; };
+    w.logits = (float *)take((size_t)ntok * c->n_experts * 4);
+    w.flags = (uint32_t *)take(((size_t)ntok + 1) * 4);
+    w.perm_ws = take(ck::permute_workspace_bytes(perm_params(c, ntok)));
+    w.xp = (uint16_t *)take(XR * c->hidden * 2);
+    w.row_w = (float *)take(R * 4);
+    w.pair_pos = (int32_t *)take(A * 4);
+    w.tiles = (int4 *)take((size_t)mt * 16);
+    w.ntiles = (int32_t *)take(4);
+    w.h = (uint16_t *)take(R * c->inter * 2);
+    w.y = (uint16_t *)take(R * c->hidden * 2);
+    w.err = (int *)take(4);
+    w.total = o;
+    return w;
+}
+
+int check_cfg(const ck_moe_config *c) {
+    if (!c) return CK_EARG;
+    if (c->n_experts == 0 || c->n_experts > 256 || c->nsel == 0 || c->nsel > 16 || c->nsel > c->n_experts)
+        return CK_ESHAPE;
+    if (c->hidden % 64 || c->inter % 64 || c->hidden == 0 || c->inter == 0) return CK_ESHAPE;
+    if (c->mode != 3 && c->mode != 4) return CK_EARG;
+    if (c->mode == 4 && (c->ngroups == 0 || c->ngroups > 32 || c->n_experts % c->ngroups || c->topk_groups == 0 ||
+                         c->topk_groups > c->ngroups))
+        return CK_ESHAPE;
+    return 0;
+}
+}  // namespace
+
+extern "C" {
+
+const char *ck_last_error(void) { return g_err; }
+
+int ck_device_ok(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return 0;
+    cudaDeviceProp prop;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return 0;
+    return prop.major == 10 ? 1 : 0;
+}
+
+int ck_q8_0_dequant_f32(const void *qb, float *w, uint64_t off, uint64_t n, void *s) {
+    if (!qb || !w) return fail(CK_EARG, "ck_q8_0_dequant_f32");
+    return fail(ck::launch_q80_dequant((const uint8_t *)qb, w, off, n, S(s)), "ck_q8_0_dequant_f32");
+}
+int ck_q4k_dequant_f32(const void *qb, float *w, uint64_t off, uint64_t n, void *s) {
+    if (!qb || !w) return fail(CK_EARG, "ck_q4k_dequant_f32");
+    return fail(ck::launch_q4k_dequant((const uint8_t *)qb, w, off, n, S(s)), "ck_q4k_dequant_f32");
+}
+int ck_q4k_dequant_bf16(const void *qb, void *w, uint64_t off, uint64_t n, void *s) {
+    if (!qb || !w) return fail(CK_EARG, "ck_q4k_dequant_bf16");
+    return fail(ck::launch_q4k_dequant_bf16((const uint8_t *)qb, w, off, n, S(s)), "ck_q4k_dequant_bf16");
+}
+int ck_q8_0_matvec_f32(const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, void *s) {
+    if (!qb || !x || !y || (reinterpret_cast<uintptr_t>(qb) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
+        return fail(CK_EARG, "ck_q8_0_matvec_f32");
+    return fail(ck::launch_q80_matvec((const uint8_t *)qb, x, y, rows, cols, S(s)), "ck_q8_0_matvec_f32");
+}
+int ck_q4k_matvec_f32(const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, void *s) {
+    if (!qb || !x || !y || (reinterpret_cast<uintptr_t>(qb) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
+        return fail(CK_EARG, "ck_q4k_matvec_f32");
+    return fail(ck::launch_q4k_matvec((const uint8_t *)qb, x, y, rows, cols, 1, S(s)), "ck_q4k_matvec_f32");
+}
+int ck_q4k_matmul_batch_f32(const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
+                            void *s) {
+    if (!qb || !x || !y || ntok == 0 || (reinterpret_cast<uintptr_t>(qb) & 15) ||
+        (reinterpret_cast<uintptr_t>(x) & 15))
+        return fail(CK_EARG, "ck_q4k_matmul_batch_f32");
+    return fail(ck::launch_q4k_matvec((const uint8_t *)qb, x, y, rows, cols, ntok, S(s)), "ck_q4k_matmul_batch_f32");
+}
+int ck_matvec_ordered_f32(int t, const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, void *s) {
+    if (!qb || !x || !y || (t != 8 && t != 12)) return fail(CK_EARG, "ck_matvec_ordered_f32");
+    if ((t == 8 && cols % 32) || (t == 12 && ((uint64_t)rows * cols) % 256)) return fail(CK_ESHAPE, "ck_matvec_ordered_f32");
+    return fail(ck::launch_matvec_ordered(t, (const uint8_t *)qb, x, y, rows, cols, S(s)), "ck_matvec_ordered_f32");
+}
+
+size_t ck_q4k_gemm_workspace_bytes(uint32_t ntok) { return al(((size_t)ntok / 16 + 2) * 16) + 256 + 256; }
+
+int ck_q4k_gemm_bf16(const void *qb, const void *x, void *y, uint32_t rows, uint32_t cols, uint32_t ntok, void *ws,
+                     size_t wsb, void *s) {
+    if (!qb || !x || !y || !ws) return fail(CK_EARG, "ck_q4k_gemm_bf16");
+    if (wsb < ck_q4k_gemm_workspace_bytes(ntok)) return fail(CK_EARG, "ck_q4k_gemm_bf16 workspace");
+    if (ntok == 0) return 0;
+    uint8_t *b = (uint8_t *)ws;
+    const size_t tb = al(((size_t)ntok / 16 + 2) * 16);
+    int4 *tiles = (int4 *)b;
+    int32_t *ntiles = (int32_t *)(b + tb);
+    int *err = (int *)(b + tb + 256);
+    cudaMemsetAsync(err, 0, 4, S(s));
+    int rc = ck::launch_single_tiles(tiles, ntiles, ntok, 256, S(s));
+    if (rc) return fail(rc, "ck_q4k_gemm_bf16 tiles");
+    ck::GemmParams p = {};
+    p.w0 = (const uint8_t *)qb;
+    p.w_stride = 0;
+    p.x = x;
+    p.x_rows = ntok;
+    p.out = y;
+    p.out_rows = ntok;
+    p.tiles = tiles;
+    p.ntiles = ntiles;
+    p.max_tiles = (uint32_t)(ntok / 16 + 2);
+    p.n_routed = 1;
+    p.N = rows;
+    p.K = cols;
+    p.dual = 0;
+    p.err = err;
+    return fail(ck::launch_gemm_q4k(p, S(s)), "ck_q4k_gemm_bf16");
+}
+
+int ck_f16_matvec_f32(const void *w, const float *x, float *y, uint32_t rows, uint32_t cols, void *s) {
+    if (!w || !x || !y) return fail(CK_EARG, "ck_f16_matvec_f32");
+    return fail(ck::launch_f16_matvec((const uint16_t *)w, x, y, rows, cols, S(s)), "ck_f16_matvec_f32");
+}
+int ck_route_softmax_f32(const float *L, uint32_t *ids, float *wts, uint32_t ne, uint32_t nsel, uint32_t ntok,
+                         int renorm, void *s) {
+    if (!L || !ids || !wts) return fail(CK_EARG, "ck_route_softmax_f32");
+    return fail(ck::launch_route_softmax_tokens(L, ids, wts, ne, nsel, ntok, renorm, S(s)), "ck_route_softmax_f32");
+}
+int ck_route_dsv4_f32(const float *L, const float *bias, uint32_t *ids, float *wts, uint32_t ne, uint32_t nused,
+                      float wscale, uint32_t ntok, void *s) {
+    if (!L || !bias || !ids || !wts) return fail(CK_EARG, "ck_route_dsv4_f32");
+    return fail(ck::launch_route_dsv4_tokens(L, bias, ids, wts, ne, nused, wscale, ntok, S(s)), "ck_route_dsv4_f32");
+}
+int ck_scale_f32(const float *x, float *y, float a, uint32_t n, void *s) {
+    if (!x || !y) return fail(CK_EARG, "ck_scale_f32");
+    return fail(ck::launch_scale(x, y, a, n, S(s)), "ck_scale_f32");
+}
+int ck_axpy_f32(const float *x, float *y, float a, uint32_t n, void *s) {
+    if (!x || !y) return fail(CK_EARG, "ck_axpy_f32");
+    return fail(ck::launch_axpy(x, y, a, n, S(s)), "ck_axpy_f32");
+}
+int ck_swiglu_f32(const float *g, const float *u, float *o, uint32_t n, float w, float lim, void *s) {
+    if (!g || !u || !o) return fail(CK_EARG, "ck_swiglu_f32");
+    return fail(ck::launch_swiglu(g, u, o, n, w, lim, S(s)), "ck_swiglu_f32");
+}
+
+// ------------------------------------------------------------------------------ MoE layer
+uint32_t ck_moe_max_tiles(uint32_t ntok, uint32_t nsel, uint32_t n_experts, uint32_t n_shared) {
+    const uint64_t A = (uint64_t)ntok * nsel;
+    return (uint32_t)(n_experts + A / 128 + 1 + (uint64_t)n_shared * (ntok / 128 + 2));
+}
+size_t ck_moe_permute_workspace_bytes(uint32_t ntok, uint32_t nsel, uint32_t n_experts) {
+    ck::PermuteParams p = {};
+    p.ntok = ntok;
+    p.nsel = nsel;
+    p.n_experts = n_experts;
+    return ck::permute_workspace_bytes(p);
+}
+size_t ck_moe_workspace_bytes(const ck_moe_config *c, uint32_t ntok) {
+    if (check_cfg(c)) return 0;
+    return moe_ws(c, ntok, nullptr).total;
+}
+
+int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const float *rw, const float *bias,
+                 float *logits, int32_t *ids, float *wts, uint32_t *flags, void *s) {
+    int rc = check_cfg(c);
+    if (rc) return fail(rc, "ck_moe_route config");
+    if (!x || !rw || !logits || !ids || !wts || !flags || (c->mode == 4 && !bias)) return fail(CK_EARG, "ck_moe_route");
+    rc = ck::launch_router_logits((const uint16_t *)x, rw, logits, ntok, c->n_experts, c->hidden, S(s));
+    if (rc) return fail(rc, "ck_moe_route logits");
+    ck::RouteParams p = {ntok, c->n_experts, c->nsel, c->hidden, c->mode, c->ngroups, c->topk_groups, c->wscale, c->tau};
+    rc = ck::launch_route_select(logits, bias, ids, wts, flags + 1, flags, p, S(s));
+    if (rc) return fail(rc, "ck_moe_route select");
+    rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, flags + 1, flags, p, S(s));
+    return fail(rc, "ck_moe_route exact");
+}
+
+int ck_moe_permute(const int32_t *ids, const float *wts, const void *x, uint32_t ntok, uint32_t nsel,
+                   uint32_t n_experts, uint32_t n_shared, uint32_t hidden, int weight_in_mid, void *xp, float *row_w,
+                   int32_t *pair_pos, int32_t *counts, void *tiles, int32_t *ntiles, void *ws, void *s) {
+    ck::PermuteParams p = {ntok, nsel, n_experts, n_shared, hidden, 256, (uint32_t)(weight_in_mid ? 1 : 0)};
+    return fail(ck::launch_permute(ids, wts, (const uint16_t *)x, (uint16_t *)xp, row_w, pair_pos, counts,
+                                   (int4 *)tiles, ntiles, ws, p, S(s)),
+                "ck_moe_permute");
+}
+
+int ck_moe_expert_gemm(int dual, const void *w0, const void *w1, const void *s0, const void *s1, uint64_t w_stride,
+                       uint32_t n_routed, const void *x, uint32_t x_rows, void *out, uint32_t out_rows,
+                       const float *row_w, const void *tiles, const int32_t *ntiles, uint32_t max_tiles, uint32_t n,
+                       uint32_t k, int xrow_is_orow, int *err, void *s) {
+    ck::GemmParams p = {};
+    p.w0 = (const uint8_t *)w0;
+    p.w1 = (const uint8_t *)w1;
+    p.s0 = (const uint8_t *)s0;
+    p.s1 = (const uint8_t *)s1;
+    p.w_stride = w_stride;
+    p.x = x;
+    p.x_rows = x_rows;
+    p.out = out;
+    p.out_rows = out_rows;
+    p.row_w = row_w;
+    p.tiles = (const int4 *)tiles;
+    p.ntiles = ntiles;
+    p.max_tiles = max_tiles;
+    p.n_routed = n_routed;
+    p.N = n;
+    p.K = k;
+    p.dual = dual;
+    p.xrow_is_orow = xrow_is_orow;
+    p.err = err;
+    return fail(ck::launch_gemm_q4k(p, S(s)), "ck_moe_expert_gemm");
+}
+
+int ck_moe_combine(const void *y, const int32_t *ids, const float *wts, const int32_t *pair_pos, uint32_t ntok,
+                   uint32_t nsel, uint32_t n_shared, uint32_t hidden, int order_by_expert, void *out, float *out_f32,
+                   void *s) {
+    ck::PermuteParams p = {ntok, nsel, 0, n_shared, hidden, 256, 0};
+    return fail(ck::launch_combine((const uint16_t *)y, ids, wts, pair_pos, (uint16_t *)out, out_f32, p,
+                                   order_by_expert, S(s)),
+                "ck_moe_combine");
+}
+
+int ck_token_tiles(void *tiles, int32_t *ntiles, uint32_t ntok, void *s) {
+    return fail(ck::launch_single_tiles((int4 *)tiles, ntiles, ntok, 256, S(s)), "ck_token_tiles");
+}
+
+int ck_gather_rows(const void *src, const int32_t *idx, void *dst, uint32_t nrows, uint32_t row_bytes, void *s) {
+    return fail(ck::launch_gather_rows(src, idx, dst, nrows, row_bytes, S(s)), "ck_gather_rows");
+}
+
+int ck_moe_layer_bf16(const ck_moe_config *c, const void *x, uint32_t ntok, const void *wg, const void *wu,
+                      const void *wd, const void *sg, const void *su, const void *sd, const float *rw,
+                      const float *bias, int32_t *ids, float *wts, int32_t *counts, void *out, void *ws, size_t wsb,
+                      void *s) {
+    int rc = check_cfg(c);
+    if (rc) return fail(rc, "ck_moe_layer_bf16 config");
+    if (!x || !wg || !wu || !wd || !rw || !ids || !wts || !counts || !out || !ws) return fail(CK_EARG, "ck_moe_layer_bf16");
+    if (c->n_shared && (!sg || !su || !sd)) return fail(CK_EARG, "ck_moe_layer_bf16 shared weights");
+    if (wsb < ck_moe_workspace_bytes(c, ntok)) return fail(CK_EARG, "ck_moe_layer_bf16 workspace");
+    if (ntok == 0) return 0;
+    MoeWs w = moe_ws(c, ntok, ws);
+    cudaStream_t st = S(s);
+    cudaMemsetAsync(w.err, 0, 4, st);
+    rc = ck_moe_route(c, x, ntok, rw, bias, w.logits, ids, wts, w.flags, s);
+    if (rc) return rc;
+    const uint32_t A = ntok * c->nsel, R = A + c->n_shared * ntok;
+    rc = ck_moe_permute(ids, wts, x, ntok, c->nsel, c->n_experts, c->n_shared, c->hidden, c->mode == 4, w.xp, w.row_w,
+                        w.pair_pos, counts, w.tiles, w.ntiles, w.perm_ws, s);
+    if (rc) return rc;
+    const uint32_t mt = ck_moe_max_tiles(ntok, c->nsel, c->n_experts, c->n_shared);
+    const uint64_t stride = (uint64_t)c->inter * c->hidden / 256 * 144;
+    rc = ck_moe_expert_gemm(1, wg, wu, sg, su, stride, c->n_experts, w.xp, A + ntok, w.h, R, w.row_w, w.tiles, w.ntiles,
+                            mt, c->inter, c->hidden, 0, w.err, s);
+    if (rc) return rc;
+    rc = ck_moe_expert_gemm(0, wd, nullptr, sd, nullptr, stride, c->n_experts, w.h, R, w.y, R, nullptr, w.tiles,
+                            w.ntiles, mt, c->hidden, c->inter, 1, w.err, s);
+    if (rc) return rc;
+    return ck_moe_combine(w.y, ids, wts, w.pair_pos, ntok, c->nsel, c->n_shared, c->hidden, c->mode == 3, out, nullptr,
+                          s);
+}
+
+// Reads the device error word of a layer's workspace (synchronizes the stream).
+int ck_moe_layer_status(const ck_moe_config *c, uint32_t ntok, const void *ws, void *s) {
+    if (check_cfg(c) || !ws) return fail(CK_EARG, "ck_moe_layer_status");
+    MoeWs w = moe_ws(c, ntok, const_cast<void *>(ws));
+    int e = 0;
+    cudaError_t r = cudaMemcpyAsync(&e, w.err, 4, cudaMemcpyDeviceToHost, S(s));
+    if (r == cudaSuccess) r = cudaStreamSynchronize(S(s));
+    if (r != cudaSuccess) return fail((int)r, "ck_moe_layer_status");
+    if (e) {
+        snprintf(g_err, sizeof(g_err), "ck_moe_layer_bf16: device wait timed out (role code %d)", e);
+        return CK_ETIMEOUT;
+    }
+    return 0;
+}
+
+}  // extern "C"

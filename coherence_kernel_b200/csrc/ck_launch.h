@@ -1,0 +1,85 @@
+// ck_launch.h -- internal launcher declarations shared by the kernel files and the C-ABI layer.
+// Launchers return 0 on success, a positive cudaError_t, or one of the negative CK_ERR_* codes.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define CK_ERR_SHAPE (-2)    // a size the kernel does not support (stated in the entry point's doc)
+#define CK_ERR_ARG (-3)      // a null pointer or an out-of-range argument
+#define CK_ERR_TIMEOUT (-4)  // a device-side bounded wait gave up (the kernel returned early)
+#define CK_ERR_NODEV (-5)    // no CUDA device, or the driver entry point is unavailable
+
+namespace ck {
+
+int launch_q80_dequant(const uint8_t *qb, float *w, uint64_t off, uint64_t n, cudaStream_t s);
+int launch_q4k_dequant(const uint8_t *qb, float *w, uint64_t off, uint64_t n, cudaStream_t s);
+int launch_q4k_dequant_bf16(const uint8_t *qb, void *w, uint64_t off, uint64_t n, cudaStream_t s);
+int launch_matvec_ordered(int kind, const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols,
+                          cudaStream_t s);
+int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
+                      cudaStream_t s);
+int launch_q80_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
+int launch_f16_matvec(const uint16_t *w, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
+int launch_scale(const float *x, float *y, float a, uint32_t n, cudaStream_t s);
+int launch_axpy(const float *x, float *y, float a, uint32_t n, cudaStream_t s);
+int launch_swiglu(const float *g, const float *u, float *out, uint32_t n, float w, float lim, cudaStream_t s);
+
+// routers (router_kernels.cu)
+int launch_route_softmax_tokens(const float *logits, uint32_t *ids, float *wts, uint32_t ne, uint32_t nsel,
+                                uint32_t ntok, int renorm, cudaStream_t s);
+int launch_route_dsv4_tokens(const float *logits, const float *bias, uint32_t *ids, float *wts, uint32_t ne,
+                             uint32_t nused, float wscale, uint32_t ntok, cudaStream_t s);
+int launch_router_logits(const uint16_t *x_bf16, const float *w, float *logits, uint32_t ntok, uint32_t ne,
+                         uint32_t hidden, cudaStream_t s);
+struct RouteParams {
+    uint32_t ntok, ne, nsel, hidden;
+    uint32_t mode;         // 3: softmax top-k (no renorm); 4: sigmoid + bias, group-limited
+    uint32_t ngroups, topk_groups;
+    float wscale;          // mode 4 weight scale
+    float tau;             // decision margin below which a token is re-routed exactly in fp64
+};
+int launch_route_select(const float *logits, const float *bias, int32_t *ids, float *wts, uint32_t *flag_list,
+                        uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
+int launch_route_exact(const uint16_t *x_bf16, const float *w, const float *bias, int32_t *ids, float *wts,
+                       const uint32_t *flag_list, const uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
+
+// MoE permute / combine (moe_kernels.cu)
+struct PermuteParams {
+    uint32_t ntok, nsel, n_experts, n_shared, hidden;
+    uint32_t bn;           // token tile of the grouped GEMM
+    uint32_t weight_in_mid;  // 1: the route weight scales the SwiGLU product (dsv4); 0: combine
+};
+size_t permute_workspace_bytes(const PermuteParams &p);
+int launch_permute(const int32_t *ids, const float *wts, const uint16_t *x_bf16, uint16_t *xp, float *row_w,
+                   int32_t *pair_pos, int32_t *counts, int4 *tiles, int32_t *ntiles, void *workspace,
+                   const PermuteParams &p, cudaStream_t s);
+int launch_single_tiles(int4 *tiles, int32_t *ntiles, uint32_t ntok, uint32_t bn, cudaStream_t s);
+int launch_gather_rows(const void *src, const int32_t *idx, void *dst, uint32_t nrows, uint32_t row_bytes,
+                       cudaStream_t s);
+int launch_combine(const uint16_t *y, const int32_t *ids, const float *wts, const int32_t *pair_pos, uint16_t *out,
+                   float *out_f32, const PermuteParams &p, int order_by_expert, cudaStream_t s);
+
+// tcgen05 grouped Q4_K GEMM (gemm_tc.cu)
+struct GemmParams {
+    const uint8_t *w0;       // routed weights (gate, or the only matrix), expert g at w0 + g*w_stride
+    const uint8_t *w1;       // routed up weights (dual mode), same stride
+    const uint8_t *s0;       // shared-expert weights, expert s at s0 + s*w_stride
+    const uint8_t *s1;
+    uint64_t w_stride;       // bytes per expert matrix
+    const void *x;           // bf16 activations [x_rows, K], rows addressed by the tile table
+    uint32_t x_rows;
+    void *out;               // bf16 output [out_rows, N]
+    uint32_t out_rows;
+    const float *row_w;      // per output row weight (dual mode; null = 1)
+    const int4 *tiles;       // (group, x_row, out_row, ntok) per token tile
+    const int32_t *ntiles;   // device-side tile count
+    uint32_t max_tiles;
+    uint32_t n_routed;       // groups >= n_routed use the shared weights
+    uint32_t N, K;           // output features (weight rows), reduction length
+    int dual;                // 1: out = silu(x.W0) * (x.W1) * row_w ; 0: out = x.W0
+    int xrow_is_orow;        // 1: read X at the tile's output row (the down projection over H)
+    int *err;                // device error word (bounded waits)
+};
+int launch_gemm_q4k(const GemmParams &p, cudaStream_t s);
+
+}  // namespace ck

@@ -1,0 +1,501 @@
+// router_kernels.cu -- MoE gating: router logits, top-k selection, and the exact fp64 re-route.
+//
+// Selection semantics are the reference's: top-k by repeated argmax where a strict '>' keeps the
+// LOWER expert index on a tie (moe-msl.fk:84-98 mm-argmax-free, dsv4-forward.fk:72-81
+// dsv4-argmax).  The batched layer routes in three steps:
+//   1. k_router_logits   fp32 logits = x . W_r (bf16 x, fp32 W_r)
+//   2. k_route_select    one warp per token: selection, weights, and the token's decision margin
+//                        (the smallest gap between a chosen and a rejected candidate)
+//   3. k_route_exact     tokens whose margin is below tau are routed again in fp64 with the
+//                        reference's own fold order and numerics (tb-dot right fold, tn-exp,
+//                        ln-sigmoid), so their expert ids are the reference's bit for bit.
+#include "ck_common.cuh"
+#include "ck_launch.h"
+
+namespace ck {
+
+// ------------------------------------------------------------------ warp argmax
+// (value, index) maximum with the lower index winning ties.
+CK_DEV void warp_argmax(float &v, int &i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+    }
+}
+CK_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ------------------------------------------------------------------ 1. logits
+// L[t, e] = sum_j x[t, j] * W[e, j]; 64 tokens x 64 experts per block, 4x4 per thread.
+__global__ void __launch_bounds__(256) k_router_logits(const uint16_t *__restrict__ x, const float *__restrict__ w,
+                                                       float *__restrict__ L, uint32_t T, uint32_t E, uint32_t H) {
+    __shared__ float xs[32][64 + 4];
+    __shared__ float ws[32][64 + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const uint32_t t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+    float acc[4][4] = {};
+    for (uint32_t k0 = 0; k0 < H; k0 += 32) {
+        for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+            const int r = i >> 5, k = i & 31;
+            const uint32_t t = t0 + r, e = e0 + r, kk = k0 + k;
+            xs[k][r] = (t < T && kk < H) ? bf16_bits_to_float(x[(size_t)t * H + kk]) : 0.0f;
+            ws[k][r] = (e < E && kk < H) ? w[(size_t)e * H + kk] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+            const float4 xv = *reinterpret_cast<const float4 *>(&xs[k][ty * 4]);
+            const float4 wv = *reinterpret_cast<const float4 *>(&ws[k][tx * 4]);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(xa[a], wa[b], acc[a][b]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t t = t0 + ty * 4 + a, e = e0 + tx * 4 + b;
+            if (t < T && e < E) L[(size_t)t * E + e] = acc[a][b];
+        }
+}
+
+// ------------------------------------------------------------------ 2. fast selection
+// One warp per token; lane l holds experts e = 32*i + l.  At most 256 experts, 16 selections.
+constexpr int RMAX = 8;
+__global__ void k_route_select(const float *__restrict__ L, const float *__restrict__ bias, int32_t *__restrict__ ids,
+                               float *__restrict__ wts, uint32_t *__restrict__ flag_list,
+                               uint32_t *__restrict__ flag_count, RouteParams p) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= p.ntok) return;
+    const float NEG = -3.0e38f;
+    float sc[RMAX], pr[RMAX];
+    const int nreg = (int)((p.ne + 31) / 32);
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i) {
+        const int e = 32 * i + lane;
+        const bool v = i < nreg && e < (int)p.ne;
+        const float l = v ? L[(size_t)t * p.ne + e] : NEG;
+        if (p.mode == 4) {
+            pr[i] = v ? 1.0f / (1.0f + expf(-l)) : 0.0f;
+            sc[i] = v ? pr[i] + bias[e] : NEG;
+        } else {
+            pr[i] = l;
+            sc[i] = l;
+        }
+    }
+    float margin = 3.0e38f;
+    bool allowed[RMAX];
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i) allowed[i] = true;
+    if (p.mode == 4 && p.ngroups > 1) {
+        // group score = sum of the group's two best scores (ties: lower index first, like dsv4-topk)
+        const int gs = (int)(p.ne / p.ngroups);
+        float gsc[32];
+        for (int g = 0; g < (int)p.ngroups; ++g) {
+            float b1 = NEG, b2 = NEG;
+            int i1 = 1 << 30;
+#pragma unroll
+            for (int i = 0; i < RMAX; ++i) {
+                const int e = 32 * i + lane;
+                if (e / gs == g && sc[i] > b1) { b1 = sc[i]; i1 = e; }
+            }
+            float v = b1;
+            int vi = i1;
+            warp_argmax(v, vi);
+            const float best = v;
+#pragma unroll
+            for (int i = 0; i < RMAX; ++i) {
+                const int e = 32 * i + lane;
+                if (e / gs == g && e != vi && sc[i] > b2) b2 = sc[i];
+            }
+            int dummy = 0;
+            warp_argmax(b2, dummy);
+            gsc[g] = b2 + best;  // tn-sum over (second, best): (0 + second) + best
+        }
+        // top groups by repeated argmax; the margin is min(chosen) - max(rejected)
+        unsigned gmask = 0;
+        float gmin = 3.0e38f;
+        for (int r = 0; r < (int)p.topk_groups; ++r) {
+            float bv = NEG;
+            int bi = 0;
+            for (int g = 0; g < (int)p.ngroups; ++g)
+                if (!(gmask >> g & 1) && gsc[g] > bv) { bv = gsc[g]; bi = g; }
+            gmask |= 1u << bi;
+            gmin = fminf(gmin, bv);
+        }
+        float gmax = NEG;
+        for (int g = 0; g < (int)p.ngroups; ++g)
+            if (!(gmask >> g & 1)) gmax = fmaxf(gmax, gsc[g]);
+        if ((int)p.topk_groups < (int)p.ngroups) margin = fminf(margin, gmin - gmax);
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i) {
+            const int e = 32 * i + lane;
+            allowed[i] = e < (int)p.ne && (gmask >> (e / gs) & 1);
+        }
+    }
+    // expert selection, best first
+    int sel[16];
+    float selv[16];
+    const int k = (int)p.nsel;
+    for (int r = 0; r < k; ++r) {
+        float bv = NEG;
+        int bi = 1 << 30;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (allowed[i] && sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
+        warp_argmax(bv, bi);
+        sel[r] = bi;
+        selv[r] = bv;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (32 * i + lane == bi) allowed[i] = false;
+    }
+    {
+        float bv = NEG;
+        int bi = 1 << 30;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (allowed[i] && sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
+        warp_argmax(bv, bi);
+        if (bv > NEG) margin = fminf(margin, selv[k - 1] - bv);
+    }
+    // weights
+    float w[16];
+    if (p.mode == 4) {
+        // dsv4-topk lists the picks last-first; weights from the unbiased probs, sum floored at
+        // 2^-14, times wscale / sum (dsv4-forward.fk:105-111)
+        float s0 = 0.0f;
+        for (int r = 0; r < k; ++r) {
+            const int e = sel[k - 1 - r];
+            float pe = 0.0f;
+#pragma unroll
+            for (int i = 0; i < RMAX; ++i)
+                if (32 * i + lane == e) pe = pr[i];
+            pe = __shfl_sync(0xffffffffu, pe, e & 31);
+            w[r] = pe;
+            s0 += pe;
+        }
+        const float s = s0 < 6.103515625e-05f ? 6.103515625e-05f : s0;
+        const float scl = p.wscale / s;
+        for (int r = 0; r < k; ++r) w[r] *= scl;
+        if (lane == 0)
+            for (int r = 0; r < k; ++r) {
+                ids[(size_t)t * k + r] = sel[k - 1 - r];
+                wts[(size_t)t * k + r] = w[r];
+            }
+    } else {
+        // softmax over all experts (max-subtracted), the chosen probabilities, best first
+        float mx = NEG;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i) mx = fmaxf(mx, sc[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (32 * i + lane < (int)p.ne) s += expf(sc[i] - mx);
+        s = warp_sum(s);
+        if (lane == 0)
+            for (int r = 0; r < k; ++r) {
+                ids[(size_t)t * k + r] = sel[r];
+                wts[(size_t)t * k + r] = expf(selv[r] - mx) / s;
+            }
+    }
+    if (lane == 0 && !(margin >= p.tau)) {
+        const uint32_t slot = atomicAdd(flag_count, 1u);
+        flag_list[slot] = t;
+    }
+}
+
+// ------------------------------------------------------------------ 3. exact fp64 re-route
+// The reference's numerics in fp64 with explicit round-to-nearest operations (no contraction):
+// transformer-numerics.fk:16-24 tn-exp, llama-numerics.fk:29 ln-sigmoid.
+CK_DEV double ref_exp(double x) {
+    int k = 0;
+    for (;;) {
+        const double ax = x < 0.0 ? 0.0 - x : x;
+        if (ax <= 0.5) break;
+        x = __ddiv_rn(x, 2.0);
+        ++k;
+    }
+    double n = 1.0, term = 1.0, acc = 1.0;
+    while (!(n > 14.0)) {
+        const double tt = __dmul_rn(term, __ddiv_rn(x, n));
+        acc = __dadd_rn(acc, tt);
+        term = tt;
+        n = __dadd_rn(n, 1.0);
+    }
+    for (int i = 0; i < k; ++i) acc = __dmul_rn(acc, acc);
+    return acc;
+}
+CK_DEV double ref_sigmoid(double x) { return __ddiv_rn(1.0, __dadd_rn(1.0, ref_exp(__dsub_rn(0.0, x)))); }
+
+// dsv4-topk over n values in smem: repeated first-maximum, winners set to -1e9, list last-first
+CK_DEV void ref_topk(double *s, int n, int k, int *out) {
+    for (int r = 0; r < k; ++r) {
+        double best = s[0];
+        int bi = 0;
+        for (int i = 1; i < n; ++i)
+            if (s[i] > best) { best = s[i]; bi = i; }
+        s[bi] = -1000000000.0;
+        out[k - 1 - r] = bi;
+    }
+}
+
+constexpr int EX_THREADS = 256;
+constexpr int EX_MAXE = 256;
+__global__ void __launch_bounds__(EX_THREADS) k_route_exact(const uint16_t *__restrict__ x, const float *__restrict__ W,
+                                                            const float *__restrict__ bias, int32_t *__restrict__ ids,
+                                                            float *__restrict__ wts, const uint32_t *__restrict__ flag_list,
+                                                            const uint32_t *__restrict__ flag_count, RouteParams p) {
+    __shared__ float wtile[EX_MAXE][33];
+    __shared__ double xtile[32];
+    __shared__ double lg[EX_MAXE], sc[EX_MAXE], tmp[EX_MAXE];
+    const uint32_t nflag = *flag_count;
+    for (uint32_t f = blockIdx.x; f < nflag; f += gridDim.x) {
+        const uint32_t t = flag_list[f];
+        // logits: right fold over j descending, acc = w*x + acc in fp64 (transformer-block.fk:25-26)
+        double acc[EX_MAXE / EX_THREADS];
+        for (int q = 0; q < EX_MAXE / EX_THREADS; ++q) acc[q] = 0.0;
+        for (int j0 = (int)p.hidden - 32; j0 >= 0; j0 -= 32) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < (int)p.ne * 32; i += EX_THREADS) {
+                const int e = i >> 5, j = i & 31;
+                wtile[e][j] = W[(size_t)e * p.hidden + j0 + j];
+            }
+            if (threadIdx.x < 32) xtile[threadIdx.x] = (double)bf16_bits_to_float(x[(size_t)t * p.hidden + j0 + threadIdx.x]);
+            __syncthreads();
+            for (int q = 0; q < EX_MAXE / EX_THREADS; ++q) {
+                const int e = threadIdx.x + q * EX_THREADS;
+                if (e < (int)p.ne) {
+                    double a = acc[q];
+                    for (int j = 31; j >= 0; --j) a = __dadd_rn(__dmul_rn((double)wtile[e][j], xtile[j]), a);
+                    acc[q] = a;
+                }
+            }
+        }
+        for (int q = 0; q < EX_MAXE / EX_THREADS; ++q) {
+            const int e = threadIdx.x + q * EX_THREADS;
+            if (e < (int)p.ne) lg[e] = acc[q];
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int ne = (int)p.ne, k = (int)p.nsel;
+            int sel[16];
+            double w[16];
+            if (p.mode == 4) {
+                for (int e = 0; e < ne; ++e) {
+                    lg[e] = ref_sigmoid(lg[e]);  // probs
+                    sc[e] = __dadd_rn(lg[e], (double)bias[e]);
+                }
+                const int ng = (int)p.ngroups, gs = ne / ng;
+                double gsc[64];
+                for (int g = 0; g < ng; ++g) {
+                    int two[2];
+                    for (int i = 0; i < gs; ++i) tmp[i] = sc[g * gs + i];
+                    ref_topk(tmp, gs, 2, two);
+                    gsc[g] = __dadd_rn(__dadd_rn(0.0, sc[g * gs + two[0]]), sc[g * gs + two[1]]);
+                }
+                int gsel[64];
+                ref_topk(gsc, ng, (int)p.topk_groups, gsel);
+                unsigned long long gon = 0;
+                for (int i = 0; i < (int)p.topk_groups; ++i) gon |= 1ull << gsel[i];
+                for (int e = 0; e < ne; ++e) tmp[e] = (gon >> (e / gs) & 1) ? sc[e] : -1000000000.0;
+                ref_topk(tmp, ne, k, sel);
+                double s0 = 0.0;
+                for (int i = 0; i < k; ++i) s0 = __dadd_rn(s0, lg[sel[i]]);
+                const double s = s0 < 0.00006103515625 ? 0.00006103515625 : s0;
+                const double scl = __ddiv_rn((double)p.wscale, s);
+                for (int i = 0; i < k; ++i) w[i] = __dmul_rn(lg[sel[i]], scl);
+            } else {
+                // mm-softmax / mm-topk / mm-gather (moe-msl.fk:73-99), no renormalization
+                double mx = lg[0];
+                for (int e = 1; e < ne; ++e)
+                    if (lg[e] > mx) mx = lg[e];
+                double s = 0.0;
+                for (int e = 0; e < ne; ++e) {
+                    tmp[e] = ref_exp(__dsub_rn(lg[e], mx));
+                    s = __dadd_rn(s, tmp[e]);
+                }
+                const double inv = __ddiv_rn(1.0, s);
+                for (int e = 0; e < ne; ++e) tmp[e] = __dmul_rn(tmp[e], inv);
+                unsigned char taken[EX_MAXE];
+                for (int e = 0; e < ne; ++e) taken[e] = 0;
+                for (int r = 0; r < k; ++r) {
+                    int best = -1;
+                    double bv = 0.0;
+                    for (int e = 0; e < ne; ++e)
+                        if (!taken[e] && (best == -1 || tmp[e] > bv)) { best = e; bv = tmp[e]; }
+                    taken[best] = 1;
+                    sel[r] = best;
+                    w[r] = bv;
+                }
+            }
+            for (int i = 0; i < k; ++i) {
+                ids[(size_t)t * k + i] = sel[i];
+                wts[(size_t)t * k + i] = (float)w[i];
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ single-token Form routers
+// form_moe_route_f32 / form_moe_route_wide_f32 (moe-msl.fk:114-117, moe-route-wide-msl.fk):
+// softmax over ne logits, top-nsel best first, renormalized over the chosen.
+__global__ void k_route_softmax_tokens(const float *__restrict__ L, uint32_t *__restrict__ ids, float *__restrict__ wts,
+                                       uint32_t ne, uint32_t nsel, uint32_t ntok, int renorm) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= ntok) return;
+    float v[RMAX];
+    float mx = -3.0e38f;
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i) {
+        const int e = 32 * i + lane;
+        v[i] = e < (int)ne ? L[(size_t)t * ne + e] : -3.0e38f;
+        mx = fmaxf(mx, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i) {
+        v[i] = (32 * i + lane < (int)ne) ? expf(v[i] - mx) : -1.0f;
+        if (v[i] > 0.0f) s += v[i];
+    }
+    s = warp_sum(s);
+    const float inv = 1.0f / s;
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i)
+        if (v[i] >= 0.0f) v[i] *= inv;
+    float pick[8];
+    int pid[8];
+    float wsum = 0.0f;
+    for (uint32_t r = 0; r < nsel; ++r) {
+        float bv = -2.0f;
+        int bi = 1 << 30;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (v[i] > bv) { bv = v[i]; bi = 32 * i + lane; }
+        warp_argmax(bv, bi);
+        pick[r] = bv;
+        pid[r] = bi;
+        wsum += bv;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (32 * i + lane == bi) v[i] = -2.0f;
+    }
+    if (lane == 0) {
+        const float winv = 1.0f / wsum;
+        for (uint32_t r = 0; r < nsel; ++r) {
+            ids[(size_t)t * nsel + r] = (uint32_t)pid[r];
+            wts[(size_t)t * nsel + r] = renorm ? pick[r] * winv : pick[r];
+        }
+    }
+}
+
+// form_dsv4_router_f32 (dsv4-router-msl.fk:103-106): probs = sqrt(log(1 + exp(l))), selection on
+// probs + bias, weights from the probs, sum floored at 2^-14, times wscale/sum, ids last-first.
+__global__ void k_route_dsv4_tokens(const float *__restrict__ L, const float *__restrict__ bias,
+                                    uint32_t *__restrict__ ids, float *__restrict__ wts, uint32_t ne, uint32_t nused,
+                                    float wscale, uint32_t ntok) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= ntok) return;
+    float pr[RMAX], sc[RMAX];
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i) {
+        const int e = 32 * i + lane;
+        if (e < (int)ne) {
+            pr[i] = sqrtf(log1pf(expf(L[(size_t)t * ne + e])));
+            sc[i] = pr[i] + bias[e];
+        } else {
+            pr[i] = 0.0f;
+            sc[i] = -3.0e38f;
+        }
+    }
+    int pick[8];
+    for (uint32_t r = 0; r < nused; ++r) {
+        float bv = -3.0e38f;
+        int bi = 1 << 30;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
+        warp_argmax(bv, bi);
+        pick[r] = bi;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (32 * i + lane == bi) sc[i] = -3.0e38f;
+    }
+    float pp[8];
+    float s0 = 0.0f;
+    for (uint32_t r = 0; r < nused; ++r) {
+        float pe = 0.0f;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i)
+            if (32 * i + lane == pick[r]) pe = pr[i];
+        pp[r] = __shfl_sync(0xffffffffu, pe, pick[r] & 31);
+        s0 += pp[r];
+    }
+    if (lane == 0) {
+        const float s = s0 < 6.103515625e-05f ? 6.103515625e-05f : s0;
+        const float scl = wscale / s;
+        for (uint32_t j = 0; j < nused; ++j) {
+            const uint32_t src = nused - 1 - j;
+            ids[(size_t)t * nused + j] = (uint32_t)pick[src];
+            wts[(size_t)t * nused + j] = pp[src] * scl;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ launchers
+int launch_router_logits(const uint16_t *x, const float *w, float *L, uint32_t T, uint32_t E, uint32_t H,
+                         cudaStream_t s) {
+    if (!T || !E) return 0;
+    k_router_logits<<<dim3((T + 63) / 64, (E + 63) / 64), 256, 0, s>>>(x, w, L, T, E, H);
+    return (int)cudaGetLastError();
+}
+int launch_route_select(const float *L, const float *bias, int32_t *ids, float *wts, uint32_t *flag_list,
+                        uint32_t *flag_count, const RouteParams &p, cudaStream_t s) {
+    if (p.ne == 0 || p.ne > 32 * RMAX || p.nsel == 0 || p.nsel > 16 || p.nsel > p.ne) return CK_ERR_SHAPE;
+    if (p.mode == 4 && (p.ngroups == 0 || p.ngroups > 32 || p.ne % p.ngroups || p.topk_groups == 0 ||
+                        p.topk_groups > p.ngroups || p.nsel > p.topk_groups * (p.ne / p.ngroups)))
+        return CK_ERR_SHAPE;
+    if (p.mode == 4 && !bias) return CK_ERR_ARG;
+    cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
+    if (p.ntok) k_route_select<<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, bias, ids, wts, flag_list, flag_count, p);
+    return (int)cudaGetLastError();
+}
+int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int32_t *ids, float *wts,
+                       const uint32_t *flag_list, const uint32_t *flag_count, const RouteParams &p, cudaStream_t s) {
+    if (p.ne > EX_MAXE || p.hidden % 32 != 0) return CK_ERR_SHAPE;
+    int dev = 0, nsm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    k_route_exact<<<nsm * 2, EX_THREADS, 0, s>>>(x, w, bias, ids, wts, flag_list, flag_count, p);
+    return (int)cudaGetLastError();
+}
+int launch_route_softmax_tokens(const float *L, uint32_t *ids, float *wts, uint32_t ne, uint32_t nsel, uint32_t ntok,
+                                int renorm, cudaStream_t s) {
+    if (ne == 0 || ne > 32 * RMAX || nsel == 0 || nsel > 8 || nsel > ne) return CK_ERR_SHAPE;
+    if (ntok) k_route_softmax_tokens<<<(ntok * 32 + 127) / 128, 128, 0, s>>>(L, ids, wts, ne, nsel, ntok, renorm);
+    return (int)cudaGetLastError();
+}
+int launch_route_dsv4_tokens(const float *L, const float *bias, uint32_t *ids, float *wts, uint32_t ne, uint32_t nused,
+                             float wscale, uint32_t ntok, cudaStream_t s) {
+    if (ne == 0 || ne > 32 * RMAX || nused == 0 || nused > 8 || nused > ne) return CK_ERR_SHAPE;
+    if (ntok) k_route_dsv4_tokens<<<(ntok * 32 + 127) / 128, 128, 0, s>>>(L, bias, ids, wts, ne, nused, wscale, ntok);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace ck

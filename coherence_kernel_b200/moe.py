@@ -1,0 +1,324 @@
+"""The batched MoE layer on B200: single GPU and expert-parallel over the GPUs of one box.
+
+The reference runs an MoE FFN one token at a time (form/form-stdlib/dsv4-forward.fk:105-115,
+moe-gate.fk:32-40, form/native/metal/moe-token.fk): route, bind the chosen experts' weights at
+``t.off + e*nb02``, run three quantized matvecs per expert, combine.  Here a whole batch is routed
+at once, the (token, slot) pairs are sorted by expert, each expert's rows run through one grouped
+tensor-core GEMM, and the combine restores the reference's per-token summation order.
+
+Two combine conventions, both the reference's:
+  mode 3  softmax router, top-k, no renormalization; moe-mix order (ascending expert, acc + g*y)
+  mode 4  sigmoid + bias, group-limited top-k, renormalized x wscale, weight inside the expert
+          (dsv4-mid), dsv4-moe-acc order (selection list), then the shared expert.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .ops import _dev, _ptr, _stream, q4k_nbytes
+
+
+@dataclass
+class MoeSpec:
+    hidden: int
+    inter: int
+    n_experts: int
+    n_shared: int
+    nsel: int
+    mode: int            # 3 or 4
+    ngroups: int = 1
+    topk_groups: int = 1
+    wscale: float = 1.0
+    tau: float = 1e-4    # decision margin below which a token is re-routed in fp64
+
+    def cfg(self) -> _lib.MoeConfig:
+        return _lib.MoeConfig(self.hidden, self.inter, self.n_experts, self.n_shared, self.nsel, self.mode,
+                              self.ngroups, self.topk_groups, self.wscale, self.tau)
+
+    @property
+    def matrix_bytes(self) -> int:
+        return q4k_nbytes(self.inter * self.hidden)
+
+    def flops_per_token(self) -> int:
+        """Algorithmic FLOPs of one token: router + (nsel routed + n_shared) SwiGLU experts."""
+        expert = 2 * 3 * self.hidden * self.inter
+        return 2 * self.hidden * self.n_experts + (self.nsel + self.n_shared) * expert
+
+
+class MoELayer:
+    """One MoE layer with its weights resident in HBM (single GPU)."""
+
+    def __init__(self, spec: MoeSpec, w_gate, w_up, w_down, s_gate, s_up, s_down, router_w, bias, max_tokens: int):
+        self.spec = spec
+        mb = spec.matrix_bytes
+        E, S = spec.n_experts, spec.n_shared
+        self.w = [_dev(w_gate, "w_gate", torch.uint8, E * mb), _dev(w_up, "w_up", torch.uint8, E * mb),
+                  _dev(w_down, "w_down", torch.uint8, E * mb)]
+        self.s = [None, None, None] if S == 0 else [_dev(s_gate, "s_gate", torch.uint8, S * mb),
+                                                     _dev(s_up, "s_up", torch.uint8, S * mb),
+                                                     _dev(s_down, "s_down", torch.uint8, S * mb)]
+        self.router_w = _dev(router_w, "router_w", torch.float32, E * spec.hidden)
+        self.bias = None if bias is None else _dev(bias, "bias", torch.float32, E)
+        self.max_tokens = max_tokens
+        self._cfg = spec.cfg()
+        L = _lib.load()
+        self.ws_bytes = L.ck_moe_workspace_bytes(ctypes.byref(self._cfg), max_tokens)
+        if self.ws_bytes == 0:
+            raise ValueError(f"unsupported MoE configuration {spec}")
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=w_gate.device)
+
+    def forward(self, x, out=None, ids=None, wts=None, counts=None):
+        """x bf16 [ntok, hidden] -> (out bf16 [ntok, hidden], ids int32 [ntok, nsel],
+        wts fp32 [ntok, nsel], counts int32 [n_experts])."""
+        sp = self.spec
+        ntok = x.shape[0]
+        if ntok > self.max_tokens:
+            raise ValueError("more tokens than the layer's workspace was sized for")
+        _dev(x, "x", (torch.bfloat16, torch.uint16, torch.int16), ntok * sp.hidden)
+        dev = x.device
+        out = out if out is not None else torch.empty((ntok, sp.hidden), dtype=torch.bfloat16, device=dev)
+        ids = ids if ids is not None else torch.empty((ntok, sp.nsel), dtype=torch.int32, device=dev)
+        wts = wts if wts is not None else torch.empty((ntok, sp.nsel), dtype=torch.float32, device=dev)
+        counts = counts if counts is not None else torch.empty(sp.n_experts, dtype=torch.int32, device=dev)
+        L = _lib.load()
+        rc = L.ck_moe_layer_bf16(ctypes.byref(self._cfg), _ptr(x), ntok, _ptr(self.w[0]), _ptr(self.w[1]),
+                                 _ptr(self.w[2]), _ptr(self.s[0]), _ptr(self.s[1]), _ptr(self.s[2]),
+                                 _ptr(self.router_w), _ptr(self.bias), _ptr(ids), _ptr(wts), _ptr(counts), _ptr(out),
+                                 _ptr(self.ws), self.ws_bytes, _stream())
+        _lib.check(rc, "ck_moe_layer_bf16")
+        return out, ids, wts, counts
+
+    __call__ = forward
+
+    def forward_steps(self, x, out, ids, wts, counts, marks=None):
+        """The same layer as `forward`, issued step by step through the C ABI (route, permute,
+        gate/up GEMM, down GEMM, combine) -- the sequence ck_moe_layer_bf16 runs internally.
+        `marks(name)` is called between steps (the benchmark records CUDA events there)."""
+        sp, L, st = self.spec, _lib.load(), _stream()
+        T, H, I, K, E = x.shape[0], sp.hidden, sp.inter, sp.nsel, sp.n_experts
+        A, R = T * K, T * K + sp.n_shared * T
+        w = self._ws_views(T)
+        mark = marks or (lambda name: None)
+        cfg = ctypes.byref(self._cfg)
+        w["err"].zero_()
+        mark("start")
+        _lib.check(L.ck_moe_route(cfg, _ptr(x), T, _ptr(self.router_w), _ptr(self.bias), _ptr(w["logits"]), _ptr(ids),
+                                  _ptr(wts), _ptr(w["flags"]), st), "route")
+        mark("route")
+        _lib.check(L.ck_moe_permute(_ptr(ids), _ptr(wts), _ptr(x), T, K, E, sp.n_shared, H, int(sp.mode == 4),
+                                    _ptr(w["xp"]), _ptr(w["row_w"]), _ptr(w["pair_pos"]), _ptr(counts), _ptr(w["tiles"]),
+                                    _ptr(w["ntiles"]), _ptr(w["perm_ws"]), st), "permute")
+        mark("permute")
+        mb = sp.matrix_bytes
+        _lib.check(L.ck_moe_expert_gemm(1, _ptr(self.w[0]), _ptr(self.w[1]), _ptr(self.s[0]), _ptr(self.s[1]), mb, E,
+                                         _ptr(w["xp"]), A + T, _ptr(w["h"]), R, _ptr(w["row_w"]), _ptr(w["tiles"]),
+                                         _ptr(w["ntiles"]), w["mt"], I, H, 0, _ptr(w["err"]), st), "gate/up")
+        mark("gate_up")
+        _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, _ptr(self.s[2]), None, mb, E, _ptr(w["h"]), R,
+                                         _ptr(w["y"]), R, None, _ptr(w["tiles"]), _ptr(w["ntiles"]), w["mt"], H, I, 1,
+                                         _ptr(w["err"]), st), "down")
+        mark("down")
+        _lib.check(L.ck_moe_combine(_ptr(w["y"]), _ptr(ids), _ptr(wts), _ptr(w["pair_pos"]), T, K, sp.n_shared, H,
+                                    int(sp.mode == 3), _ptr(out), None, st), "combine")
+        mark("combine")
+        return out, ids, wts, counts
+
+    def _ws_views(self, T):
+        """Views of the workspace laid out as ck_moe_layer_bf16 lays it out (api.cu moe_ws)."""
+        sp, L = self.spec, _lib.load()
+        K, H, I, E = sp.nsel, sp.hidden, sp.inter, sp.n_experts
+        A, XR, R = T * K, T * K + T, T * K + sp.n_shared * T
+        mt = L.ck_moe_max_tiles(T, K, E, sp.n_shared)
+        off = 0
+        views = {}
+
+        def take(name, nbytes, dtype, shape):
+            nonlocal off
+            views[name] = self.ws[off:off + nbytes].view(dtype).view(shape)
+            off += _align(nbytes)
+
+        take("logits", T * E * 4, torch.float32, (T, E))
+        take("flags", (T + 1) * 4, torch.int32, (T + 1,))
+        pw = L.ck_moe_permute_workspace_bytes(T, K, E)
+        views["perm_ws"] = self.ws[off:off + pw]
+        off += _align(pw)
+        take("xp", XR * H * 2, torch.bfloat16, (XR, H))
+        take("row_w", R * 4, torch.float32, (R,))
+        take("pair_pos", A * 4, torch.int32, (A,))
+        take("tiles", mt * 16, torch.int32, (mt, 4))
+        take("ntiles", 4, torch.int32, (1,))
+        take("h", R * I * 2, torch.bfloat16, (R, I))
+        take("y", R * H * 2, torch.bfloat16, (R, H))
+        take("err", 4, torch.int32, (1,))
+        views["mt"] = mt
+        return views
+
+    def status(self, ntok):
+        """Synchronize and raise if a device-side wait of the last layer gave up."""
+        _lib.check(_lib.load().ck_moe_layer_status(ctypes.byref(self._cfg), ntok, _ptr(self.ws), _stream()),
+                   "ck_moe_layer_status")
+
+
+def _align(n, a=256):
+    return (n + a - 1) // a * a
+
+
+class ExpertParallelMoE:
+    """The MoE layer with experts sharded over the ranks of a process group (one GPU per rank).
+
+    Rank r holds experts [r*E/W, (r+1)*E/W) and a replica of the router and the shared expert(s).
+    Each rank routes its own tokens, sorts the (token, slot) pairs by expert -- which also sorts
+    them by destination rank -- and exchanges the rows with one all-to-all (NCCL over NVLink).
+    The receiver regroups the rows by local expert, runs the grouped GEMMs, restores the arrival
+    order and sends the rows back with a second all-to-all; the source combines in the
+    reference's order.  The shared expert runs on the local tokens.
+    """
+
+    def __init__(self, spec: MoeSpec, local_w_gate, local_w_up, local_w_down, s_gate, s_up, s_down, router_w, bias,
+                 max_tokens: int, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        sp = self.spec = spec
+        if sp.n_experts % self.world:
+            raise ValueError("the experts must divide evenly over the ranks")
+        self.el = sp.n_experts // self.world
+        mb = sp.matrix_bytes
+        self.w = [_dev(t, n, torch.uint8, self.el * mb) for t, n in
+                  ((local_w_gate, "w_gate"), (local_w_up, "w_up"), (local_w_down, "w_down"))]
+        self.s = [None, None, None] if sp.n_shared == 0 else [_dev(t, n, torch.uint8, sp.n_shared * mb) for t, n in
+                                                               ((s_gate, "s_gate"), (s_up, "s_up"), (s_down, "s_down"))]
+        self.router_w = router_w
+        self.bias = bias
+        self.max_tokens = max_tokens
+        self._cfg = sp.cfg()
+        dev = router_w.device
+        T, K, H, I, E = max_tokens, sp.nsel, sp.hidden, sp.inter, sp.n_experts
+        A = T * K
+        L = _lib.load()
+        self.dev = dev
+        # source side
+        self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        self.flags = torch.empty(T + 1, dtype=torch.int32, device=dev)
+        self.xp = torch.empty((A + T, H), dtype=torch.bfloat16, device=dev)
+        self.row_w = torch.empty(A + sp.n_shared * T, dtype=torch.float32, device=dev)
+        self.pair_pos = torch.empty(A, dtype=torch.int32, device=dev)
+        self.counts = torch.empty(E, dtype=torch.int32, device=dev)
+        self.mt = L.ck_moe_max_tiles(T, K, E, sp.n_shared)
+        self.tiles = torch.empty((self.mt, 4), dtype=torch.int32, device=dev)
+        self.ntiles = torch.empty(1, dtype=torch.int32, device=dev)
+        self.perm_ws = torch.empty(_align(L.ck_moe_permute_workspace_bytes(T, K, E)), dtype=torch.uint8, device=dev)
+        self.y = torch.empty((A + sp.n_shared * T, H), dtype=torch.bfloat16, device=dev)
+        self.h_sh = torch.empty((max(1, sp.n_shared) * T, I), dtype=torch.bfloat16, device=dev)
+        self.sh_tiles = torch.empty((T // 16 + 2, 4), dtype=torch.int32, device=dev)
+        self.sh_ntiles = torch.empty(1, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # receiver side: at most every rank's pairs could land here
+        R = A * self.world
+        self.R = R
+        self.recv_x = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+        self.recv_w = torch.empty(R, dtype=torch.float32, device=dev)
+        self.recv_e = torch.empty(R, dtype=torch.int32, device=dev)
+        self.xp2 = torch.empty((R + 1, H), dtype=torch.bfloat16, device=dev)
+        self.row_w2 = torch.empty(R + 1, dtype=torch.float32, device=dev)
+        self.pair_pos2 = torch.empty(R, dtype=torch.int32, device=dev)
+        self.counts2 = torch.empty(self.el, dtype=torch.int32, device=dev)
+        self.mt2 = L.ck_moe_max_tiles(R, 1, self.el, 0)
+        self.tiles2 = torch.empty((self.mt2, 4), dtype=torch.int32, device=dev)
+        self.ntiles2 = torch.empty(1, dtype=torch.int32, device=dev)
+        self.perm_ws2 = torch.empty(_align(L.ck_moe_permute_workspace_bytes(R, 1, self.el)), dtype=torch.uint8,
+                                    device=dev)
+        self.h2 = torch.empty((R, I), dtype=torch.bfloat16, device=dev)
+        self.y2 = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+        self.y_recv = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+        self.wts_dummy = torch.ones(1, dtype=torch.float32, device=dev)
+        self.last_recv_rows = 0
+
+    def forward(self, x, out=None):
+        sp, L, dist = self.spec, _lib.load(), self.dist
+        T, H, I, K, E = x.shape[0], sp.hidden, sp.inter, sp.nsel, sp.n_experts
+        if T > self.max_tokens:
+            raise ValueError("more tokens than the layer was sized for")
+        A = T * K
+        dev = x.device
+        st = _stream()
+        ids = torch.empty((T, K), dtype=torch.int32, device=dev)
+        wts = torch.empty((T, K), dtype=torch.float32, device=dev)
+        out = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        self.err.zero_()
+        _lib.check(L.ck_moe_route(ctypes.byref(self._cfg), _ptr(x), T, _ptr(self.router_w), _ptr(self.bias),
+                                  _ptr(self.logits), _ptr(ids), _ptr(wts), _ptr(self.flags), st), "ck_moe_route")
+        _lib.check(L.ck_moe_permute(_ptr(ids), _ptr(wts), _ptr(x), T, K, E, sp.n_shared, H, int(sp.mode == 4),
+                                    _ptr(self.xp), _ptr(self.row_w), _ptr(self.pair_pos), _ptr(self.counts),
+                                    _ptr(self.tiles), _ptr(self.ntiles), _ptr(self.perm_ws), st), "ck_moe_permute")
+        # shared expert(s) on the local tokens (rows A.. of xp), into y rows A + s*T ..
+        if sp.n_shared:
+            mb = sp.matrix_bytes
+            _lib.check(L.ck_token_tiles(_ptr(self.sh_tiles), _ptr(self.sh_ntiles), T, st), "ck_token_tiles")
+            for s in range(sp.n_shared):
+                xs = self.xp[A:A + T]
+                hs = self.h_sh[s * T:(s + 1) * T]
+                ys = self.y[A + s * T:A + (s + 1) * T]
+                _lib.check(L.ck_moe_expert_gemm(1, ctypes.c_void_p(self.s[0].data_ptr() + s * mb),
+                                                 ctypes.c_void_p(self.s[1].data_ptr() + s * mb), None, None, 0, 1,
+                                                 _ptr(xs), T, _ptr(hs), T, None, _ptr(self.sh_tiles),
+                                                 _ptr(self.sh_ntiles), self.sh_tiles.shape[0], I, H, 0, _ptr(self.err),
+                                                 st), "shared gate/up")
+                _lib.check(L.ck_moe_expert_gemm(0, ctypes.c_void_p(self.s[2].data_ptr() + s * mb), None, None, None, 0,
+                                                 1, _ptr(hs), T, _ptr(ys), T, None, _ptr(self.sh_tiles),
+                                                 _ptr(self.sh_ntiles), self.sh_tiles.shape[0], H, I, 0, _ptr(self.err),
+                                                 st), "shared down")
+        # rows per destination rank: experts are contiguous per rank, and so are their rows in xp
+        cnt_rank = self.counts.view(self.world, self.el)
+        send_counts = cnt_rank.sum(dim=1)
+        recv_counts_e = torch.empty_like(self.counts)
+        dist.all_to_all_single(recv_counts_e, self.counts, group=self.group)  # [src, local expert]
+        recv_counts = recv_counts_e.view(self.world, self.el).sum(dim=1)
+        sc = send_counts.tolist()
+        rc = recv_counts.tolist()
+        nrecv = int(sum(rc))
+        self.last_recv_rows = nrecv
+        dist.all_to_all_single(self.recv_x[:nrecv], self.xp[:A], output_split_sizes=rc, input_split_sizes=sc,
+                               group=self.group)
+        if sp.mode == 4:
+            dist.all_to_all_single(self.recv_w[:nrecv], self.row_w[:A], output_split_sizes=rc, input_split_sizes=sc,
+                                   group=self.group)
+        else:
+            self.recv_w[:nrecv].fill_(1.0)
+        # the local expert of every received row: each source's block is sorted by expert
+        rce = recv_counts_e.view(self.world, self.el).reshape(-1)
+        eidx = torch.arange(self.el, device=dev, dtype=torch.int32).repeat(self.world)
+        self.recv_e[:nrecv] = torch.repeat_interleave(eidx, rce.to(torch.int64), output_size=nrecv)
+        # regroup by local expert (a stable counting sort), grouped GEMMs, restore arrival order
+        if nrecv:
+            _lib.check(L.ck_moe_permute(_ptr(self.recv_e), _ptr(self.recv_w), _ptr(self.recv_x), nrecv, 1, self.el, 0,
+                                        H, 1, _ptr(self.xp2), _ptr(self.row_w2), _ptr(self.pair_pos2),
+                                        _ptr(self.counts2), _ptr(self.tiles2), _ptr(self.ntiles2),
+                                        _ptr(self.perm_ws2), st), "regroup")
+            _lib.check(L.ck_moe_expert_gemm(1, _ptr(self.w[0]), _ptr(self.w[1]), None, None, sp.matrix_bytes, self.el,
+                                             _ptr(self.xp2), nrecv, _ptr(self.h2), nrecv, _ptr(self.row_w2),
+                                             _ptr(self.tiles2), _ptr(self.ntiles2), self.mt2, I, H, 0, _ptr(self.err),
+                                             st), "expert gate/up")
+            _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, None, None, sp.matrix_bytes, self.el,
+                                             _ptr(self.h2), nrecv, _ptr(self.y2), nrecv, None, _ptr(self.tiles2),
+                                             _ptr(self.ntiles2), self.mt2, H, I, 1, _ptr(self.err), st), "expert down")
+            _lib.check(L.ck_gather_rows(_ptr(self.y2), _ptr(self.pair_pos2), _ptr(self.y_recv), nrecv, H * 2, st),
+                       "restore order")
+        dist.all_to_all_single(self.y[:A], self.y_recv[:nrecv], output_split_sizes=sc, input_split_sizes=rc,
+                               group=self.group)
+        _lib.check(L.ck_moe_combine(_ptr(self.y), _ptr(ids), _ptr(wts), _ptr(self.pair_pos), T, K, sp.n_shared, H,
+                                    int(sp.mode == 3), _ptr(out), None, st), "combine")
+        return out, ids, wts, self.counts
+
+    __call__ = forward
+
+    def check(self):
+        torch.cuda.current_stream().synchronize()
+        if int(self.err.item()):
+            raise _lib.CKError(f"a grouped-GEMM device wait timed out (role code {int(self.err.item())})")

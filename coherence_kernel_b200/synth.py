@@ -26,7 +26,11 @@ Q4K_BLOCK_WEIGHTS = 256
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 bit patterns, round to nearest even (finite inputs)."""
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.size > (1 << 20):
+        import torch
+        return torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    u = x.view(np.uint32)
     rounding = ((u >> 16) & 1) + np.uint32(0x7FFF)
     return ((u + rounding) >> 16).astype(np.uint16)
 
@@ -85,7 +89,7 @@ def make_q4k(rng: np.random.Generator, n_weights: int, chunk_blocks: int = 1 << 
         mn = rng.integers(0, 64, size=(n, 8), dtype=np.uint8)
         out[b0:b1, 4:16] = pack_q4k_scales(sc, mn)
         # two uniform 4-bit codes per byte == one uniform byte
-        out[b0:b1, 16:] = np.frombuffer(rng.bytes(n * 128), dtype=np.uint8).reshape(n, 128)
+        out[b0:b1, 16:] = rng.integers(0, 1 << 32, size=n * 32, dtype=np.uint32).view(np.uint8).reshape(n, 128)
     return out.reshape(-1)
 
 

@@ -1,0 +1,132 @@
+/* ck_b200.h -- C ABI of the B200 (sm_100a) kernels for coherence-kernel's quantized path.
+ *
+ * Plain pointers and sizes only.  Every pointer argument named *_dev is CUDA device memory (or
+ * host memory the device can address); `stream` is a cudaStream_t (NULL = the legacy default
+ * stream).  Every entry point enqueues work and returns without waiting.  Return value: 0 on
+ * success, a positive cudaError_t, or a negative CK_E* code; ck_last_error() names the failure.
+ *
+ * Layouts are the reference's: GGUF block_q8_0 (34 bytes / 32 weights) and block_q4_K (144 bytes
+ * / 256 weights) read by FLAT weight index, so row r of a rows x cols tensor is the flat range
+ * [r*cols, (r+1)*cols) and may straddle blocks (form/form-stdlib/q4k-msl.fk:73-86,
+ * q8-0-msl.fk:53-70).  Token-major activations x[t*cols + j] and outputs y[t*rows + r]
+ * (form/form-stdlib/qk-matmul-batch.fk:117-121).
+ */
+#ifndef CK_B200_H
+#define CK_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CK_OK 0
+#define CK_ESHAPE (-2)   /* a size outside the entry point's stated limits */
+#define CK_EARG (-3)     /* a null or misaligned pointer, or an out-of-range argument */
+#define CK_ETIMEOUT (-4) /* a device-side bounded wait gave up; the kernel returned early */
+#define CK_ENODEV (-5)   /* no CUDA device / driver entry point */
+
+const char *ck_last_error(void);
+/* 1 when the library was built for sm_100a and a device is present */
+int ck_device_ok(void);
+
+/* ---- dequant (replaces form_q8_0_dequant_f32, q8-0-msl.fk:92-95; form_q4k_dequant_f32,
+ *      q4k-msl.fk:104-107): w[i] = weight(off + i), i < n */
+int ck_q8_0_dequant_f32(const void *qb_dev, float *w_dev, uint64_t off, uint64_t n, void *stream);
+int ck_q4k_dequant_f32(const void *qb_dev, float *w_dev, uint64_t off, uint64_t n, void *stream);
+int ck_q4k_dequant_bf16(const void *qb_dev, void *w_bf16_dev, uint64_t off, uint64_t n, void *stream);
+
+/* ---- decode matvec, fp32 x / y (replaces form_q8_0_matvec_f32 / _lane / wide,
+ *      q8-0-msl.fk:100-123; form_q4k_matvec_f32, q4k-msl.fk:111-114, and the hoist / lane / slot
+ *      variants, qk-matvec-lane.fk:218-238, qk-matvec-slot.fk:163-235).
+ *      Q8_0: cols % 32 == 0 (fastest at cols % 256 == 0).  Q4_K: cols % 64 == 0. */
+int ck_q8_0_matvec_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
+                       void *stream);
+int ck_q4k_matvec_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
+                      void *stream);
+/* The attestant association: one thread per row, j counting down, acc = w*x + acc with no fused
+ * multiply-add (q8-0-msl.fk:100-103, q4k-msl.fk:111-114).  ggml_type 8 = Q8_0, 12 = Q4_K. */
+int ck_matvec_ordered_f32(int ggml_type, const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows,
+                          uint32_t cols, void *stream);
+/* Batched matvec over ntok tokens, fp32 (replaces form_q4k_matmul_batch_f32,
+ * qk-matmul-batch.fk:206-217): y[t*rows + r] = sum_j W[r, j] x[t*cols + j].  cols % 64 == 0. */
+int ck_q4k_matmul_batch_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
+                            uint32_t ntok, void *stream);
+
+/* ---- prefill GEMM on the tensor cores: Y[t, r] = sum_j X[t, j] W[r, j], X bf16 [ntok, cols],
+ *      Y bf16 [ntok, rows], fp32 accumulation (the bf16-MMA form of form_q4k_matmul_batch_f32).
+ *      cols % 64 == 0, rows*cols % 256 == 0.  workspace: ck_q4k_gemm_workspace_bytes(ntok). */
+size_t ck_q4k_gemm_workspace_bytes(uint32_t ntok);
+int ck_q4k_gemm_bf16(const void *qb_dev, const void *x_bf16_dev, void *y_bf16_dev, uint32_t rows, uint32_t cols,
+                     uint32_t ntok, void *workspace_dev, size_t workspace_bytes, void *stream);
+
+/* ---- small kernels of the reference's MoE decode (moe-msl.fk:114-140, dsv4-moe-msl.fk:87-88,
+ *      dsv4-router-msl.fk:103-106, moe-route-wide-msl.fk) -- one routing per token, ntok tokens */
+int ck_f16_matvec_f32(const void *w_f16_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
+                      void *stream);
+int ck_route_softmax_f32(const float *logits_dev, uint32_t *ids_dev, float *wts_dev, uint32_t ne, uint32_t nsel,
+                         uint32_t ntok, int renorm, void *stream);
+int ck_route_dsv4_f32(const float *logits_dev, const float *bias_dev, uint32_t *ids_dev, float *wts_dev,
+                      uint32_t ne, uint32_t nused, float wscale, uint32_t ntok, void *stream);
+int ck_scale_f32(const float *x_dev, float *y_dev, float a, uint32_t n, void *stream);
+int ck_axpy_f32(const float *x_dev, float *y_dev, float a, uint32_t n, void *stream);
+int ck_swiglu_f32(const float *gate_dev, const float *up_dev, float *out_dev, uint32_t n, float w, float lim,
+                  void *stream);
+
+/* ---- the batched MoE layer (new: the reference routes and combines one token at a time) ----
+ * mode 3: softmax router, top-nsel, no renormalization, combine in ascending expert index with
+ *         the weight applied at the combine (moe-gate.fk:22-37), n_shared shared experts added.
+ * mode 4: sigmoid + bias, group-limited (ngroups, topk_groups), top-nsel, weights renormalized x
+ *         wscale (dsv4-forward.fk:105-111), applied inside the expert (dsv4-mid), combine in
+ *         selection-list order, shared expert(s) added.
+ * Experts: Q4_K gate/up [inter x hidden] and down [hidden x inter], expert e at byte offset
+ * e * (inter*hidden/256*144) of each array; shared experts likewise.  router_w fp32 [ne, hidden];
+ * bias fp32 [ne] (mode 4).  x bf16 [ntok, hidden].  Outputs: ids int32 [ntok, nsel], wts fp32
+ * [ntok, nsel] (the reference's list order), counts int32 [ne], out bf16 [ntok, hidden].
+ * Limits: ne <= 256, nsel <= 16, hidden % 64 == 0, inter % 64 == 0, ngroups <= 32.
+ * tau: a token whose decision margin (smallest gap between a chosen and a rejected candidate's
+ * fp32 score) is below tau is routed again in fp64 in the reference's own fold order. */
+typedef struct {
+    uint32_t hidden, inter, n_experts, n_shared, nsel, mode, ngroups, topk_groups;
+    float wscale, tau;
+} ck_moe_config;
+
+size_t ck_moe_workspace_bytes(const ck_moe_config *cfg, uint32_t ntok);
+int ck_moe_layer_bf16(const ck_moe_config *cfg, const void *x_bf16_dev, uint32_t ntok, const void *w_gate_dev,
+                      const void *w_up_dev, const void *w_down_dev, const void *s_gate_dev, const void *s_up_dev,
+                      const void *s_down_dev, const float *router_w_dev, const float *bias_dev, int32_t *ids_dev,
+                      float *wts_dev, int32_t *counts_dev, void *out_bf16_dev, void *workspace_dev,
+                      size_t workspace_bytes, void *stream);
+
+/* After a layer has run: synchronizes `stream` and returns CK_ETIMEOUT when a device-side wait in
+ * the grouped GEMM gave up (the layer's output is then not valid), else 0. */
+int ck_moe_layer_status(const ck_moe_config *cfg, uint32_t ntok, const void *workspace_dev, void *stream);
+
+/* the layer's steps, for callers that place an all-to-all between them (expert parallelism) */
+int ck_moe_route(const ck_moe_config *cfg, const void *x_bf16_dev, uint32_t ntok, const float *router_w_dev,
+                 const float *bias_dev, float *logits_dev, int32_t *ids_dev, float *wts_dev, uint32_t *flags_dev,
+                 void *stream);
+size_t ck_moe_permute_workspace_bytes(uint32_t ntok, uint32_t nsel, uint32_t n_experts);
+uint32_t ck_moe_max_tiles(uint32_t ntok, uint32_t nsel, uint32_t n_experts, uint32_t n_shared);
+int ck_moe_permute(const int32_t *ids_dev, const float *wts_dev, const void *x_bf16_dev, uint32_t ntok,
+                   uint32_t nsel, uint32_t n_experts, uint32_t n_shared, uint32_t hidden, int weight_in_mid,
+                   void *xp_bf16_dev, float *row_w_dev, int32_t *pair_pos_dev, int32_t *counts_dev,
+                   void *tiles_dev, int32_t *ntiles_dev, void *workspace_dev, void *stream);
+int ck_moe_expert_gemm(int dual, const void *w0_dev, const void *w1_dev, const void *s0_dev, const void *s1_dev,
+                       uint64_t w_stride, uint32_t n_routed, const void *x_bf16_dev, uint32_t x_rows,
+                       void *out_bf16_dev, uint32_t out_rows, const float *row_w_dev, const void *tiles_dev,
+                       const int32_t *ntiles_dev, uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow,
+                       int *err_dev, void *stream);
+int ck_moe_combine(const void *y_bf16_dev, const int32_t *ids_dev, const float *wts_dev, const int32_t *pair_pos_dev,
+                   uint32_t ntok, uint32_t nsel, uint32_t n_shared, uint32_t hidden, int order_by_expert,
+                   void *out_bf16_dev, float *out_f32_dev, void *stream);
+/* the token-tile table of one matrix over ntok rows (group 0, rows in order), at most
+ * ntok/16 + 2 entries of 4 int32 */
+int ck_token_tiles(void *tiles_dev, int32_t *ntiles_dev, uint32_t ntok, void *stream);
+int ck_gather_rows(const void *src_dev, const int32_t *idx_dev, void *dst_dev, uint32_t nrows, uint32_t row_bytes,
+                   void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

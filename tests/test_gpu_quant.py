@@ -1,0 +1,116 @@
+"""Parity of the dequant / decode-matvec kernels with the oracle (GPU).
+
+Tolerances: Q8_0 dequant is exact in fp32 (d*q needs <= 19 significand bits, q8-0-msl.fk:17-21),
+so equality; Q4_K dequant within one rounding |gpu - w| <= 2^-24 |w| (q4k-msl.fk:20-28); fp32
+matvecs within 1e-3 * sum_j |w_j x_j| per row, and the attestant-order kernel within the
+reference's derived bound (cols + 2) * 2^-24 * sum_j |w_j x_j| (qk-matvec-split.fk:41-54, p = 1).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from coherence_kernel_b200 import ops, synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+U = 2.0 ** -24
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def absdot(wq_deq, x, rows, cols):
+    return np.abs(wq_deq.reshape(rows, cols)) @ np.abs(x.astype(np.float64))
+
+
+def test_q8_0_dequant_exact_on_reference_fixture():
+    f = np.load(os.path.join(G, "ref_fixtures.npz"))
+    w = ops.q8_0_dequant(dev(f["q80"]), 0, 96).cpu().numpy()
+    assert np.array_equal(w, f["w8"].astype(np.float32))
+
+
+def test_q4k_dequant_one_rounding_on_reference_fixture():
+    f = np.load(os.path.join(G, "ref_fixtures.npz"))
+    w = ops.q4k_dequant(dev(f["q4k"]), 0, 512).cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(w - f["w4"]) <= U * np.abs(f["w4"]))
+
+
+@pytest.mark.parametrize("n,off", [(4096 * 32, 0), (1000, 37), (1 << 20, 256)])
+def test_dequant_large(n, off):
+    rng = np.random.default_rng(n)
+    q8 = synth.make_q8_0(rng, ((off + n + 31) // 32) * 32)
+    q4 = synth.make_q4k(rng, ((off + n + 255) // 256) * 256)
+    w8 = ops.q8_0_dequant(dev(q8), off, n).cpu().numpy()
+    assert np.array_equal(w8, O.q80_dequant(q8, off, n).astype(np.float32))
+    w4 = ops.q4k_dequant(dev(q4), off, n).cpu().numpy().astype(np.float64)
+    ref = O.q4k_dequant(q4, off, n)
+    assert np.all(np.abs(w4 - ref) <= U * np.abs(ref))
+
+
+def test_matvec_golden():
+    g = np.load(os.path.join(G, "quant_golden.npz"))
+    r8, c8, r4, c4 = (int(v) for v in g["dims"])
+    y8 = ops.q8_0_matvec(dev(g["q8"]), dev(g["x8"]), r8, c8).cpu().numpy()
+    b8 = absdot(g["w8"], g["x8"], r8, c8)
+    assert np.all(np.abs(y8 - g["y8"]) <= 1e-3 * b8)
+    y4 = ops.q4k_matvec(dev(g["q4"]), dev(g["x4"]), r4, c4).cpu().numpy()   # rows straddle superblocks
+    b4 = absdot(g["w4"], g["x4"], r4, c4)
+    assert np.all(np.abs(y4 - g["y4"]) <= 1e-3 * b4)
+    for kind, q, x, y, b, r, c in ((8, g["q8"], g["x8"], g["y8"], b8, r8, c8), (12, g["q4"], g["x4"], g["y4"], b4, r4, c4)):
+        yo = ops.matvec_ordered(kind, dev(q), dev(x), r, c).cpu().numpy()
+        assert np.all(np.abs(yo - y) <= (c + 2) * U * b)
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (512, 1408), (7168, 7168), (300, 2048)])
+def test_q4k_matvec_sizes(rows, cols):
+    rng = np.random.default_rng(rows + cols)
+    q = synth.make_q4k(rng, rows * cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = ops.q4k_matvec(dev(q), dev(x), rows, cols).cpu().numpy()
+    sample = np.unique(np.linspace(0, rows - 1, 64).astype(int))
+    for r in sample:
+        w = O.q4k_dequant(q, r * cols, cols)
+        ref = O.lib().ckr_dot(w.ctypes.data, x.astype(np.float64).ctypes.data, cols)
+        assert abs(y[r] - ref) <= 1e-3 * np.abs(w * x).sum(), r
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (64, 96), (1000, 2048)])
+def test_q8_0_matvec_sizes(rows, cols):
+    rng = np.random.default_rng(rows * 7 + cols)
+    q = synth.make_q8_0(rng, rows * cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = ops.q8_0_matvec(dev(q), dev(x), rows, cols).cpu().numpy()
+    ref = O.q80_matvec(q, x.astype(np.float64), rows, cols)
+    w = O.q80_dequant(q, 0, rows * cols)
+    assert np.all(np.abs(y - ref) <= 1e-3 * absdot(w, x, rows, cols))
+
+
+@pytest.mark.parametrize("ntok", [1, 3, 8, 13])
+def test_q4k_matmul_batch_fp32(ntok):
+    rows, cols = 384, 1408
+    rng = np.random.default_rng(ntok)
+    q = synth.make_q4k(rng, rows * cols)
+    x = rng.standard_normal((ntok, cols)).astype(np.float32)
+    y = ops.q4k_matmul_batch(dev(q), dev(x), rows, cols).cpu().numpy()
+    ref = O.q4k_matmul(q, x.astype(np.float64), rows, cols)
+    w = O.q4k_dequant(q, 0, rows * cols).reshape(rows, cols)
+    bound = np.abs(x.astype(np.float64)) @ np.abs(w).T
+    assert np.all(np.abs(y - ref) <= 1e-3 * bound)
+
+
+def test_small_routers_golden():
+    g = np.load(os.path.join(G, "route_golden.npz"))
+    for t in ("e64", "e256"):
+        ne, nsel, ng, tg = (int(v) for v in g[t + "_dims"])
+        L = dev(g[t + "_logits"])
+        ids, w = ops.route_softmax(L, nsel, renorm=True)
+        assert np.array_equal(ids.cpu().numpy(), g[t + "_mm_ids"])
+        assert np.allclose(w.cpu().numpy(), g[t + "_mm_wn"], rtol=1e-5, atol=1e-7)
+        ids, w = ops.route_dsv4(L, dev(g[t + "_bias"]), nsel, 2.5)
+        ok = np.array_equal(ids.cpu().numpy(), g[t + "_dr_ids"])
+        assert ok
+        assert np.allclose(w.cpu().numpy(), g[t + "_dr_w"], rtol=1e-5, atol=1e-6)
