@@ -53,7 +53,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -153,10 +153,13 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ck", choices=["ck", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", type=int, default=1,
+                    help="run one GPU's share of an N-way expert-parallel layer on one GPU (256/N experts, "
+                         "8192/N tokens): the small case a profiler capture uses")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -177,6 +180,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     spec = workloads.MOE_DSV3
     T_all = workloads.MOE_DSV3_TOKENS
+    if args.shard > 1:
+        import dataclasses
+        spec = dataclasses.replace(spec, n_experts=spec.n_experts // args.shard)
+        T_all //= args.shard
     T = T_all // world
     el = spec.n_experts // world
     experts = list(range(rank * el, (rank + 1) * el))
@@ -249,6 +256,7 @@ def main():
         ms = float(m.item())
     ms_step = ms / args.steps
     tokens_per_s = T_all / (ms_step / 1e3)
+    flagged = layer.flagged(T) if world == 1 else None
 
     hbm, tc_burst, tc_sust, peak_src = peaks()
     weight_bytes = (spec.n_experts + spec.n_shared) * 3 * spec.matrix_bytes
@@ -293,7 +301,10 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(spec, {k: w[k] for k in w}, tokens=2) if len(experts) == spec.n_experts else None
-        launches_per_step = 9 if world == 1 else 9 + 4 * spec.n_shared
+        # our kernels per step: route 5 (split, tiles, logits GEMM, select, exact), permute 3, GEMM 2,
+        # combine 1; expert-parallel adds the shared tiles + 2 GEMMs per shared expert, the regroup
+        # permute 3 and the row restore 1
+        launches_per_step = 11 if world == 1 else 11 + 1 + 2 * spec.n_shared + 3 + 1
         line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
@@ -304,6 +315,7 @@ def main():
                 "weight_stream_gbs": round(weight_bytes / (ms_step / 1e3) / 1e9, 1),
                 "algorithmic_tflops": round(T_all * spec.flops_per_token() / (ms_step / 1e3) / 1e12, 1),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "router_exact_tokens": flagged,
                 "gpu_launches": launches_per_step * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:

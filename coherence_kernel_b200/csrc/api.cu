@@ -23,9 +23,33 @@ int fail(int rc, const char *what) {
 inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 inline size_t al(size_t b) { return (b + 255) & ~(size_t)255; }
 
+// The router's scratch: the three-term bf16 split of the router, its token tiles, the flagged-
+// token list (count first), and a device error word.
+struct RouteWs {
+    uint16_t *wsplit;
+    int4 *tiles;
+    int32_t *ntiles;
+    int *err;
+    uint32_t *flags;
+    size_t total;
+};
+RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
+    RouteWs w;
+    uint8_t *b = (uint8_t *)base;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { uint8_t *p = b ? b + o : nullptr; o += al(bytes); return p; };
+    w.wsplit = (uint16_t *)take((size_t)c->n_experts * 3 * c->hidden * 2);
+    w.tiles = (int4 *)take(((size_t)ntok / 16 + 2) * 16);
+    w.ntiles = (int32_t *)take(4);
+    w.err = (int *)take(4);
+    w.flags = (uint32_t *)take(((size_t)ntok + 1) * 4);
+    w.total = o;
+    return w;
+}
+
 struct MoeWs {
     float *logits;
-    uint32_t *flags;
+    void *route;
     void *perm_ws;
     uint16_t *xp;
     float *row_w;
@@ -58,7 +82,7 @@ MoeWs moe_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
     size_t o = 0;
     auto take = [&](size_t bytes) { uint8_t *p = b ? b + o : nullptr; o += al(bytes); return p; };
     w.logits = (float *)take((size_t)ntok * c->n_experts * 4);
-    w.flags = (uint32_t *)take(((size_t)ntok + 1) * 4);
+    w.route = take(route_ws(c, ntok, nullptr).total);
     w.perm_ws = take(ck::permute_workspace_bytes(perm_params(c, ntok)));
     w.xp = (uint16_t *)take(XR * c->hidden * 2);
     w.row_w = (float *)take(R * 4);
@@ -211,18 +235,55 @@ size_t ck_moe_workspace_bytes(const ck_moe_config *c, uint32_t ntok) {
     return moe_ws(c, ntok, nullptr).total;
 }
 
+size_t ck_moe_route_workspace_bytes(const ck_moe_config *c, uint32_t ntok) {
+    if (check_cfg(c)) return 0;
+    return route_ws(c, ntok, nullptr).total;
+}
+
 int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const float *rw, const float *bias,
-                 float *logits, int32_t *ids, float *wts, uint32_t *flags, void *s) {
+                 float *logits, int32_t *ids, float *wts, void *ws, size_t wsb, void *s) {
     int rc = check_cfg(c);
     if (rc) return fail(rc, "ck_moe_route config");
-    if (!x || !rw || !logits || !ids || !wts || !flags || (c->mode == 4 && !bias)) return fail(CK_EARG, "ck_moe_route");
-    rc = ck::launch_router_logits((const uint16_t *)x, rw, logits, ntok, c->n_experts, c->hidden, S(s));
+    if (!x || !rw || !logits || !ids || !wts || !ws || (c->mode == 4 && !bias)) return fail(CK_EARG, "ck_moe_route");
+    if (wsb < ck_moe_route_workspace_bytes(c, ntok)) return fail(CK_EARG, "ck_moe_route workspace");
+    if (ntok == 0) return 0;
+    RouteWs w = route_ws(c, ntok, ws);
+    // logits on the tensor cores: x . [W1 | W2 | W3]^T with the fp32 router split into bf16 terms
+    rc = ck::launch_split_bf16x3(rw, w.wsplit, c->n_experts, c->hidden, S(s));
+    if (!rc) rc = ck::launch_single_tiles(w.tiles, w.ntiles, ntok, 128, S(s));
+    if (rc) return fail(rc, "ck_moe_route split");
+    cudaMemsetAsync(w.err, 0, 4, S(s));
+    ck::GemmParams g = {};
+    g.a_dense = w.wsplit;
+    g.kx = c->hidden;
+    g.K = 3 * c->hidden;
+    g.N = c->n_experts;
+    g.x = x;
+    g.x_rows = ntok;
+    g.out_f32 = logits;
+    g.out_rows = ntok;
+    g.tiles = w.tiles;
+    g.ntiles = w.ntiles;
+    g.max_tiles = ntok / 16 + 2;
+    g.err = w.err;
+    rc = ck::launch_gemm_dense(g, S(s));
     if (rc) return fail(rc, "ck_moe_route logits");
     ck::RouteParams p = {ntok, c->n_experts, c->nsel, c->hidden, c->mode, c->ngroups, c->topk_groups, c->wscale, c->tau};
-    rc = ck::launch_route_select(logits, bias, ids, wts, flags + 1, flags, p, S(s));
+    rc = ck::launch_route_select(logits, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
     if (rc) return fail(rc, "ck_moe_route select");
-    rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, flags + 1, flags, p, S(s));
+    rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
     return fail(rc, "ck_moe_route exact");
+}
+
+// How many tokens the last ck_moe_route sent to the exact fp64 re-route (synchronizes the stream).
+int ck_moe_route_flagged(const ck_moe_config *c, uint32_t ntok, const void *ws, void *s) {
+    if (check_cfg(c) || !ws) return fail(CK_EARG, "ck_moe_route_flagged");
+    RouteWs w = route_ws(c, ntok, const_cast<void *>(ws));
+    uint32_t n = 0;
+    cudaError_t r = cudaMemcpyAsync(&n, w.flags, 4, cudaMemcpyDeviceToHost, S(s));
+    if (r == cudaSuccess) r = cudaStreamSynchronize(S(s));
+    if (r != cudaSuccess) return fail((int)r, "ck_moe_route_flagged");
+    return (int)n;
 }
 
 int ck_moe_permute(const int32_t *ids, const float *wts, const void *x, uint32_t ntok, uint32_t nsel,
@@ -291,7 +352,7 @@ int ck_moe_layer_bf16(const ck_moe_config *c, const void *x, uint32_t ntok, cons
     MoeWs w = moe_ws(c, ntok, ws);
     cudaStream_t st = S(s);
     cudaMemsetAsync(w.err, 0, 4, st);
-    rc = ck_moe_route(c, x, ntok, rw, bias, w.logits, ids, wts, w.flags, s);
+    rc = ck_moe_route(c, x, ntok, rw, bias, w.logits, ids, wts, w.route, route_ws(c, ntok, nullptr).total, s);
     if (rc) return rc;
     const uint32_t A = ntok * c->nsel, R = A + c->n_shared * ntok;
     rc = ck_moe_permute(ids, wts, x, ntok, c->nsel, c->n_experts, c->n_shared, c->hidden, c->mode == 4, w.xp, w.row_w,

@@ -602,10 +602,18 @@ long long fk_metal_enqueue_external(long long pipe, const char *binding, long lo
     for (unsigned i = 0; i < nconst; ++i) k.c[i] = le32(bp + 4 + 4 * nbuf + 4 + 4 * i);
     k.threads = threads;
     k.s = g.stream;
+    const bool opened_here = !g.batch_open;
+    const int armed = g.next_concurrent;
     open_batch();
     std::string why;
     const int rc = e.fn(k, why);
     if (rc != 0) {
+        // a refused dispatch leaves no half-open batch behind it (the batch's mode stays armed)
+        if (opened_here && g.pending == 0) {
+            g.batch_open = false;
+            g.batch_concurrent = 0;
+            g.next_concurrent = armed;
+        }
         err(std::string("enqueue: ") + e.name + ": " + (why.empty() ? (rc > 0 ? cudaGetErrorString((cudaError_t)rc) : ck_last_error()) : why));
         return -1;
     }

@@ -79,7 +79,16 @@ struct GemmParams {
     int dual;                // 1: out = silu(x.W0) * (x.W1) * row_w ; 0: out = x.W0
     int xrow_is_orow;        // 1: read X at the tile's output row (the down projection over H)
     int *err;                // device error word (bounded waits)
+    // dense form (router logits): A is bf16 [N, K] read by TMA, X is walked every kx columns
+    // (A = [W1 | W2 | W3], the three bf16 terms of an fp32 matrix), the output is fp32 [rows, N]
+    const void *a_dense;
+    uint32_t kx;
+    float *out_f32;
 };
 int launch_gemm_q4k(const GemmParams &p, cudaStream_t s);
+int launch_gemm_dense(const GemmParams &p, cudaStream_t s);
+// fp32 [rows, k] -> bf16 [rows, 3k]: w = w1 + w2 + w3 with each term the bf16 rounding of the
+// remainder (exact to about 2^-24 relative)
+int launch_split_bf16x3(const float *w, uint16_t *out, uint32_t rows, uint32_t k, cudaStream_t s);
 
 }  // namespace ck

@@ -7,13 +7,16 @@
 // with W_g the GGUF Q4_K tensor of group g (flat index, rows may straddle superblocks at 64-weight
 // chunk boundaries, as q4k-msl.fk:73-86 reads it).  Output is bf16, accumulation fp32.
 //
+// A third form, dense = 1, reads a bf16 A operand through TMA instead of dequantizing and writes
+// fp32: the router logits, with the fp32 router split into three bf16 terms along K.
+//
 // One persistent CTA per SM, warp-specialised:
 //   warp 0      TMA producer: the token tile (BN x 64 bf16, 128-byte swizzle) per K step
 //   warp 1      TMEM allocator and the single MMA-issuing thread (tcgen05.mma kind::f16, M=128)
-//   warps 2-5   dequant producers: each thread owns one weight row of the 128-row tile, loads the
+//   warps 2-9   dequant producers: two threads per weight row of the 128-row tile; each loads the
 //               packed superblock fields with 16-byte loads (one stage ahead), unpacks nibbles and
 //               6-bit scales in registers and writes bf16 into the swizzled shared-memory A tile
-//   warps 6-9   epilogue: tcgen05.ld the fp32 accumulators, SwiGLU + route weight, bf16 stores
+//   warps 10-13 epilogue: tcgen05.ld the fp32 accumulators, SwiGLU + route weight, stores
 // Every wait is bounded (about one second); on a timeout the kernel records a code in *err and
 // every role leaves its loop, waits for its own copies and MMAs, and frees TMEM.
 #include "ck_common.cuh"
@@ -27,7 +30,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int BN = 256;
-constexpr int NDQ = 4;   // dequant warps
+constexpr int NDQ = 8;   // dequant warps (two threads per weight row)
 constexpr int NEPI = 4;  // epilogue warps
 constexpr int NTHREADS = (2 + NDQ + NEPI) * 32;
 constexpr int A_BYTES = BM * BK * 2;
@@ -66,41 +69,48 @@ CK_DEV void load_packed(Packed &p, const uint8_t *base, uint64_t flat) {
     p.q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + p.c * 32));
 }
 
-// Dequantize 64 weights of one row into the 128-byte swizzled smem row `r` of tile `a`.
-CK_DEV void dequant_store(const Packed &p, uint8_t *a, int r) {
+// Two adjacent weights (k, k+1) as bf16x2 from the nibbles of two qs bytes spread to the low byte
+// of each 16-bit half (pp = byte_k | byte_k+1 << 16).  OR-ing a nibble q into the mantissa of
+// bf16 128.0 (0x4300) gives exactly 128 + q; subtracting 128 is exact; then one bf16x2 FMA
+// q * (d*sc) - dmin*m rounds the weight once.
+CK_DEV uint32_t deq_pair(uint32_t pp, int hi, __nv_bfloat162 ds2, __nv_bfloat162 ndm2) {
+    const uint32_t v = ((hi ? (pp >> 4) : pp) & 0x000F000Fu) | 0x43004300u;
+    const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162 *>(&v), __floats2bfloat162_rn(128.f, 128.f));
+    const __nv_bfloat162 w = __hfma2(q, ds2, ndm2);
+    return *reinterpret_cast<const uint32_t *>(&w);
+}
+
+// Dequantize one 32-weight half of the 64-weight chunk into the 128-byte swizzled smem row `r` of
+// tile `a`: half 0 = sub-block 2c (low nibbles, k = 0..31), half 1 = sub-block 2c+1 (high
+// nibbles, k = 32..63).  16-byte chunk cc of the row holds k = 8cc .. 8cc+7 and sits at position
+// cc ^ (r & 7) (the 128-byte swizzle the MMA descriptor names).
+CK_DEV void dequant_half(const Packed &p, uint8_t *a, int r, int half) {
     const float d = f16_bits_to_float(p.hdr.x & 0xFFFF), dmin = f16_bits_to_float(p.hdr.x >> 16);
     uint32_t s[3] = {p.hdr.y, p.hdr.z, p.hdr.w};
-    int sc0, m0, sc1, m1;
-    q4k_scale_min(s, 2 * p.c, sc0, m0);
-    q4k_scale_min(s, 2 * p.c + 1, sc1, m1);
-    const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0, ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
+    int sc, mn;
+    q4k_scale_min(s, 2 * p.c + half, sc, mn);
+    const float ds = d * (float)sc, dm = dmin * (float)mn;  // both exact in fp32
+    const __nv_bfloat162 ds2 = __floats2bfloat162_rn(ds, ds), ndm2 = __floats2bfloat162_rn(-dm, -dm);
     const uint32_t qw[8] = {p.q0.x, p.q0.y, p.q0.z, p.q0.w, p.q1.x, p.q1.y, p.q1.z, p.q1.w};
     uint8_t *row = a + r * 128;
     const int sw = r & 7;
 #pragma unroll
-    for (int cc = 0; cc < 8; ++cc) {
-        // chunk cc holds k = 8cc .. 8cc+7: qs bytes 8(cc&3) .. +7, low nibbles for cc < 4
-        const uint32_t w0 = qw[2 * (cc & 3)], w1 = qw[2 * (cc & 3) + 1];
-        const int sh = cc < 4 ? 0 : 4;
-        const float ds = cc < 4 ? ds0 : ds1, dm = cc < 4 ? dm0 : dm1;
-        float v[8];
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            v[b] = fmaf(ds, (float)((w0 >> (8 * b + sh)) & 15), -dm);
-            v[4 + b] = fmaf(ds, (float)((w1 >> (8 * b + sh)) & 15), -dm);
-        }
+    for (int c4 = 0; c4 < 4; ++c4) {
+        const uint32_t w0 = qw[2 * c4], w1 = qw[2 * c4 + 1];
         uint4 o;
-        o.x = pack_bf16x2(v[0], v[1]);
-        o.y = pack_bf16x2(v[2], v[3]);
-        o.z = pack_bf16x2(v[4], v[5]);
-        o.w = pack_bf16x2(v[6], v[7]);
-        *reinterpret_cast<uint4 *>(row + ((cc ^ sw) << 4)) = o;
+        o.x = deq_pair(__byte_perm(w0, 0u, 0x4140), half, ds2, ndm2);
+        o.y = deq_pair(__byte_perm(w0, 0u, 0x4342), half, ds2, ndm2);
+        o.z = deq_pair(__byte_perm(w1, 0u, 0x4140), half, ds2, ndm2);
+        o.w = deq_pair(__byte_perm(w1, 0u, 0x4342), half, ds2, ndm2);
+        *reinterpret_cast<uint4 *>(row + (((c4 + 4 * half) ^ sw) << 4)) = o;
     }
 }
 
-template <int DUAL>
-__global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap tmap_x, GemmParams p) {
+template <int DUAL, int DENSE>
+__global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap tmap_x,
+                                                          const __grid_constant__ CUtensorMap tmap_a, GemmParams p) {
     using C = Cfg<DUAL>;
+    static_assert(!(DUAL && DENSE), "the dense form has one accumulator");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
@@ -117,6 +127,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
     const int nrt = (int)((p.N + BM - 1) / BM);
     const int nunits = ntiles * nrt;
     const int nk = (int)(p.K / BK);
+    // the x operand's own K steps: the dense form walks x once per bf16 term of the split A
+    const int nkx = DENSE && p.kx ? (int)(p.kx / BK) : nk;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -131,6 +143,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
         mbar_init(done_bar, 1);
         fence_barrier_init();
         prefetch_tmap(&tmap_x);
+        if (DENSE) prefetch_tmap(&tmap_a);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
@@ -153,8 +166,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                     const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
                     if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, 1)) { ok = false; break; }
                     uint8_t *b_tile = smem + s * C::STAGE_BYTES + C::NMAT * A_BYTES;
-                    mbar_arrive_expect_tx(&full_b[s], B_BYTES);
-                    tma_load_2d(b_tile, &tmap_x, &full_b[s], kb * BK, p.xrow_is_orow ? t.orow : t.xrow);
+                    mbar_arrive_expect_tx(&full_b[s], DENSE ? B_BYTES + A_BYTES : B_BYTES);
+                    tma_load_2d(b_tile, &tmap_x, &full_b[s], (kb % nkx) * BK, p.xrow_is_orow ? t.orow : t.xrow);
+                    if (DENSE) tma_load_2d(smem + s * C::STAGE_BYTES, &tmap_a, &full_b[s], kb * BK, (u % nrt) * BM);
                 }
                 if (!ok) break;
             }
@@ -182,7 +196,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-                    if (!mbar_wait_bounded(&full_a[s], ph, p.err, 3) || !mbar_wait_bounded(&full_b[s], ph, p.err, 4)) {
+                    if ((!DENSE && !mbar_wait_bounded(&full_a[s], ph, p.err, 3)) ||
+                        !mbar_wait_bounded(&full_b[s], ph, p.err, 4)) {
                         ok = false;
                         break;
                     }
@@ -205,54 +220,59 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
             umma_commit(done_bar);
             mbar_wait_bounded(done_bar, 0, nullptr, 0);
         }
-    } else if (warp < 2 + NDQ) {
+    } else if (warp < 2 + NDQ && !DENSE) {  // in the dense form the A operand arrives by TMA
         // ------------------------------------------------------------ dequant producers
-        const int r = threadIdx.x - 64;  // row within the 128-row tile
+        // 256 threads: thread i owns row (i & 127) of the tile; part = i >> 7 selects the matrix
+        // (dual: gate or up, both halves of the 64-weight chunk) or the nibble half (single).
+        const int di = threadIdx.x - 64;
+        const int r = di & (BM - 1);
+        const int part = di >> 7;
         int it = 0;
         // software pipeline: the packed fields of step it+1 are in flight while step it is unpacked
-        Packed cur[C::NMAT], nxt[C::NMAT];
+        Packed cur, nxt;
         int u = blockIdx.x, kb = 0;
-        auto bases = [&](int uu, const uint8_t *&b0, const uint8_t *&b1, uint64_t &rowflat) {
+        auto base_of = [&](int uu, uint64_t &rowflat) -> const uint8_t * {
             const Tile t = load_tile(p.tiles, uu / nrt);
             const int n0 = (uu % nrt) * BM;
             const uint32_t row = min((uint32_t)(n0 + r), p.N - 1);
             const bool shared = (uint32_t)t.g >= p.n_routed;
             const uint64_t g = shared ? (uint64_t)(t.g - p.n_routed) : (uint64_t)t.g;
-            b0 = (shared ? p.s0 : p.w0) + g * p.w_stride;
-            b1 = DUAL ? (shared ? p.s1 : p.w1) + g * p.w_stride : nullptr;
+            const uint8_t *b = (DUAL && part) ? (shared ? p.s1 : p.w1) : (shared ? p.s0 : p.w0);
             rowflat = (uint64_t)row * p.K;
+            return b + g * p.w_stride;
         };
-        const uint8_t *b0 = nullptr, *b1 = nullptr;
+        const uint8_t *b = nullptr;
         uint64_t rowflat = 0;
         if (u < nunits) {
-            bases(u, b0, b1, rowflat);
-            load_packed(nxt[0], b0, rowflat);
-            if (DUAL) load_packed(nxt[1], b1, rowflat);
+            b = base_of(u, rowflat);
+            load_packed(nxt, b, rowflat);
         }
         while (u < nunits) {
-#pragma unroll
-            for (int m = 0; m < C::NMAT; ++m) cur[m] = nxt[m];
+            cur = nxt;
             // advance to the next (unit, k step) and issue its loads
             int nu = u, nkb = kb + 1;
             if (nkb == nk) { nkb = 0; nu = u + gridDim.x; }
             if (nu < nunits) {
-                if (nu != u) bases(nu, b0, b1, rowflat);
-                load_packed(nxt[0], b0, rowflat + (uint64_t)nkb * BK);
-                if (DUAL) load_packed(nxt[1], b1, rowflat + (uint64_t)nkb * BK);
+                if (nu != u) b = base_of(nu, rowflat);
+                load_packed(nxt, b, rowflat + (uint64_t)nkb * BK);
             }
             const int s = it % C::STAGES;
             const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
             if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, 5)) break;
             uint8_t *a = smem + s * C::STAGE_BYTES;
-            dequant_store(cur[0], a, r);
-            if (DUAL) dequant_store(cur[1], a + A_BYTES, r);
+            if (DUAL) {
+                dequant_half(cur, a + part * A_BYTES, r, 0);
+                dequant_half(cur, a + part * A_BYTES, r, 1);
+            } else {
+                dequant_half(cur, a, r, part);
+            }
             fence_proxy_async_smem();
             mbar_arrive(&full_a[s]);
             ++it;
             u = nu;
             kb = nkb;
         }
-    } else {
+    } else if (warp >= 2 + NDQ) {
         // ------------------------------------------------------------ epilogue
         const int sp = warp & 3;  // TMEM sub-partition this warp may read
         int ut = 0;
@@ -281,7 +301,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                             const float rw = p.row_w ? p.row_w[t.orow + tok] : 1.0f;
                             val = (val / (1.0f + __expf(-val))) * up * rw;
                         }
-                        out[(uint64_t)(t.orow + tok) * p.N + row] = __float2bfloat16_rn(val);
+                        if (DENSE)
+                            p.out_f32[(uint64_t)(t.orow + tok) * p.N + row] = val;
+                        else
+                            out[(uint64_t)(t.orow + tok) * p.N + row] = __float2bfloat16_rn(val);
                     }
                 }
             }
@@ -316,13 +339,13 @@ static EncodeTiledFn get_encode() {
     return fn;
 }
 
-// bf16 [rows, K] row-major, box = BN rows x 64 columns, 128-byte swizzle.
-static int make_x_map(CUtensorMap *m, const void *x, uint32_t rows, uint32_t K) {
+// bf16 [rows, K] row-major, box = box_rows x 64 columns, 128-byte swizzle.
+static int make_map(CUtensorMap *m, const void *x, uint32_t rows, uint32_t K, uint32_t box_rows) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return CK_ERR_NODEV;
     cuuint64_t dims[2] = {K, rows};
     cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    cuuint32_t box[2] = {BK, BN};
+    cuuint32_t box[2] = {BK, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -330,25 +353,32 @@ static int make_x_map(CUtensorMap *m, const void *x, uint32_t rows, uint32_t K) 
     return r == CUDA_SUCCESS ? 0 : CK_ERR_ARG;
 }
 
-template <int DUAL>
+template <int DUAL, int DENSE>
 static int launch_t(const GemmParams &p, cudaStream_t s) {
     using C = Cfg<DUAL>;
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_q4k<DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaError_t e =
+            cudaFuncSetAttribute(k_gemm_q4k<DUAL, DENSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return (int)e;
         attr = true;
     }
-    CUtensorMap m;
-    int rc = make_x_map(&m, p.x, p.x_rows, p.K);
+    CUtensorMap mx, ma;
+    int rc = make_map(&mx, p.x, p.x_rows, DENSE && p.kx ? p.kx : p.K, BN);
     if (rc) return rc;
+    if (DENSE) {
+        rc = make_map(&ma, p.a_dense, p.N, p.K, BM);
+        if (rc) return rc;
+    } else {
+        ma = mx;
+    }
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const long long units = (long long)p.max_tiles * ((p.N + BM - 1) / BM);
     const int grid = (int)(units < nsm ? units : nsm);
     if (grid <= 0) return 0;
-    k_gemm_q4k<DUAL><<<grid, NTHREADS, C::SMEM, s>>>(m, p);
+    k_gemm_q4k<DUAL, DENSE><<<grid, NTHREADS, C::SMEM, s>>>(mx, ma, p);
     return (int)cudaGetLastError();
 }
 }  // namespace gemm
@@ -358,7 +388,14 @@ int launch_gemm_q4k(const GemmParams &p, cudaStream_t s) {
     if (p.K % gemm::BK != 0 || p.N == 0 || p.K == 0 || ((uint64_t)p.N * p.K) % 256 != 0) return CK_ERR_SHAPE;
     if (p.dual && !p.w1) return CK_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.w0) & 15)) return CK_ERR_ARG;
-    return p.dual ? gemm::launch_t<1>(p, s) : gemm::launch_t<0>(p, s);
+    return p.dual ? gemm::launch_t<1, 0>(p, s) : gemm::launch_t<0, 0>(p, s);
+}
+
+int launch_gemm_dense(const GemmParams &p, cudaStream_t s) {
+    if (!p.a_dense || !p.x || !p.out_f32 || !p.tiles || !p.ntiles || !p.err) return CK_ERR_ARG;
+    if (p.K % gemm::BK != 0 || p.K == 0 || p.N == 0 || (p.kx && (p.kx % gemm::BK || p.K % p.kx))) return CK_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.a_dense) & 15)) return CK_ERR_ARG;
+    return gemm::launch_t<0, 1>(p, s);
 }
 
 }  // namespace ck

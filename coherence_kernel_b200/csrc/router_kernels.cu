@@ -254,42 +254,50 @@ CK_DEV void ref_topk(double *s, int n, int k, int *out) {
 
 constexpr int EX_THREADS = 256;
 constexpr int EX_MAXE = 256;
+constexpr int EX_TB = 2;
 __global__ void __launch_bounds__(EX_THREADS) k_route_exact(const uint16_t *__restrict__ x, const float *__restrict__ W,
                                                             const float *__restrict__ bias, int32_t *__restrict__ ids,
                                                             float *__restrict__ wts, const uint32_t *__restrict__ flag_list,
                                                             const uint32_t *__restrict__ flag_count, RouteParams p) {
+    // EX_TB flagged tokens per block share each 32-column tile of the router; thread e folds
+    // expert e for all of them (independent chains)
     __shared__ float wtile[EX_MAXE][33];
-    __shared__ double xtile[32];
-    __shared__ double lg[EX_MAXE], sc[EX_MAXE], tmp[EX_MAXE];
+    __shared__ double xtile[EX_TB][32];
+    __shared__ double lgs[EX_TB][EX_MAXE], scs[EX_TB][EX_MAXE], tmps[EX_TB][EX_MAXE];
     const uint32_t nflag = *flag_count;
-    for (uint32_t f = blockIdx.x; f < nflag; f += gridDim.x) {
-        const uint32_t t = flag_list[f];
+    for (uint32_t f0 = blockIdx.x * EX_TB; f0 < nflag; f0 += gridDim.x * EX_TB) {
+        const int nt = (int)min((uint32_t)EX_TB, nflag - f0);
         // logits: right fold over j descending, acc = w*x + acc in fp64 (transformer-block.fk:25-26)
-        double acc[EX_MAXE / EX_THREADS];
-        for (int q = 0; q < EX_MAXE / EX_THREADS; ++q) acc[q] = 0.0;
+        double acc[EX_TB];
+        for (int q = 0; q < EX_TB; ++q) acc[q] = 0.0;
+        const int e = threadIdx.x;
         for (int j0 = (int)p.hidden - 32; j0 >= 0; j0 -= 32) {
             __syncthreads();
             for (int i = threadIdx.x; i < (int)p.ne * 32; i += EX_THREADS) {
-                const int e = i >> 5, j = i & 31;
-                wtile[e][j] = W[(size_t)e * p.hidden + j0 + j];
+                const int ee = i >> 5, j = i & 31;
+                wtile[ee][j] = W[(size_t)ee * p.hidden + j0 + j];
             }
-            if (threadIdx.x < 32) xtile[threadIdx.x] = (double)bf16_bits_to_float(x[(size_t)t * p.hidden + j0 + threadIdx.x]);
+            for (int i = threadIdx.x; i < EX_TB * 32; i += EX_THREADS) {
+                const int q = i >> 5, j = i & 31;
+                const uint32_t t = flag_list[f0 + min(q, nt - 1)];
+                xtile[q][j] = (double)bf16_bits_to_float(x[(size_t)t * p.hidden + j0 + j]);
+            }
             __syncthreads();
-            for (int q = 0; q < EX_MAXE / EX_THREADS; ++q) {
-                const int e = threadIdx.x + q * EX_THREADS;
-                if (e < (int)p.ne) {
+            if (e < (int)p.ne) {
+#pragma unroll
+                for (int q = 0; q < EX_TB; ++q) {
                     double a = acc[q];
-                    for (int j = 31; j >= 0; --j) a = __dadd_rn(__dmul_rn((double)wtile[e][j], xtile[j]), a);
+                    for (int j = 31; j >= 0; --j) a = __dadd_rn(__dmul_rn((double)wtile[e][j], xtile[q][j]), a);
                     acc[q] = a;
                 }
             }
         }
-        for (int q = 0; q < EX_MAXE / EX_THREADS; ++q) {
-            const int e = threadIdx.x + q * EX_THREADS;
-            if (e < (int)p.ne) lg[e] = acc[q];
-        }
+        if (e < (int)p.ne)
+            for (int q = 0; q < EX_TB; ++q) lgs[q][e] = acc[q];
         __syncthreads();
-        if (threadIdx.x == 0) {
+        if (threadIdx.x < nt) {
+            const uint32_t t = flag_list[f0 + threadIdx.x];
+            double *lg = lgs[threadIdx.x], *sc = scs[threadIdx.x], *tmp = tmps[threadIdx.x];
             const int ne = (int)p.ne, k = (int)p.nsel;
             int sel[16];
             double w[16];
@@ -456,6 +464,32 @@ __global__ void k_route_dsv4_tokens(const float *__restrict__ L, const float *__
             wts[(size_t)t * nused + j] = pp[src] * scl;
         }
     }
+}
+
+// ------------------------------------------------------------------ router split for the tensor cores
+// out[r, i*k + j] = term i of w[r, j]: t1 = bf16(w), t2 = bf16(w - t1), t3 = bf16(w - t1 - t2).
+// Each difference is exact in fp32, so t1 + t2 + t3 carries about 24 significand bits of w and
+// x . (t1 + t2 + t3) on bf16 tensor cores (exact bf16 products, fp32 accumulation) stands in for
+// the fp32 router product.
+__global__ void k_split_bf16x3(const float *__restrict__ w, __nv_bfloat16 *__restrict__ out, uint32_t rows, uint32_t k) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)rows * k) return;
+    const uint64_t r = i / k, j = i - r * k;
+    const float v = w[i];
+    const __nv_bfloat16 a = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(a);
+    const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+    const float r2 = r1 - __bfloat162float(b);
+    const __nv_bfloat16 c = __float2bfloat16_rn(r2);
+    __nv_bfloat16 *o = out + r * 3 * k;
+    o[j] = a;
+    o[k + j] = b;
+    o[2 * k + j] = c;
+}
+int launch_split_bf16x3(const float *w, uint16_t *out, uint32_t rows, uint32_t k, cudaStream_t s) {
+    const uint64_t n = (uint64_t)rows * k;
+    if (n) k_split_bf16x3<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(w, (__nv_bfloat16 *)out, rows, k);
+    return (int)cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ launchers

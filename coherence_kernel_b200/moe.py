@@ -107,7 +107,7 @@ class MoELayer:
         w["err"].zero_()
         mark("start")
         _lib.check(L.ck_moe_route(cfg, _ptr(x), T, _ptr(self.router_w), _ptr(self.bias), _ptr(w["logits"]), _ptr(ids),
-                                  _ptr(wts), _ptr(w["flags"]), st), "route")
+                                  _ptr(wts), _ptr(w["route"]), w["route"].numel(), st), "route")
         mark("route")
         _lib.check(L.ck_moe_permute(_ptr(ids), _ptr(wts), _ptr(x), T, K, E, sp.n_shared, H, int(sp.mode == 4),
                                     _ptr(w["xp"]), _ptr(w["row_w"]), _ptr(w["pair_pos"]), _ptr(counts), _ptr(w["tiles"]),
@@ -142,7 +142,9 @@ class MoELayer:
             off += _align(nbytes)
 
         take("logits", T * E * 4, torch.float32, (T, E))
-        take("flags", (T + 1) * 4, torch.int32, (T + 1,))
+        rw = L.ck_moe_route_workspace_bytes(ctypes.byref(self._cfg), T)
+        views["route"] = self.ws[off:off + rw]
+        off += _align(rw)
         pw = L.ck_moe_permute_workspace_bytes(T, K, E)
         views["perm_ws"] = self.ws[off:off + pw]
         off += _align(pw)
@@ -156,6 +158,11 @@ class MoELayer:
         take("err", 4, torch.int32, (1,))
         views["mt"] = mt
         return views
+
+    def flagged(self, ntok) -> int:
+        """Tokens the last layer re-routed in fp64 (synchronizes)."""
+        w = self._ws_views(ntok)
+        return _lib.load().ck_moe_route_flagged(ctypes.byref(self._cfg), ntok, _ptr(w["route"]), _stream())
 
     def status(self, ntok):
         """Synchronize and raise if a device-side wait of the last layer gave up."""
@@ -205,7 +212,8 @@ class ExpertParallelMoE:
         self.dev = dev
         # source side
         self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
-        self.flags = torch.empty(T + 1, dtype=torch.int32, device=dev)
+        self.route_ws = torch.empty(_align(L.ck_moe_route_workspace_bytes(ctypes.byref(self._cfg), T)),
+                                    dtype=torch.uint8, device=dev)
         self.xp = torch.empty((A + T, H), dtype=torch.bfloat16, device=dev)
         self.row_w = torch.empty(A + sp.n_shared * T, dtype=torch.float32, device=dev)
         self.pair_pos = torch.empty(A, dtype=torch.int32, device=dev)
@@ -253,7 +261,8 @@ class ExpertParallelMoE:
         out = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         self.err.zero_()
         _lib.check(L.ck_moe_route(ctypes.byref(self._cfg), _ptr(x), T, _ptr(self.router_w), _ptr(self.bias),
-                                  _ptr(self.logits), _ptr(ids), _ptr(wts), _ptr(self.flags), st), "ck_moe_route")
+                                  _ptr(self.logits), _ptr(ids), _ptr(wts), _ptr(self.route_ws),
+                                  self.route_ws.numel(), st), "ck_moe_route")
         _lib.check(L.ck_moe_permute(_ptr(ids), _ptr(wts), _ptr(x), T, K, E, sp.n_shared, H, int(sp.mode == 4),
                                     _ptr(self.xp), _ptr(self.row_w), _ptr(self.pair_pos), _ptr(self.counts),
                                     _ptr(self.tiles), _ptr(self.ntiles), _ptr(self.perm_ws), st), "ck_moe_permute")

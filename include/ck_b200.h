@@ -102,10 +102,16 @@ int ck_moe_layer_bf16(const ck_moe_config *cfg, const void *x_bf16_dev, uint32_t
  * the grouped GEMM gave up (the layer's output is then not valid), else 0. */
 int ck_moe_layer_status(const ck_moe_config *cfg, uint32_t ntok, const void *workspace_dev, void *stream);
 
-/* the layer's steps, for callers that place an all-to-all between them (expert parallelism) */
+/* the layer's steps, for callers that place an all-to-all between them (expert parallelism).
+ * ck_moe_route: router logits on the tensor cores (the fp32 router split into three bf16 terms),
+ * selection, and the exact fp64 re-route of near-tie tokens; route_ws sized by
+ * ck_moe_route_workspace_bytes.  ck_moe_route_flagged synchronizes and answers how many tokens
+ * the last route re-routed exactly. */
+size_t ck_moe_route_workspace_bytes(const ck_moe_config *cfg, uint32_t ntok);
 int ck_moe_route(const ck_moe_config *cfg, const void *x_bf16_dev, uint32_t ntok, const float *router_w_dev,
-                 const float *bias_dev, float *logits_dev, int32_t *ids_dev, float *wts_dev, uint32_t *flags_dev,
-                 void *stream);
+                 const float *bias_dev, float *logits_dev, int32_t *ids_dev, float *wts_dev, void *route_ws_dev,
+                 size_t route_ws_bytes, void *stream);
+int ck_moe_route_flagged(const ck_moe_config *cfg, uint32_t ntok, const void *route_ws_dev, void *stream);
 size_t ck_moe_permute_workspace_bytes(uint32_t ntok, uint32_t nsel, uint32_t n_experts);
 uint32_t ck_moe_max_tiles(uint32_t ntok, uint32_t nsel, uint32_t n_experts, uint32_t n_shared);
 int ck_moe_permute(const int32_t *ids_dev, const float *wts_dev, const void *x_bf16_dev, uint32_t ntok,

@@ -25,10 +25,13 @@ def layer_for(spec, w, ntok):
                     t(w["s_down"]) if spec.n_shared else None, t(w["router"]), t(w["bias"]), max_tokens=ntok)
 
 
-def run_layer(spec, w, x):
+def run_layer(spec, w, x, keep=None):
     lay = layer_for(spec, w, x.shape[0])
     out, ids, wts, counts = lay(torch.from_numpy(x.view(np.int16)).cuda())
     lay.status(x.shape[0])
+    if keep is not None:
+        keep["logits"] = lay._ws_views(x.shape[0])["logits"].cpu().numpy()
+        keep["flagged"] = lay.flagged(x.shape[0])
     return (out.float().cpu().numpy(), ids.cpu().numpy(), wts.cpu().numpy(), counts.cpu().numpy())
 
 
@@ -55,7 +58,14 @@ def test_moe_golden(mode):
 
 def full_size(spec, ntok, sample):
     w = workloads.make_moe(spec, ntok, seed=0)
-    out, ids, wts, counts = run_layer(spec, w, w["x"])
+    keep = {}
+    out, ids, wts, counts = run_layer(spec, w, w["x"], keep)
+    # the tensor-core logits (three-term bf16 split of the fp32 router) against fp64: their error
+    # must sit far below the margin tau under which a token is re-routed exactly
+    ref_logits = synth.bf16_bits_to_f32(w["x"]).astype(np.float64) @ w["router"].astype(np.float64).T
+    lerr = np.abs(keep["logits"] - ref_logits).max()
+    print(f"router logits max abs error {lerr:.3e}, tokens re-routed exactly {keep['flagged']}")
+    assert lerr <= spec.tau / 4
     cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
                     spec.topk_groups, spec.wscale)
     rids, rwts, margin = O.moe_route(cfg, w["router"], w["bias"], w["x"])

@@ -72,9 +72,10 @@ def test_q4k_matvec_sizes(rows, cols):
     x = rng.standard_normal(cols).astype(np.float32)
     y = ops.q4k_matvec(dev(q), dev(x), rows, cols).cpu().numpy()
     sample = np.unique(np.linspace(0, rows - 1, 64).astype(int))
+    x64 = x.astype(np.float64)
     for r in sample:
         w = O.q4k_dequant(q, r * cols, cols)
-        ref = O.lib().ckr_dot(w.ctypes.data, x.astype(np.float64).ctypes.data, cols)
+        ref = O.lib().ckr_dot(w.ctypes.data, x64.ctypes.data, cols)
         assert abs(y[r] - ref) <= 1e-3 * np.abs(w * x).sum(), r
 
 
