@@ -43,6 +43,11 @@ struct Cfg {
     static constexpr int STAGES = DUAL ? 3 : 4;
     static constexpr int ACC_COLS = NMAT * BN;
     static constexpr int ACC_BUFS = 512 / ACC_COLS;
+    // the dense form splits its K loop over DENSE_ACC accumulators of 128 columns (token tiles of
+    // at most 128) and sums them in fp32 in the epilogue: each tensor-core accumulation chain is a
+    // quarter as long, and so is its rounding error
+    static constexpr int DENSE_ACC = 4;
+    static constexpr int DENSE_TILE = 128;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
 };
@@ -111,6 +116,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap tmap_a, GemmParams p) {
     using C = Cfg<DUAL>;
     static_assert(!(DUAL && DENSE), "the dense form has one accumulator");
+    constexpr int NBUF = DENSE ? 1 : C::ACC_BUFS;  // accumulator buffers in flight
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
@@ -188,11 +194,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                 int nmma = ((t.ntok + 15) / 16) * 16;
                 nmma = nmma < 16 ? 16 : (nmma > BN ? BN : nmma);
                 const uint32_t idesc = idesc_bf16(BM, nmma);
-                const int ab = ut % C::ACC_BUFS;
-                const uint32_t aph = (uint32_t)(ut / C::ACC_BUFS) & 1u;
+                const int ab = ut % NBUF;
+                const uint32_t aph = (uint32_t)(ut / NBUF) & 1u;
                 if (!mbar_wait_bounded(&acc_empty[ab], aph ^ 1u, p.err, 2)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
+                const int chunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
@@ -204,11 +211,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
                     const uint32_t b0 = smem_u32(smem + s * C::STAGE_BYTES + C::NMAT * A_BYTES);
+                    // dense form: K chunk kb / chunk accumulates into its own 128-column accumulator
+                    const uint32_t dd = DENSE ? d0 + (uint32_t)((kb / chunk) * C::DENSE_TILE) : d0;
+                    const int kfirst = DENSE ? kb % chunk : kb;
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         const uint64_t bd = sdesc_k_sw128(b0 + k * 32);
-                        const uint32_t acc = (kb | k) != 0;
-                        umma_bf16(d0, sdesc_k_sw128(a0 + k * 32), bd, idesc, acc);
+                        const uint32_t acc = (kfirst | k) != 0;
+                        umma_bf16(dd, sdesc_k_sw128(a0 + k * 32), bd, idesc, acc);
                         if (DUAL) umma_bf16(d0 + BN, sdesc_k_sw128(a0 + A_BYTES + k * 32), bd, idesc, acc);
                     }
                     umma_commit(&empty[s]);
@@ -280,8 +290,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ut) {
             const Tile t = load_tile(p.tiles, u / nrt);
             const int n0 = (u % nrt) * BM;
-            const int ab = ut % C::ACC_BUFS;
-            const uint32_t aph = (uint32_t)(ut / C::ACC_BUFS) & 1u;
+            const int ab = ut % NBUF;
+            const uint32_t aph = (uint32_t)(ut / NBUF) & 1u;
             if (!mbar_wait_bounded(&acc_full[ab], aph, p.err, 6)) break;
             tc_fence_after();
             const uint32_t row = (uint32_t)(n0 + 32 * sp + lane);
@@ -291,6 +301,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                 tmem_ld32(tbase + cb * 32, g);
                 if (DUAL) tmem_ld32(tbase + BN + cb * 32, v);
                 tmem_ld_wait();
+                if (DENSE) {
+                    // sum the K-chunk accumulators in fp32, in chunk order
+#pragma unroll 1
+                    for (int a = 1; a < C::DENSE_ACC; ++a) {
+                        tmem_ld32(tbase + a * C::DENSE_TILE + cb * 32, v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) g[j] = __float_as_uint(__uint_as_float(g[j]) + __uint_as_float(v[j]));
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int tok = cb * 32 + j;

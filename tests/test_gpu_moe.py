@@ -65,7 +65,9 @@ def full_size(spec, ntok, sample):
     ref_logits = synth.bf16_bits_to_f32(w["x"]).astype(np.float64) @ w["router"].astype(np.float64).T
     lerr = np.abs(keep["logits"] - ref_logits).max()
     print(f"router logits max abs error {lerr:.3e}, tokens re-routed exactly {keep['flagged']}")
-    assert lerr <= spec.tau / 4
+    # the margin is in score units: sigmoid(l) + b moves by at most |dl|/4, softmax order by |dl|
+    score_err = lerr / 4 if spec.mode == 4 else lerr
+    assert score_err <= spec.tau / 4
     cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
                     spec.topk_groups, spec.wscale)
     rids, rwts, margin = O.moe_route(cfg, w["router"], w["bias"], w["x"])
