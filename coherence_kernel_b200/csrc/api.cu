@@ -31,6 +31,7 @@ struct RouteWs {
     int32_t *ntiles;
     int *err;
     uint32_t *flags;
+    double *exact;  // fp64 logits of the flagged tokens
     size_t total;
 };
 RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
@@ -43,6 +44,7 @@ RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
     w.ntiles = (int32_t *)take(4);
     w.err = (int *)take(4);
     w.flags = (uint32_t *)take(((size_t)ntok + 1) * 4);
+    w.exact = (double *)take((size_t)ntok * c->n_experts * 8);
     w.total = o;
     return w;
 }
@@ -250,7 +252,7 @@ int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const flo
     RouteWs w = route_ws(c, ntok, ws);
     // logits on the tensor cores: x . [W1 | W2 | W3]^T with the fp32 router split into bf16 terms
     rc = ck::launch_split_bf16x3(rw, w.wsplit, c->n_experts, c->hidden, S(s));
-    if (!rc) rc = ck::launch_single_tiles(w.tiles, w.ntiles, ntok, 128, S(s));
+    if (!rc) rc = ck::launch_single_tiles(w.tiles, w.ntiles, ntok, 64, S(s));
     if (rc) return fail(rc, "ck_moe_route split");
     cudaMemsetAsync(w.err, 0, 4, S(s));
     ck::GemmParams g = {};
@@ -271,7 +273,7 @@ int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const flo
     ck::RouteParams p = {ntok, c->n_experts, c->nsel, c->hidden, c->mode, c->ngroups, c->topk_groups, c->wscale, c->tau};
     rc = ck::launch_route_select(logits, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
     if (rc) return fail(rc, "ck_moe_route select");
-    rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
+    rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, w.flags + 1, w.flags, w.exact, p, S(s));
     return fail(rc, "ck_moe_route exact");
 }
 

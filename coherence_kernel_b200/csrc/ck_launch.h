@@ -40,8 +40,10 @@ struct RouteParams {
 };
 int launch_route_select(const float *logits, const float *bias, int32_t *ids, float *wts, uint32_t *flag_list,
                         uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
+// scratch: fp64 [ntok, ne] (the exact logits of the flagged tokens)
 int launch_route_exact(const uint16_t *x_bf16, const float *w, const float *bias, int32_t *ids, float *wts,
-                       const uint32_t *flag_list, const uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
+                       const uint32_t *flag_list, const uint32_t *flag_count, double *scratch, const RouteParams &p,
+                       cudaStream_t s);
 
 // MoE permute / combine (moe_kernels.cu)
 struct PermuteParams {

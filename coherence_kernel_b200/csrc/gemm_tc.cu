@@ -43,11 +43,12 @@ struct Cfg {
     static constexpr int STAGES = DUAL ? 3 : 4;
     static constexpr int ACC_COLS = NMAT * BN;
     static constexpr int ACC_BUFS = 512 / ACC_COLS;
-    // the dense form splits its K loop over DENSE_ACC accumulators of 128 columns (token tiles of
-    // at most 128) and sums them in fp32 in the epilogue: each tensor-core accumulation chain is a
-    // quarter as long, and so is its rounding error
-    static constexpr int DENSE_ACC = 4;
-    static constexpr int DENSE_TILE = 128;
+    // the dense form splits its K loop over DENSE_ACC accumulators of DENSE_TILE columns (token
+    // tiles of at most DENSE_TILE) and sums them in fp32 in the epilogue: each tensor-core
+    // accumulation chain is an eighth as long, and so is its rounding error
+    static constexpr int DENSE_ACC = 8;
+    static constexpr int DENSE_TILE = 64;
+    static constexpr int DENSE_B_BYTES = DENSE_TILE * BK * 2;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
 };
@@ -172,7 +173,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                     const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
                     if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, 1)) { ok = false; break; }
                     uint8_t *b_tile = smem + s * C::STAGE_BYTES + C::NMAT * A_BYTES;
-                    mbar_arrive_expect_tx(&full_b[s], DENSE ? B_BYTES + A_BYTES : B_BYTES);
+                    mbar_arrive_expect_tx(&full_b[s], DENSE ? C::DENSE_B_BYTES + A_BYTES : B_BYTES);
                     tma_load_2d(b_tile, &tmap_x, &full_b[s], (kb % nkx) * BK, p.xrow_is_orow ? t.orow : t.xrow);
                     if (DENSE) tma_load_2d(smem + s * C::STAGE_BYTES, &tmap_a, &full_b[s], kb * BK, (u % nrt) * BM);
                 }
@@ -192,7 +193,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++ut) {
                 const Tile t = load_tile(p.tiles, u / nrt);
                 int nmma = ((t.ntok + 15) / 16) * 16;
-                nmma = nmma < 16 ? 16 : (nmma > BN ? BN : nmma);
+                const int nmax = DENSE ? C::DENSE_TILE : BN;
+                nmma = nmma < 16 ? 16 : (nmma > nmax ? nmax : nmma);
                 const uint32_t idesc = idesc_bf16(BM, nmma);
                 const int ab = ut % NBUF;
                 const uint32_t aph = (uint32_t)(ut / NBUF) & 1u;
@@ -384,7 +386,7 @@ static int launch_t(const GemmParams &p, cudaStream_t s) {
         attr = true;
     }
     CUtensorMap mx, ma;
-    int rc = make_map(&mx, p.x, p.x_rows, DENSE && p.kx ? p.kx : p.K, BN);
+    int rc = make_map(&mx, p.x, p.x_rows, DENSE && p.kx ? p.kx : p.K, DENSE ? C::DENSE_TILE : BN);
     if (rc) return rc;
     if (DENSE) {
         rc = make_map(&ma, p.a_dense, p.N, p.K, BM);

@@ -1,0 +1,241 @@
+// route_exact.cu -- the exact fp64 re-route of near-tie tokens.
+//
+// A token whose fast-path decision margin is below tau (a chosen/rejected gap at the group or the
+// expert step, or the gap between two chosen experts whose list order it decides) is routed again
+// here with the reference's own numerics, so its expert ids and their list order are the
+// reference's bit for bit:
+//   logits  tb-dot's right fold (transformer-block.fk:25-26): acc = w*x + acc over j descending,
+//           each product exact in fp64 (fp32 w times bf16 x), each add rounded once
+//   mode 4  ln-sigmoid over tn-exp (llama-numerics.fk:29, transformer-numerics.fk:16-24), score =
+//           prob + bias, group score = tn-sum of dsv4-topk-2, dsv4-topk over groups and then over
+//           the masked scores (dsv4-forward.fk:72-81), weights = probs * (wscale / max(sum, 2^-14))
+//   mode 3  mm-softmax (max, tn-exp, left-fold sum, * 1/sum) and mm-topk (moe-msl.fk:73-99)
+// Explicit round-to-nearest intrinsics keep the compiler from contracting a multiply and an add.
+//
+// Two kernels: k_exact_logits spreads (token, expert) right folds over the whole GPU (each fold is a
+// 7168-long dependent chain, so many chains must be in flight); k_exact_select is one warp per
+// token.
+#include "ck_common.cuh"
+#include "ck_launch.h"
+
+namespace ck {
+
+CK_DEV double ref_exp(double x) {
+    int k = 0;
+    for (;;) {
+        const double ax = x < 0.0 ? 0.0 - x : x;
+        if (ax <= 0.5) break;
+        x = __ddiv_rn(x, 2.0);
+        ++k;
+    }
+    double n = 1.0, term = 1.0, acc = 1.0;
+    while (!(n > 14.0)) {
+        const double tt = __dmul_rn(term, __ddiv_rn(x, n));
+        acc = __dadd_rn(acc, tt);
+        term = tt;
+        n = __dadd_rn(n, 1.0);
+    }
+    for (int i = 0; i < k; ++i) acc = __dmul_rn(acc, acc);
+    return acc;
+}
+CK_DEV double ref_sigmoid(double x) { return __ddiv_rn(1.0, __dadd_rn(1.0, ref_exp(__dsub_rn(0.0, x)))); }
+
+constexpr int XL_TOK = 8;    // flagged tokens per work item
+constexpr int XL_EXP = 64;   // experts per work item
+constexpr int XL_J = 32;     // columns per shared-memory tile
+
+// out[f * ne + e] = right fold of router row e with flagged token f's activations, fp64.
+__global__ void __launch_bounds__(256) k_exact_logits(const uint16_t *__restrict__ x, const float *__restrict__ W,
+                                                      const uint32_t *__restrict__ flag_list,
+                                                      const uint32_t *__restrict__ flag_count, double *__restrict__ out,
+                                                      uint32_t ne, uint32_t hidden) {
+    __shared__ float wt[XL_EXP][XL_J + 1];
+    __shared__ double xt[XL_TOK][XL_J];
+    const uint32_t nflag = *flag_count;
+    const int el = threadIdx.x & (XL_EXP - 1);
+    const int q = threadIdx.x / XL_EXP;  // 0..3: this thread folds tokens 2q and 2q+1 of the item
+    const uint32_t ntg = (nflag + XL_TOK - 1) / XL_TOK, neg = (ne + XL_EXP - 1) / XL_EXP;
+    for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
+        const uint32_t f0 = (item / neg) * XL_TOK, e0 = (item % neg) * XL_EXP;
+        double a0 = 0.0, a1 = 0.0;
+        for (int j0 = (int)hidden - XL_J; j0 >= 0; j0 -= XL_J) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < XL_EXP * XL_J; i += blockDim.x) {
+                const uint32_t e = e0 + (i / XL_J);
+                wt[i / XL_J][i % XL_J] = e < ne ? W[(size_t)e * hidden + j0 + (i % XL_J)] : 0.0f;
+            }
+            {
+                const int tq = threadIdx.x / XL_J, j = threadIdx.x % XL_J;  // 8 tokens x 32 columns
+                const uint32_t f = min(f0 + tq, nflag - 1);
+                xt[tq][j] = (double)bf16_bits_to_float(x[(size_t)flag_list[f] * hidden + j0 + j]);
+            }
+            __syncthreads();
+#pragma unroll 8
+            for (int j = XL_J - 1; j >= 0; --j) {
+                const double w = (double)wt[el][j];
+                a0 = __dadd_rn(__dmul_rn(w, xt[2 * q][j]), a0);
+                a1 = __dadd_rn(__dmul_rn(w, xt[2 * q + 1][j]), a1);
+            }
+        }
+        const uint32_t e = e0 + el;
+        if (e < ne) {
+            if (f0 + 2 * q < nflag) out[(size_t)(f0 + 2 * q) * ne + e] = a0;
+            if (f0 + 2 * q + 1 < nflag) out[(size_t)(f0 + 2 * q + 1) * ne + e] = a1;
+        }
+    }
+}
+
+// (value, index) maximum over the warp: the larger value, the lower index on a tie -- the
+// first-maximum rule of a left-to-right scan with strict '>'
+CK_DEV void warp_argmax_d(double &v, int &i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+    }
+}
+
+constexpr int XS_MAXR = 8;  // up to 256 experts: lane holds e = lane + 32 r
+__global__ void k_exact_select(const double *__restrict__ lg, const float *__restrict__ bias, int32_t *__restrict__ ids,
+                               float *__restrict__ wts, const uint32_t *__restrict__ flag_list,
+                               const uint32_t *__restrict__ flag_count, RouteParams p) {
+    __shared__ double sbuf[8][256];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const uint32_t nflag = *flag_count;
+    const int ne = (int)p.ne, k = (int)p.nsel;
+    const double NEG = -1000000000.0;  // dsv4-set-nth's sentinel
+    for (uint32_t f = blockIdx.x * (blockDim.x >> 5) + wib; f < nflag; f += gridDim.x * (blockDim.x >> 5)) {
+        const uint32_t t = flag_list[f];
+        const double *L = lg + (size_t)f * ne;
+        double v[XS_MAXR], pr[XS_MAXR];
+        int sel[16];
+        double w[16];
+        if (p.mode == 4) {
+#pragma unroll
+            for (int r = 0; r < XS_MAXR; ++r) {
+                const int e = lane + 32 * r;
+                pr[r] = e < ne ? ref_sigmoid(L[e]) : 0.0;
+                v[r] = e < ne ? __dadd_rn(pr[r], (double)bias[e]) : -3.0e300;
+            }
+            // group scores: dsv4-topk-2 of the group (first max, then the first max of the rest),
+            // tn-sum over (second, best) = (0 + second) + best
+            const int gs = ne / (int)p.ngroups;
+            double gsc[32];
+            for (int g = 0; g < (int)p.ngroups; ++g) {
+                double b1 = -3.0e300;
+                int i1 = 1 << 30;
+#pragma unroll
+                for (int r = 0; r < XS_MAXR; ++r) {
+                    const int e = lane + 32 * r;
+                    if (e < ne && e / gs == g && (v[r] > b1 || (v[r] == b1 && e < i1))) { b1 = v[r]; i1 = e; }
+                }
+                warp_argmax_d(b1, i1);
+                double b2 = -3.0e300;
+                int i2 = 1 << 30;
+#pragma unroll
+                for (int r = 0; r < XS_MAXR; ++r) {
+                    const int e = lane + 32 * r;
+                    if (e < ne && e / gs == g && e != i1 && (v[r] > b2 || (v[r] == b2 && e < i2))) { b2 = v[r]; i2 = e; }
+                }
+                warp_argmax_d(b2, i2);
+                gsc[g] = __dadd_rn(__dadd_rn(0.0, b2), b1);
+            }
+            unsigned gon = 0;
+            for (int r = 0; r < (int)p.topk_groups; ++r) {
+                double best = -3.0e300;
+                int bi = 0;
+                for (int g = 0; g < (int)p.ngroups; ++g)
+                    if (!(gon >> g & 1) && gsc[g] > best) { best = gsc[g]; bi = g; }
+                gon |= 1u << bi;
+            }
+#pragma unroll
+            for (int r = 0; r < XS_MAXR; ++r) {
+                const int e = lane + 32 * r;
+                if (e < ne && !(gon >> (e / gs) & 1)) v[r] = NEG;
+            }
+            // dsv4-topk over the masked scores: the picks listed last-first
+            for (int r = 0; r < k; ++r) {
+                double b = -3.0e300;
+                int bi = 1 << 30;
+#pragma unroll
+                for (int rr = 0; rr < XS_MAXR; ++rr) {
+                    const int e = lane + 32 * rr;
+                    if (e < ne && v[rr] > b) { b = v[rr]; bi = e; }
+                }
+                warp_argmax_d(b, bi);
+                sel[k - 1 - r] = bi;
+#pragma unroll
+                for (int rr = 0; rr < XS_MAXR; ++rr)
+                    if (lane + 32 * rr == bi) v[rr] = NEG;
+            }
+            double s0 = 0.0;
+            for (int i = 0; i < k; ++i) {
+                double pe = 0.0;
+#pragma unroll
+                for (int rr = 0; rr < XS_MAXR; ++rr)
+                    if (lane + 32 * rr == sel[i]) pe = pr[rr];
+                pe = __shfl_sync(0xffffffffu, pe, sel[i] & 31);
+                w[i] = pe;
+                s0 = __dadd_rn(s0, pe);
+            }
+            const double s = s0 < 0.00006103515625 ? 0.00006103515625 : s0;
+            const double scl = __ddiv_rn((double)p.wscale, s);
+            for (int i = 0; i < k; ++i) w[i] = __dmul_rn(w[i], scl);
+        } else {
+            // mm-softmax: mm-max over the tail from the head, tn-exp of (l - max), the sum as a left
+            // fold in index order, p = e * (1/sum); mm-topk keeps the first index on a tie
+            double *buf = sbuf[wib];
+            for (int e = lane; e < ne; e += 32) buf[e] = L[e];
+            __syncwarp();
+            double mx = buf[0];
+            for (int e = 1; e < ne; ++e)
+                if (buf[e] > mx) mx = buf[e];
+            for (int e = lane; e < ne; e += 32) buf[e] = ref_exp(__dsub_rn(buf[e], mx));
+            __syncwarp();
+            double s = 0.0;
+            for (int e = 0; e < ne; ++e) s = __dadd_rn(s, buf[e]);
+            const double inv = __ddiv_rn(1.0, s);
+#pragma unroll
+            for (int r = 0; r < XS_MAXR; ++r) {
+                const int e = lane + 32 * r;
+                v[r] = e < ne ? __dmul_rn(buf[e], inv) : -3.0e300;
+            }
+            __syncwarp();
+            for (int r = 0; r < k; ++r) {
+                double b = -3.0e300;
+                int bi = 1 << 30;
+#pragma unroll
+                for (int rr = 0; rr < XS_MAXR; ++rr) {
+                    const int e = lane + 32 * rr;
+                    if (e < ne && v[rr] > b) { b = v[rr]; bi = e; }
+                }
+                warp_argmax_d(b, bi);
+                sel[r] = bi;
+                w[r] = b;
+#pragma unroll
+                for (int rr = 0; rr < XS_MAXR; ++rr)
+                    if (lane + 32 * rr == bi) v[rr] = -3.0e300;
+            }
+        }
+        if (lane == 0)
+            for (int i = 0; i < k; ++i) {
+                ids[(size_t)t * k + i] = sel[i];
+                wts[(size_t)t * k + i] = (float)w[i];
+            }
+    }
+}
+
+int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int32_t *ids, float *wts,
+                       const uint32_t *flag_list, const uint32_t *flag_count, double *scratch,
+                       const RouteParams &p, cudaStream_t s) {
+    if (p.ne > 256 || p.hidden % XL_J != 0 || p.nsel > 16 || (p.mode == 4 && p.ngroups > 32)) return CK_ERR_SHAPE;
+    int dev = 0, nsm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    k_exact_logits<<<nsm * 4, 256, 0, s>>>(x, w, flag_list, flag_count, scratch, p.ne, p.hidden);
+    k_exact_select<<<nsm * 2, 256, 0, s>>>(scratch, bias, ids, wts, flag_list, flag_count, p);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace ck

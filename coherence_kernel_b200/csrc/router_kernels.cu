@@ -1,14 +1,17 @@
-// router_kernels.cu -- MoE gating: router logits, top-k selection, and the exact fp64 re-route.
+// router_kernels.cu -- MoE gating: top-k selection, the router split for the tensor cores, and the
+// single-token routers the reference's Form cells dispatch.
 //
 // Selection semantics are the reference's: top-k by repeated argmax where a strict '>' keeps the
 // LOWER expert index on a tie (moe-msl.fk:84-98 mm-argmax-free, dsv4-forward.fk:72-81
 // dsv4-argmax).  The batched layer routes in three steps:
-//   1. k_router_logits   fp32 logits = x . W_r (bf16 x, fp32 W_r)
+//   1. logits            x . W_r on the tensor cores (gemm_tc.cu dense form, W_r split into three
+//                        bf16 terms by k_split_bf16x3); k_router_logits is the fp32 CUDA-core form
 //   2. k_route_select    one warp per token: selection, weights, and the token's decision margin
-//                        (the smallest gap between a chosen and a rejected candidate)
-//   3. k_route_exact     tokens whose margin is below tau are routed again in fp64 with the
-//                        reference's own fold order and numerics (tb-dot right fold, tn-exp,
-//                        ln-sigmoid), so their expert ids are the reference's bit for bit.
+//                        (the smallest gap between a chosen and a rejected candidate, or between
+//                        two chosen ones whose list order it decides)
+//   3. route_exact.cu    tokens whose margin is below tau are routed again in fp64 with the
+//                        reference's own fold order and numerics, so their expert ids are the
+//                        reference's bit for bit.
 #include "ck_common.cuh"
 #include "ck_launch.h"
 
@@ -168,6 +171,9 @@ __global__ void k_route_select(const float *__restrict__ L, const float *__restr
             if (allowed[i] && sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
         warp_argmax(bv, bi);
         if (bv > NEG) margin = fminf(margin, selv[k - 1] - bv);
+        // the list order of the chosen experts is part of the answer: two chosen experts closer
+        // than the margin could be listed in the other order by an exact fold
+        for (int r = 1; r < k; ++r) margin = fminf(margin, selv[r - 1] - selv[r]);
     }
     // weights
     float w[16];
@@ -214,146 +220,6 @@ __global__ void k_route_select(const float *__restrict__ L, const float *__restr
     if (lane == 0 && !(margin >= p.tau)) {
         const uint32_t slot = atomicAdd(flag_count, 1u);
         flag_list[slot] = t;
-    }
-}
-
-// ------------------------------------------------------------------ 3. exact fp64 re-route
-// The reference's numerics in fp64 with explicit round-to-nearest operations (no contraction):
-// transformer-numerics.fk:16-24 tn-exp, llama-numerics.fk:29 ln-sigmoid.
-CK_DEV double ref_exp(double x) {
-    int k = 0;
-    for (;;) {
-        const double ax = x < 0.0 ? 0.0 - x : x;
-        if (ax <= 0.5) break;
-        x = __ddiv_rn(x, 2.0);
-        ++k;
-    }
-    double n = 1.0, term = 1.0, acc = 1.0;
-    while (!(n > 14.0)) {
-        const double tt = __dmul_rn(term, __ddiv_rn(x, n));
-        acc = __dadd_rn(acc, tt);
-        term = tt;
-        n = __dadd_rn(n, 1.0);
-    }
-    for (int i = 0; i < k; ++i) acc = __dmul_rn(acc, acc);
-    return acc;
-}
-CK_DEV double ref_sigmoid(double x) { return __ddiv_rn(1.0, __dadd_rn(1.0, ref_exp(__dsub_rn(0.0, x)))); }
-
-// dsv4-topk over n values in smem: repeated first-maximum, winners set to -1e9, list last-first
-CK_DEV void ref_topk(double *s, int n, int k, int *out) {
-    for (int r = 0; r < k; ++r) {
-        double best = s[0];
-        int bi = 0;
-        for (int i = 1; i < n; ++i)
-            if (s[i] > best) { best = s[i]; bi = i; }
-        s[bi] = -1000000000.0;
-        out[k - 1 - r] = bi;
-    }
-}
-
-constexpr int EX_THREADS = 256;
-constexpr int EX_MAXE = 256;
-constexpr int EX_TB = 2;
-__global__ void __launch_bounds__(EX_THREADS) k_route_exact(const uint16_t *__restrict__ x, const float *__restrict__ W,
-                                                            const float *__restrict__ bias, int32_t *__restrict__ ids,
-                                                            float *__restrict__ wts, const uint32_t *__restrict__ flag_list,
-                                                            const uint32_t *__restrict__ flag_count, RouteParams p) {
-    // EX_TB flagged tokens per block share each 32-column tile of the router; thread e folds
-    // expert e for all of them (independent chains)
-    __shared__ float wtile[EX_MAXE][33];
-    __shared__ double xtile[EX_TB][32];
-    __shared__ double lgs[EX_TB][EX_MAXE], scs[EX_TB][EX_MAXE], tmps[EX_TB][EX_MAXE];
-    const uint32_t nflag = *flag_count;
-    for (uint32_t f0 = blockIdx.x * EX_TB; f0 < nflag; f0 += gridDim.x * EX_TB) {
-        const int nt = (int)min((uint32_t)EX_TB, nflag - f0);
-        // logits: right fold over j descending, acc = w*x + acc in fp64 (transformer-block.fk:25-26)
-        double acc[EX_TB];
-        for (int q = 0; q < EX_TB; ++q) acc[q] = 0.0;
-        const int e = threadIdx.x;
-        for (int j0 = (int)p.hidden - 32; j0 >= 0; j0 -= 32) {
-            __syncthreads();
-            for (int i = threadIdx.x; i < (int)p.ne * 32; i += EX_THREADS) {
-                const int ee = i >> 5, j = i & 31;
-                wtile[ee][j] = W[(size_t)ee * p.hidden + j0 + j];
-            }
-            for (int i = threadIdx.x; i < EX_TB * 32; i += EX_THREADS) {
-                const int q = i >> 5, j = i & 31;
-                const uint32_t t = flag_list[f0 + min(q, nt - 1)];
-                xtile[q][j] = (double)bf16_bits_to_float(x[(size_t)t * p.hidden + j0 + j]);
-            }
-            __syncthreads();
-            if (e < (int)p.ne) {
-#pragma unroll
-                for (int q = 0; q < EX_TB; ++q) {
-                    double a = acc[q];
-                    for (int j = 31; j >= 0; --j) a = __dadd_rn(__dmul_rn((double)wtile[e][j], xtile[q][j]), a);
-                    acc[q] = a;
-                }
-            }
-        }
-        if (e < (int)p.ne)
-            for (int q = 0; q < EX_TB; ++q) lgs[q][e] = acc[q];
-        __syncthreads();
-        if (threadIdx.x < nt) {
-            const uint32_t t = flag_list[f0 + threadIdx.x];
-            double *lg = lgs[threadIdx.x], *sc = scs[threadIdx.x], *tmp = tmps[threadIdx.x];
-            const int ne = (int)p.ne, k = (int)p.nsel;
-            int sel[16];
-            double w[16];
-            if (p.mode == 4) {
-                for (int e = 0; e < ne; ++e) {
-                    lg[e] = ref_sigmoid(lg[e]);  // probs
-                    sc[e] = __dadd_rn(lg[e], (double)bias[e]);
-                }
-                const int ng = (int)p.ngroups, gs = ne / ng;
-                double gsc[64];
-                for (int g = 0; g < ng; ++g) {
-                    int two[2];
-                    for (int i = 0; i < gs; ++i) tmp[i] = sc[g * gs + i];
-                    ref_topk(tmp, gs, 2, two);
-                    gsc[g] = __dadd_rn(__dadd_rn(0.0, sc[g * gs + two[0]]), sc[g * gs + two[1]]);
-                }
-                int gsel[64];
-                ref_topk(gsc, ng, (int)p.topk_groups, gsel);
-                unsigned long long gon = 0;
-                for (int i = 0; i < (int)p.topk_groups; ++i) gon |= 1ull << gsel[i];
-                for (int e = 0; e < ne; ++e) tmp[e] = (gon >> (e / gs) & 1) ? sc[e] : -1000000000.0;
-                ref_topk(tmp, ne, k, sel);
-                double s0 = 0.0;
-                for (int i = 0; i < k; ++i) s0 = __dadd_rn(s0, lg[sel[i]]);
-                const double s = s0 < 0.00006103515625 ? 0.00006103515625 : s0;
-                const double scl = __ddiv_rn((double)p.wscale, s);
-                for (int i = 0; i < k; ++i) w[i] = __dmul_rn(lg[sel[i]], scl);
-            } else {
-                // mm-softmax / mm-topk / mm-gather (moe-msl.fk:73-99), no renormalization
-                double mx = lg[0];
-                for (int e = 1; e < ne; ++e)
-                    if (lg[e] > mx) mx = lg[e];
-                double s = 0.0;
-                for (int e = 0; e < ne; ++e) {
-                    tmp[e] = ref_exp(__dsub_rn(lg[e], mx));
-                    s = __dadd_rn(s, tmp[e]);
-                }
-                const double inv = __ddiv_rn(1.0, s);
-                for (int e = 0; e < ne; ++e) tmp[e] = __dmul_rn(tmp[e], inv);
-                unsigned char taken[EX_MAXE];
-                for (int e = 0; e < ne; ++e) taken[e] = 0;
-                for (int r = 0; r < k; ++r) {
-                    int best = -1;
-                    double bv = 0.0;
-                    for (int e = 0; e < ne; ++e)
-                        if (!taken[e] && (best == -1 || tmp[e] > bv)) { best = e; bv = tmp[e]; }
-                    taken[best] = 1;
-                    sel[r] = best;
-                    w[r] = bv;
-                }
-            }
-            for (int i = 0; i < k; ++i) {
-                ids[(size_t)t * k + i] = sel[i];
-                wts[(size_t)t * k + i] = (float)w[i];
-            }
-        }
     }
 }
 
@@ -508,15 +374,6 @@ int launch_route_select(const float *L, const float *bias, int32_t *ids, float *
     if (p.mode == 4 && !bias) return CK_ERR_ARG;
     cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
     if (p.ntok) k_route_select<<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, bias, ids, wts, flag_list, flag_count, p);
-    return (int)cudaGetLastError();
-}
-int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int32_t *ids, float *wts,
-                       const uint32_t *flag_list, const uint32_t *flag_count, const RouteParams &p, cudaStream_t s) {
-    if (p.ne > EX_MAXE || p.hidden % 32 != 0) return CK_ERR_SHAPE;
-    int dev = 0, nsm = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    k_route_exact<<<nsm * 2, EX_THREADS, 0, s>>>(x, w, bias, ids, wts, flag_list, flag_count, p);
     return (int)cudaGetLastError();
 }
 int launch_route_softmax_tokens(const float *L, uint32_t *ids, float *wts, uint32_t ne, uint32_t nsel, uint32_t ntok,

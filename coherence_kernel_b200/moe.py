@@ -33,7 +33,7 @@ class MoeSpec:
     ngroups: int = 1
     topk_groups: int = 1
     wscale: float = 1.0
-    tau: float = 1e-4    # decision margin below which a token is re-routed in fp64
+    tau: float = 5e-5    # decision margin below which a token is re-routed in fp64
 
     def cfg(self) -> _lib.MoeConfig:
         return _lib.MoeConfig(self.hidden, self.inter, self.n_experts, self.n_shared, self.nsel, self.mode,
@@ -174,6 +174,23 @@ def _align(n, a=256):
     return (n + a - 1) // a * a
 
 
+def ep_split_sizes(counts, recv_counts_e, world):
+    """Row counts of the dispatch all-to-all.  `counts` [E] is this rank's rows per (global) expert,
+    sorted by expert and therefore by destination rank (rank r owns experts r*E/W ..); after the
+    counts all-to-all, `recv_counts_e` [W * E/W] is, per source rank, its rows per local expert.
+    Returns (send sizes per destination, receive sizes per source) as Python lists."""
+    send = counts.view(world, -1).sum(dim=1)
+    recv = recv_counts_e.view(world, -1).sum(dim=1)
+    return send.tolist(), recv.tolist()
+
+
+def ep_recv_local_experts(recv_counts_e, world, nrecv):
+    """The local expert of every received row: each source's block arrives sorted by expert."""
+    el = recv_counts_e.numel() // world
+    eidx = torch.arange(el, device=recv_counts_e.device, dtype=torch.int32).repeat(world)
+    return torch.repeat_interleave(eidx, recv_counts_e.to(torch.int64), output_size=nrecv)
+
+
 class ExpertParallelMoE:
     """The MoE layer with experts sharded over the ranks of a process group (one GPU per rank).
 
@@ -283,14 +300,9 @@ class ExpertParallelMoE:
                                                  1, _ptr(hs), T, _ptr(ys), T, None, _ptr(self.sh_tiles),
                                                  _ptr(self.sh_ntiles), self.sh_tiles.shape[0], H, I, 0, _ptr(self.err),
                                                  st), "shared down")
-        # rows per destination rank: experts are contiguous per rank, and so are their rows in xp
-        cnt_rank = self.counts.view(self.world, self.el)
-        send_counts = cnt_rank.sum(dim=1)
         recv_counts_e = torch.empty_like(self.counts)
         dist.all_to_all_single(recv_counts_e, self.counts, group=self.group)  # [src, local expert]
-        recv_counts = recv_counts_e.view(self.world, self.el).sum(dim=1)
-        sc = send_counts.tolist()
-        rc = recv_counts.tolist()
+        sc, rc = ep_split_sizes(self.counts, recv_counts_e, self.world)
         nrecv = int(sum(rc))
         self.last_recv_rows = nrecv
         dist.all_to_all_single(self.recv_x[:nrecv], self.xp[:A], output_split_sizes=rc, input_split_sizes=sc,
@@ -300,10 +312,7 @@ class ExpertParallelMoE:
                                    group=self.group)
         else:
             self.recv_w[:nrecv].fill_(1.0)
-        # the local expert of every received row: each source's block is sorted by expert
-        rce = recv_counts_e.view(self.world, self.el).reshape(-1)
-        eidx = torch.arange(self.el, device=dev, dtype=torch.int32).repeat(self.world)
-        self.recv_e[:nrecv] = torch.repeat_interleave(eidx, rce.to(torch.int64), output_size=nrecv)
+        self.recv_e[:nrecv] = ep_recv_local_experts(recv_counts_e, self.world, nrecv)
         # regroup by local expert (a stable counting sort), grouped GEMMs, restore arrival order
         if nrecv:
             _lib.check(L.ck_moe_permute(_ptr(self.recv_e), _ptr(self.recv_w), _ptr(self.recv_x), nrecv, 1, self.el, 0,

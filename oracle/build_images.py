@@ -1,7 +1,10 @@
-"""Compile the Form driver cells (oracle/fk/*.fk, tests/fk/*.fk) into self-contained fkwu program
-images (.fkb + .sym) under oracle/_ref/fk/, using the reference runtime (oracle/_ref/fkwu) over a
-temporary writable copy of the reference's Form stdlib.  The images run without the reference tree,
-so they travel with the repository to a machine that has none.  Test infrastructure only.
+"""Compile the Form driver cells into self-contained fkwu program images (.fkb + .sym) over a
+temporary writable copy of the reference's Form stdlib.  An image only loads in the binary that
+wrote it, so the oracle's cells (oracle/fk/*.fk) are compiled by the reference runtime
+(oracle/_ref/fkwu) into oracle/_ref/fk/, and the door cells (tests/fk/*.fk) by the same runtime
+linked with the CUDA carrier (oracle/_ref/fkwu-cuda) into oracle/_ref/fk-cuda/.  The images run
+without the reference tree, so they travel with the repository to a machine that has none.  Test
+infrastructure only.
 
     python oracle/build_images.py [--ref /root/reference]
 """
@@ -17,11 +20,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 
 
-def build(ref: str) -> list:
-    fkwu = os.path.join(HERE, "_ref", "fkwu")
-    if not os.path.exists(fkwu):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
-    out_dir = os.path.join(HERE, "_ref", "fk")
+PRELUDES = ("ck_io.fk", "ck_group_route.fk")  # prelude cells, not programs
+
+
+def _compile(binary: str, cells: list, out_dir: str, ref: str) -> list:
     os.makedirs(out_dir, exist_ok=True)
     tmp = tempfile.mkdtemp(prefix="ck_images_")
     built = []
@@ -30,16 +32,13 @@ def build(ref: str) -> list:
         shutil.copytree(os.path.join(ref, "form", "form-stdlib"), os.path.join(form, "form-stdlib"))
         os.makedirs(os.path.join(form, "ck"))
         os.makedirs(os.path.join(form, "ck_in"))
-        cells = []
-        for d in (os.path.join(HERE, "fk"), os.path.join(REPO, "tests", "fk")):
-            for f in sorted(os.listdir(d)):
-                if f.endswith(".fk"):
-                    shutil.copy(os.path.join(d, f), os.path.join(form, "ck", f))
-                    cells.append(f)
-        for f in cells:
-            if f in ("ck_io.fk", "ck_group_route.fk"):
-                continue  # preludes, not programs
-            p = subprocess.run([fkwu, f"ck/{f}"], cwd=form, capture_output=True, text=True, timeout=600)
+        for f in PRELUDES:
+            shutil.copy(os.path.join(HERE, "fk", f), os.path.join(form, "ck", f))
+        for path in cells:
+            shutil.copy(path, os.path.join(form, "ck", os.path.basename(path)))
+        for path in cells:
+            f = os.path.basename(path)
+            p = subprocess.run([binary, f"ck/{f}"], cwd=form, capture_output=True, text=True, timeout=600)
             if " error(s)" in p.stderr and "0 error(s)" not in p.stderr:
                 raise RuntimeError(f"{f} does not compile cleanly:\n{p.stderr[-3000:]}")
             stem = f[:-3]
@@ -48,6 +47,21 @@ def build(ref: str) -> list:
             built.append(stem)
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
+    return built
+
+
+def build(ref: str) -> list:
+    fkwu = os.path.join(HERE, "_ref", "fkwu")
+    if not os.path.exists(fkwu):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
+    oracle_cells = [os.path.join(HERE, "fk", f) for f in sorted(os.listdir(os.path.join(HERE, "fk")))
+                    if f.endswith(".fk") and f not in PRELUDES]
+    built = _compile(fkwu, oracle_cells, os.path.join(HERE, "_ref", "fk"), ref)
+    fkwu_cuda = os.path.join(HERE, "_ref", "fkwu-cuda")
+    if os.path.exists(fkwu_cuda):
+        door = os.path.join(REPO, "tests", "fk")
+        door_cells = [os.path.join(door, f) for f in sorted(os.listdir(door)) if f.endswith(".fk")]
+        built += [c + " (cuda)" for c in _compile(fkwu_cuda, door_cells, os.path.join(HERE, "_ref", "fk-cuda"), ref)]
     return built
 
 

@@ -18,7 +18,7 @@ from coherence_kernel_b200 import synth
 pytestmark = pytest.mark.gpu
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 FKWU_CUDA = os.path.join(REPO, "oracle", "_ref", "fkwu-cuda")
-IMAGE = os.path.join(REPO, "oracle", "_ref", "fk", "ck_door_q4k.fkb")
+IMAGE = os.path.join(REPO, "oracle", "_ref", "fk-cuda", "ck_door_q4k.fkb")
 
 
 @pytest.mark.skipif(not (os.path.exists(FKWU_CUDA) and os.path.exists(IMAGE)),
