@@ -298,14 +298,15 @@ int ck_moe_permute(const int32_t *ids, const float *wts, const void *x, uint32_t
 }
 
 int ck_moe_expert_gemm(int dual, const void *w0, const void *w1, const void *s0, const void *s1, uint64_t w_stride,
-                       uint32_t n_routed, const void *x, uint32_t x_rows, void *out, uint32_t out_rows,
-                       const float *row_w, const void *tiles, const int32_t *ntiles, uint32_t max_tiles, uint32_t n,
-                       uint32_t k, int xrow_is_orow, int *err, void *s) {
+                       uint32_t n_routed, uint32_t n_shared, const void *x, uint32_t x_rows, void *out,
+                       uint32_t out_rows, const float *row_w, const void *tiles, const int32_t *ntiles,
+                       uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow, int *err, void *s) {
     ck::GemmParams p = {};
     p.w0 = (const uint8_t *)w0;
     p.w1 = (const uint8_t *)w1;
     p.s0 = (const uint8_t *)s0;
     p.s1 = (const uint8_t *)s1;
+    p.n_shared = s0 ? n_shared : 0;
     p.w_stride = w_stride;
     p.x = x;
     p.x_rows = x_rows;
@@ -362,11 +363,11 @@ int ck_moe_layer_bf16(const ck_moe_config *c, const void *x, uint32_t ntok, cons
     if (rc) return rc;
     const uint32_t mt = ck_moe_max_tiles(ntok, c->nsel, c->n_experts, c->n_shared);
     const uint64_t stride = (uint64_t)c->inter * c->hidden / 256 * 144;
-    rc = ck_moe_expert_gemm(1, wg, wu, sg, su, stride, c->n_experts, w.xp, A + ntok, w.h, R, w.row_w, w.tiles, w.ntiles,
-                            mt, c->inter, c->hidden, 0, w.err, s);
+    rc = ck_moe_expert_gemm(1, wg, wu, sg, su, stride, c->n_experts, c->n_shared, w.xp, A + ntok, w.h, R, w.row_w,
+                            w.tiles, w.ntiles, mt, c->inter, c->hidden, 0, w.err, s);
     if (rc) return rc;
-    rc = ck_moe_expert_gemm(0, wd, nullptr, sd, nullptr, stride, c->n_experts, w.h, R, w.y, R, nullptr, w.tiles,
-                            w.ntiles, mt, c->hidden, c->inter, 1, w.err, s);
+    rc = ck_moe_expert_gemm(0, wd, nullptr, sd, nullptr, stride, c->n_experts, c->n_shared, w.h, R, w.y, R, nullptr,
+                            w.tiles, w.ntiles, mt, c->hidden, c->inter, 1, w.err, s);
     if (rc) return rc;
     return ck_moe_combine(w.y, ids, wts, w.pair_pos, ntok, c->nsel, c->n_shared, c->hidden, c->mode == 3, out, nullptr,
                           s);

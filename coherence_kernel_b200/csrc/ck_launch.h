@@ -77,6 +77,7 @@ struct GemmParams {
     const int32_t *ntiles;   // device-side tile count
     uint32_t max_tiles;
     uint32_t n_routed;       // groups >= n_routed use the shared weights
+    uint32_t n_shared;       // how many shared matrices s0/s1 hold
     uint32_t N, K;           // output features (weight rows), reduction length
     int dual;                // 1: out = silu(x.W0) * (x.W1) * row_w ; 0: out = x.W0
     int xrow_is_orow;        // 1: read X at the tile's output row (the down projection over H)

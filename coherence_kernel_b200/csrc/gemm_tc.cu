@@ -10,18 +10,26 @@
 // A third form, dense = 1, reads a bf16 A operand through TMA instead of dequantizing and writes
 // fp32: the router logits, with the fp32 router split into three bf16 terms along K.
 //
-// One persistent CTA per SM, warp-specialised:
-//   warp 0      TMA producer: the token tile (BN x 64 bf16, 128-byte swizzle) per K step
-//   warp 1      TMEM allocator and the single MMA-issuing thread (tcgen05.mma kind::f16, M=128)
-//   warps 2-9   dequant producers: two threads per weight row of the 128-row tile; each loads the
-//               packed superblock fields with 16-byte loads (one stage ahead), unpacks nibbles and
-//               6-bit scales in registers and writes bf16 into the swizzled shared-memory A tile
-//   warps 10-13 epilogue: tcgen05.ld the fp32 accumulators, SwiGLU + route weight, stores
+// One persistent CTA per SM, warp-specialised, three shared-memory rings:
+//   P ring  packed Q4_K bytes of the 128-row weight tile per K step -- each row's superblock
+//           header (16 B) and the 32 qs bytes of its 64-weight chunk -- brought in by TMA (3D maps
+//           over [expert, row, byte]) several steps ahead, when every row starts on a superblock
+//           (K % 256 == 0); otherwise the dequant threads load the bytes themselves.
+//   A ring  the dequantized bf16 weight tile(s), 128-byte swizzled (the MMA's A operand)
+//   B ring  the bf16 token tile (BN x 64, 128-byte swizzle) by TMA (the MMA's B operand)
+// Warps:
+//   0       TMA producer of the B ring (and of the A operand in the dense form)
+//   1       TMEM allocator and the single MMA-issuing thread (tcgen05.mma kind::f16, M = 128)
+//   2-9     dequant: two threads per weight row; prmt + magic-exponent nibble decode, one exact
+//           bf16x2 subtract and one bf16x2 FMA per weight pair, stores into the A ring
+//   10-13   epilogue: tcgen05.ld of the fp32 accumulators, SwiGLU x route weight, stores
+//   14      TMA producer of the P ring
 // Every wait is bounded (about one second); on a timeout the kernel records a code in *err and
 // every role leaves its loop, waits for its own copies and MMAs, and frees TMEM.
 #include "ck_common.cuh"
 #include "ck_launch.h"
 
+#include <cstring>
 #include <mutex>
 
 namespace ck {
@@ -32,25 +40,36 @@ constexpr int BK = 64;
 constexpr int BN = 256;
 constexpr int NDQ = 8;   // dequant warps (two threads per weight row)
 constexpr int NEPI = 4;  // epilogue warps
-constexpr int NTHREADS = (2 + NDQ + NEPI) * 32;
+constexpr int NTHREADS = (2 + NDQ + NEPI + 1) * 32;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
+constexpr int P_HDR = BM * 16;  // superblock headers of the tile's rows
+constexpr int P_QS = BM * 32;   // the qs bytes of the K step's chunk
+constexpr int W_EPI0 = 2 + NDQ, W_PTMA = 2 + NDQ + NEPI;
 
-template <int DUAL>
+template <int DUAL, int DENSE, int PT>
 struct Cfg {
     static constexpr int NMAT = DUAL ? 2 : 1;
-    static constexpr int STAGE_BYTES = NMAT * A_BYTES + B_BYTES;
-    static constexpr int STAGES = DUAL ? 3 : 4;
-    static constexpr int ACC_COLS = NMAT * BN;
-    static constexpr int ACC_BUFS = 512 / ACC_COLS;
     // the dense form splits its K loop over DENSE_ACC accumulators of DENSE_TILE columns (token
     // tiles of at most DENSE_TILE) and sums them in fp32 in the epilogue: each tensor-core
     // accumulation chain is an eighth as long, and so is its rounding error
     static constexpr int DENSE_ACC = 8;
     static constexpr int DENSE_TILE = 64;
     static constexpr int DENSE_B_BYTES = DENSE_TILE * BK * 2;
-    static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+    static constexpr int A_ST = DENSE ? 0 : (DUAL ? 2 : 3);
+    static constexpr int A_STAGE = NMAT * A_BYTES;
+    static constexpr int B_ST = DENSE ? 6 : (DUAL ? 3 : 4);
+    static constexpr int B_STAGE = DENSE ? A_BYTES + DENSE_B_BYTES : B_BYTES;
+    static constexpr int P_ST = (DENSE || !PT) ? 0 : (DUAL ? 4 : 6);
+    static constexpr int P_STAGE = NMAT * (P_HDR + P_QS);
+    static constexpr int A_OFF = 0;
+    static constexpr int B_OFF = A_ST * A_STAGE;
+    static constexpr int P_OFF = B_OFF + B_ST * B_STAGE;
+    static constexpr int BAR_OFF = P_OFF + P_ST * P_STAGE;
+    static constexpr int ACC_COLS = DENSE ? 512 : NMAT * BN;
+    static constexpr int NBUF = 512 / ACC_COLS;
+    static constexpr int SMEM = BAR_OFF + 512 + 1024;
+    static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct Tile {
@@ -112,22 +131,35 @@ CK_DEV void dequant_half(const Packed &p, uint8_t *a, int r, int half) {
     }
 }
 
-template <int DUAL, int DENSE>
-__global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap tmap_x,
-                                                          const __grid_constant__ CUtensorMap tmap_a, GemmParams p) {
-    using C = Cfg<DUAL>;
+CK_DEV void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// the eight packed-weight maps: header and qs boxes of w0, w1 (routed) and s0, s1 (shared)
+struct PMaps {
+    CUtensorMap hdr[4];
+    CUtensorMap qs[4];
+};
+
+template <int DUAL, int DENSE, int PT>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_gemm_q4k(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_a,
+               const __grid_constant__ PMaps pm, GemmParams p) {
+    using C = Cfg<DUAL, DENSE, PT>;
     static_assert(!(DUAL && DENSE), "the dense form has one accumulator");
-    constexpr int NBUF = DENSE ? 1 : C::ACC_BUFS;  // accumulator buffers in flight
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
-    uint64_t *full_a = bars;
-    uint64_t *full_b = bars + C::STAGES;
-    uint64_t *empty = bars + 2 * C::STAGES;
-    uint64_t *acc_full = bars + 3 * C::STAGES;
-    uint64_t *acc_empty = acc_full + C::ACC_BUFS;
-    uint64_t *done_bar = acc_empty + C::ACC_BUFS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done_bar + 1);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *p_full = bars, *p_empty = bars + 8;
+    uint64_t *a_full = bars + 16, *a_empty = bars + 20;
+    uint64_t *b_full = bars + 24, *b_empty = bars + 32;
+    uint64_t *acc_full = bars + 40, *acc_empty = bars + 42;
+    uint64_t *done_bar = bars + 44;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 45);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = min(*p.ntiles, (int)p.max_tiles);
@@ -138,12 +170,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
     const int nkx = DENSE && p.kx ? (int)(p.kx / BK) : nk;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full_a[s], NDQ * 32);
-            mbar_init(&full_b[s], 1);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < 8; ++s) {
+            mbar_init(&p_full[s], 1);
+            mbar_init(&p_empty[s], NDQ * 32);
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
         }
-        for (int b = 0; b < C::ACC_BUFS; ++b) {
+        for (int s = 0; s < 4; ++s) {
+            mbar_init(&a_full[s], NDQ * 32);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], NEPI * 32);
         }
@@ -162,27 +199,64 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ B ring producer (TMA)
         if (lane == 0) {
             int it = 0;
-            for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+            bool ok = true;
+            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
                 const Tile t = load_tile(p.tiles, u / nrt);
-                bool ok = true;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % C::STAGES;
-                    const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-                    if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, 1)) { ok = false; break; }
-                    uint8_t *b_tile = smem + s * C::STAGE_BYTES + C::NMAT * A_BYTES;
-                    mbar_arrive_expect_tx(&full_b[s], DENSE ? C::DENSE_B_BYTES + A_BYTES : B_BYTES);
-                    tma_load_2d(b_tile, &tmap_x, &full_b[s], (kb % nkx) * BK, p.xrow_is_orow ? t.orow : t.xrow);
-                    if (DENSE) tma_load_2d(smem + s * C::STAGE_BYTES, &tmap_a, &full_b[s], kb * BK, (u % nrt) * BM);
+                    const int s = it % C::B_ST;
+                    const uint32_t ph = (uint32_t)(it / C::B_ST) & 1u;
+                    if (!mbar_wait_bounded(&b_empty[s], ph ^ 1u, p.err, 1)) { ok = false; break; }
+                    uint8_t *st = smem + C::B_OFF + s * C::B_STAGE;
+                    if (DENSE) {
+                        mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
+                        tma_load_2d(st, &tmap_a, &b_full[s], kb * BK, (u % nrt) * BM);
+                        tma_load_2d(st + A_BYTES, &tmap_x, &b_full[s], (kb % nkx) * BK, t.xrow);
+                    } else {
+                        mbar_arrive_expect_tx(&b_full[s], B_BYTES);
+                        tma_load_2d(st, &tmap_x, &b_full[s], kb * BK, p.xrow_is_orow ? t.orow : t.xrow);
+                    }
                 }
-                if (!ok) break;
             }
             // drain: the copies this thread issued must land before the CTA can exit
-            for (int d = 0; d < C::STAGES && it - 1 - d >= 0; ++d) {
+            for (int d = 0; d < C::B_ST && it - 1 - d >= 0; ++d) {
                 const int j = it - 1 - d;
-                mbar_wait_bounded(&full_b[j % C::STAGES], (uint32_t)(j / C::STAGES) & 1u, nullptr, 0);
+                mbar_wait_bounded(&b_full[j % C::B_ST], (uint32_t)(j / C::B_ST) & 1u, nullptr, 0);
+            }
+        }
+    } else if (warp == W_PTMA) {
+        // ------------------------------------------------------------ P ring producer (TMA)
+        if (PT && !DENSE && lane == 0) {
+            int it = 0;
+            bool ok = true;
+            const uint32_t row_bytes = p.K / 256 * Q4K_BYTES;
+            (void)row_bytes;
+            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+                const Tile t = load_tile(p.tiles, u / nrt);
+                const int n0 = (u % nrt) * BM;
+                const bool shared = (uint32_t)t.g >= p.n_routed;
+                const int gg = shared ? t.g - (int)p.n_routed : t.g;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % C::P_ST;
+                    const uint32_t ph = (uint32_t)(it / C::P_ST) & 1u;
+                    if (!mbar_wait_bounded(&p_empty[s], ph ^ 1u, p.err, 7)) { ok = false; break; }
+                    uint8_t *st = smem + C::P_OFF + s * C::P_STAGE;
+                    mbar_arrive_expect_tx(&p_full[s], C::P_STAGE);
+                    const int sb = kb >> 2, c = kb & 3;
+#pragma unroll
+                    for (int m = 0; m < C::NMAT; ++m) {
+                        const int mi = (shared ? 2 : 0) + m;
+                        tma_load_3d(st + m * (P_HDR + P_QS), &pm.hdr[mi], &p_full[s], sb * Q4K_BYTES, n0, gg);
+                        tma_load_3d(st + m * (P_HDR + P_QS) + P_HDR, &pm.qs[mi], &p_full[s], sb * Q4K_BYTES + 16 + 32 * c,
+                                    n0, gg);
+                    }
+                }
+            }
+            for (int d = 0; d < C::P_ST && it - 1 - d >= 0; ++d) {
+                const int j = it - 1 - d;
+                mbar_wait_bounded(&p_full[j % C::P_ST], (uint32_t)(j / C::P_ST) & 1u, nullptr, 0);
             }
         }
     } else if (warp == 1) {
@@ -190,30 +264,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
         if (lane == 0) {
             int it = 0, ut = 0;
             bool ok = true;
+            const int chunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++ut) {
                 const Tile t = load_tile(p.tiles, u / nrt);
                 int nmma = ((t.ntok + 15) / 16) * 16;
                 const int nmax = DENSE ? C::DENSE_TILE : BN;
                 nmma = nmma < 16 ? 16 : (nmma > nmax ? nmax : nmma);
                 const uint32_t idesc = idesc_bf16(BM, nmma);
-                const int ab = ut % NBUF;
-                const uint32_t aph = (uint32_t)(ut / NBUF) & 1u;
+                const int ab = ut % C::NBUF;
+                const uint32_t aph = (uint32_t)(ut / C::NBUF) & 1u;
                 if (!mbar_wait_bounded(&acc_empty[ab], aph ^ 1u, p.err, 2)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
-                const int chunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % C::STAGES;
-                    const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-                    if ((!DENSE && !mbar_wait_bounded(&full_a[s], ph, p.err, 3)) ||
-                        !mbar_wait_bounded(&full_b[s], ph, p.err, 4)) {
+                    const int sb = it % C::B_ST;
+                    const uint32_t phb = (uint32_t)(it / C::B_ST) & 1u;
+                    const int sa = DENSE ? 0 : it % C::A_ST;
+                    const uint32_t pha = DENSE ? 0u : (uint32_t)(it / C::A_ST) & 1u;
+                    if ((!DENSE && !mbar_wait_bounded(&a_full[sa], pha, p.err, 3)) ||
+                        !mbar_wait_bounded(&b_full[sb], phb, p.err, 4)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
-                    const uint32_t b0 = smem_u32(smem + s * C::STAGE_BYTES + C::NMAT * A_BYTES);
-                    // dense form: K chunk kb / chunk accumulates into its own 128-column accumulator
+                    const uint32_t bst = smem_u32(smem + C::B_OFF + sb * C::B_STAGE);
+                    const uint32_t a0 = DENSE ? bst : smem_u32(smem + C::A_OFF + sa * C::A_STAGE);
+                    const uint32_t b0 = DENSE ? bst + A_BYTES : bst;
+                    // dense form: K chunk kb / chunk accumulates into its own accumulator
                     const uint32_t dd = DENSE ? d0 + (uint32_t)((kb / chunk) * C::DENSE_TILE) : d0;
                     const int kfirst = DENSE ? kb % chunk : kb;
 #pragma unroll
@@ -223,7 +300,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                         umma_bf16(dd, sdesc_k_sw128(a0 + k * 32), bd, idesc, acc);
                         if (DUAL) umma_bf16(d0 + BN, sdesc_k_sw128(a0 + A_BYTES + k * 32), bd, idesc, acc);
                     }
-                    umma_commit(&empty[s]);
+                    if (!DENSE) umma_commit(&a_empty[sa]);
+                    umma_commit(&b_empty[sb]);
                 }
                 if (!ok) break;
                 umma_commit(&acc_full[ab]);
@@ -232,59 +310,89 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
             umma_commit(done_bar);
             mbar_wait_bounded(done_bar, 0, nullptr, 0);
         }
-    } else if (warp < 2 + NDQ && !DENSE) {  // in the dense form the A operand arrives by TMA
+    } else if (warp < W_EPI0 && !DENSE) {
         // ------------------------------------------------------------ dequant producers
         // 256 threads: thread i owns row (i & 127) of the tile; part = i >> 7 selects the matrix
         // (dual: gate or up, both halves of the 64-weight chunk) or the nibble half (single).
         const int di = threadIdx.x - 64;
         const int r = di & (BM - 1);
         const int part = di >> 7;
+        const int mat = DUAL ? part : 0;
         int it = 0;
-        // software pipeline: the packed fields of step it+1 are in flight while step it is unpacked
-        Packed cur, nxt;
-        int u = blockIdx.x, kb = 0;
-        auto base_of = [&](int uu, uint64_t &rowflat) -> const uint8_t * {
-            const Tile t = load_tile(p.tiles, uu / nrt);
-            const int n0 = (uu % nrt) * BM;
-            const uint32_t row = min((uint32_t)(n0 + r), p.N - 1);
-            const bool shared = (uint32_t)t.g >= p.n_routed;
-            const uint64_t g = shared ? (uint64_t)(t.g - p.n_routed) : (uint64_t)t.g;
-            const uint8_t *b = (DUAL && part) ? (shared ? p.s1 : p.w1) : (shared ? p.s0 : p.w0);
-            rowflat = (uint64_t)row * p.K;
-            return b + g * p.w_stride;
-        };
-        const uint8_t *b = nullptr;
-        uint64_t rowflat = 0;
-        if (u < nunits) {
-            b = base_of(u, rowflat);
-            load_packed(nxt, b, rowflat);
-        }
-        while (u < nunits) {
-            cur = nxt;
-            // advance to the next (unit, k step) and issue its loads
-            int nu = u, nkb = kb + 1;
-            if (nkb == nk) { nkb = 0; nu = u + gridDim.x; }
-            if (nu < nunits) {
-                if (nu != u) b = base_of(nu, rowflat);
-                load_packed(nxt, b, rowflat + (uint64_t)nkb * BK);
+        if (PT) {
+            bool ok = true;
+            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int sp = it % C::P_ST, sa = it % C::A_ST;
+                    const uint32_t php = (uint32_t)(it / C::P_ST) & 1u, pha = (uint32_t)(it / C::A_ST) & 1u;
+                    if (!mbar_wait_bounded(&p_full[sp], php, p.err, 8) || !mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t *ps = smem + C::P_OFF + sp * C::P_STAGE + mat * (P_HDR + P_QS);
+                    Packed pk;
+                    pk.hdr = *reinterpret_cast<const uint4 *>(ps + r * 16);
+                    pk.q0 = *reinterpret_cast<const uint4 *>(ps + P_HDR + r * 32);
+                    pk.q1 = *reinterpret_cast<const uint4 *>(ps + P_HDR + r * 32 + 16);
+                    pk.c = kb & 3;
+                    mbar_arrive(&p_empty[sp]);  // the packed bytes are in registers now
+                    uint8_t *a = smem + C::A_OFF + sa * C::A_STAGE;
+                    if (DUAL) {
+                        dequant_half(pk, a + mat * A_BYTES, r, 0);
+                        dequant_half(pk, a + mat * A_BYTES, r, 1);
+                    } else {
+                        dequant_half(pk, a, r, part);
+                    }
+                    fence_proxy_async_smem();
+                    mbar_arrive(&a_full[sa]);
+                }
             }
-            const int s = it % C::STAGES;
-            const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-            if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, 5)) break;
-            uint8_t *a = smem + s * C::STAGE_BYTES;
-            if (DUAL) {
-                dequant_half(cur, a + part * A_BYTES, r, 0);
-                dequant_half(cur, a + part * A_BYTES, r, 1);
-            } else {
-                dequant_half(cur, a, r, part);
+        } else {
+            // rows that straddle superblocks: each thread loads its packed fields, one step ahead
+            Packed cur, nxt;
+            int u = blockIdx.x, kb = 0;
+            auto base_of = [&](int uu, uint64_t &rowflat) -> const uint8_t * {
+                const Tile t = load_tile(p.tiles, uu / nrt);
+                const int n0 = (uu % nrt) * BM;
+                const uint32_t row = min((uint32_t)(n0 + r), p.N - 1);
+                const bool shared = (uint32_t)t.g >= p.n_routed;
+                const uint64_t g = shared ? (uint64_t)(t.g - p.n_routed) : (uint64_t)t.g;
+                const uint8_t *b = (DUAL && part) ? (shared ? p.s1 : p.w1) : (shared ? p.s0 : p.w0);
+                rowflat = (uint64_t)row * p.K;
+                return b + g * p.w_stride;
+            };
+            const uint8_t *b = nullptr;
+            uint64_t rowflat = 0;
+            if (u < nunits) {
+                b = base_of(u, rowflat);
+                load_packed(nxt, b, rowflat);
             }
-            fence_proxy_async_smem();
-            mbar_arrive(&full_a[s]);
-            ++it;
-            u = nu;
-            kb = nkb;
+            while (u < nunits) {
+                cur = nxt;
+                int nu = u, nkb = kb + 1;
+                if (nkb == nk) { nkb = 0; nu = u + gridDim.x; }
+                if (nu < nunits) {
+                    if (nu != u) b = base_of(nu, rowflat);
+                    load_packed(nxt, b, rowflat + (uint64_t)nkb * BK);
+                }
+                const int sa = it % C::A_ST;
+                const uint32_t pha = (uint32_t)(it / C::A_ST) & 1u;
+                if (!mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) break;
+                uint8_t *a = smem + C::A_OFF + sa * C::A_STAGE;
+                if (DUAL) {
+                    dequant_half(cur, a + part * A_BYTES, r, 0);
+                    dequant_half(cur, a + part * A_BYTES, r, 1);
+                } else {
+                    dequant_half(cur, a, r, part);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&a_full[sa]);
+                ++it;
+                u = nu;
+                kb = nkb;
+            }
         }
-    } else if (warp >= 2 + NDQ) {
+    } else if (warp >= W_EPI0 && warp < W_PTMA) {
         // ------------------------------------------------------------ epilogue
         const int sp = warp & 3;  // TMEM sub-partition this warp may read
         int ut = 0;
@@ -292,8 +400,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ut) {
             const Tile t = load_tile(p.tiles, u / nrt);
             const int n0 = (u % nrt) * BM;
-            const int ab = ut % NBUF;
-            const uint32_t aph = (uint32_t)(ut / NBUF) & 1u;
+            const int ab = ut % C::NBUF;
+            const uint32_t aph = (uint32_t)(ut / C::NBUF) & 1u;
             if (!mbar_wait_bounded(&acc_full[ab], aph, p.err, 6)) break;
             tc_fence_after();
             const uint32_t row = (uint32_t)(n0 + 32 * sp + lane);
@@ -302,6 +410,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
                 uint32_t g[32], v[32];
                 tmem_ld32(tbase + cb * 32, g);
                 if (DUAL) tmem_ld32(tbase + BN + cb * 32, v);
+                // lane j fetches the route weight of token cb*32 + j; shuffled out below
+                const float rw_lane = (DUAL && p.row_w && cb * 32 + lane < t.ntok) ? p.row_w[t.orow + cb * 32 + lane] : 1.0f;
                 tmem_ld_wait();
                 if (DENSE) {
                     // sum the K-chunk accumulators in fp32, in chunk order
@@ -316,11 +426,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_q4k(const __grid_constant_
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int tok = cb * 32 + j;
+                    const float rw = __shfl_sync(0xffffffffu, rw_lane, j);
                     if (tok < t.ntok && row < p.N) {
                         float val = __uint_as_float(g[j]);
                         if (DUAL) {
                             const float up = __uint_as_float(v[j]);
-                            const float rw = p.row_w ? p.row_w[t.orow + tok] : 1.0f;
                             val = (val / (1.0f + __expf(-val))) * up * rw;
                         }
                         if (DENSE)
@@ -375,13 +485,30 @@ static int make_map(CUtensorMap *m, const void *x, uint32_t rows, uint32_t K, ui
     return r == CUDA_SUCCESS ? 0 : CK_ERR_ARG;
 }
 
-template <int DUAL, int DENSE>
+// packed Q4_K weights of `count` experts viewed as bytes [count, N, K/256*144]; box = box_bytes x
+// 128 rows x 1 expert, no swizzle (rows land 16 or 32 bytes apart in shared memory).
+static int make_packed_map(CUtensorMap *m, const void *base, uint32_t count, uint32_t N, uint32_t K,
+                           uint32_t box_bytes) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return CK_ERR_NODEV;
+    const cuuint64_t row_bytes = (cuuint64_t)K / 256 * Q4K_BYTES;
+    cuuint64_t dims[3] = {row_bytes, N, count ? count : 1};
+    cuuint64_t strides[2] = {row_bytes, row_bytes * N};
+    cuuint32_t box[3] = {box_bytes, BM, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : CK_ERR_ARG;
+}
+
+template <int DUAL, int DENSE, int PT>
 static int launch_t(const GemmParams &p, cudaStream_t s) {
-    using C = Cfg<DUAL>;
+    using C = Cfg<DUAL, DENSE, PT>;
     static bool attr = false;
     if (!attr) {
         cudaError_t e =
-            cudaFuncSetAttribute(k_gemm_q4k<DUAL, DENSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+            cudaFuncSetAttribute(k_gemm_q4k<DUAL, DENSE, PT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return (int)e;
         attr = true;
     }
@@ -394,13 +521,26 @@ static int launch_t(const GemmParams &p, cudaStream_t s) {
     } else {
         ma = mx;
     }
+    PMaps pm;
+    memset(&pm, 0, sizeof(pm));
+    if (PT) {
+        const uint8_t *bases[4] = {p.w0, DUAL ? p.w1 : p.w0, p.s0 ? p.s0 : p.w0,
+                                   DUAL ? (p.s1 ? p.s1 : p.w1) : (p.s0 ? p.s0 : p.w0)};
+        const uint32_t counts[4] = {p.n_routed, p.n_routed, p.s0 ? p.n_shared : p.n_routed,
+                                    p.s0 ? p.n_shared : p.n_routed};
+        for (int i = 0; i < 4; ++i) {
+            rc = make_packed_map(&pm.hdr[i], bases[i], counts[i], p.N, p.K, 16);
+            if (!rc) rc = make_packed_map(&pm.qs[i], bases[i], counts[i], p.N, p.K, 32);
+            if (rc) return rc;
+        }
+    }
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const long long units = (long long)p.max_tiles * ((p.N + BM - 1) / BM);
     const int grid = (int)(units < nsm ? units : nsm);
     if (grid <= 0) return 0;
-    k_gemm_q4k<DUAL, DENSE><<<grid, NTHREADS, C::SMEM, s>>>(mx, ma, p);
+    k_gemm_q4k<DUAL, DENSE, PT><<<grid, NTHREADS, C::SMEM, s>>>(mx, ma, pm, p);
     return (int)cudaGetLastError();
 }
 }  // namespace gemm
@@ -410,14 +550,20 @@ int launch_gemm_q4k(const GemmParams &p, cudaStream_t s) {
     if (p.K % gemm::BK != 0 || p.N == 0 || p.K == 0 || ((uint64_t)p.N * p.K) % 256 != 0) return CK_ERR_SHAPE;
     if (p.dual && !p.w1) return CK_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.w0) & 15)) return CK_ERR_ARG;
-    return p.dual ? gemm::launch_t<1, 0>(p, s) : gemm::launch_t<0, 0>(p, s);
+    // TMA-staged packed weights when every row starts on a superblock and the tile is full height
+    const bool pt = p.K % 256 == 0 && p.N >= (uint32_t)gemm::BM && !(reinterpret_cast<uintptr_t>(p.w0) & 15) &&
+                    !(p.w1 && (reinterpret_cast<uintptr_t>(p.w1) & 15)) &&
+                    !(p.s0 && (reinterpret_cast<uintptr_t>(p.s0) & 15)) &&
+                    !(p.s1 && (reinterpret_cast<uintptr_t>(p.s1) & 15));
+    if (p.dual) return pt ? gemm::launch_t<1, 0, 1>(p, s) : gemm::launch_t<1, 0, 0>(p, s);
+    return pt ? gemm::launch_t<0, 0, 1>(p, s) : gemm::launch_t<0, 0, 0>(p, s);
 }
 
 int launch_gemm_dense(const GemmParams &p, cudaStream_t s) {
     if (!p.a_dense || !p.x || !p.out_f32 || !p.tiles || !p.ntiles || !p.err) return CK_ERR_ARG;
     if (p.K % gemm::BK != 0 || p.K == 0 || p.N == 0 || (p.kx && (p.kx % gemm::BK || p.K % p.kx))) return CK_ERR_SHAPE;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.a_dense) & 15)) return CK_ERR_ARG;
-    return gemm::launch_t<0, 1>(p, s);
+    return gemm::launch_t<0, 1, 0>(p, s);
 }
 
 }  // namespace ck

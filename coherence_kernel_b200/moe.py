@@ -115,10 +115,11 @@ class MoELayer:
         mark("permute")
         mb = sp.matrix_bytes
         _lib.check(L.ck_moe_expert_gemm(1, _ptr(self.w[0]), _ptr(self.w[1]), _ptr(self.s[0]), _ptr(self.s[1]), mb, E,
-                                         _ptr(w["xp"]), A + T, _ptr(w["h"]), R, _ptr(w["row_w"]), _ptr(w["tiles"]),
+                                         sp.n_shared, _ptr(w["xp"]), A + T, _ptr(w["h"]), R, _ptr(w["row_w"]), _ptr(w["tiles"]),
                                          _ptr(w["ntiles"]), w["mt"], I, H, 0, _ptr(w["err"]), st), "gate/up")
         mark("gate_up")
-        _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, _ptr(self.s[2]), None, mb, E, _ptr(w["h"]), R,
+        _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, _ptr(self.s[2]), None, mb, E, sp.n_shared,
+                                         _ptr(w["h"]), R,
                                          _ptr(w["y"]), R, None, _ptr(w["tiles"]), _ptr(w["ntiles"]), w["mt"], H, I, 1,
                                          _ptr(w["err"]), st), "down")
         mark("down")
@@ -292,12 +293,12 @@ class ExpertParallelMoE:
                 hs = self.h_sh[s * T:(s + 1) * T]
                 ys = self.y[A + s * T:A + (s + 1) * T]
                 _lib.check(L.ck_moe_expert_gemm(1, ctypes.c_void_p(self.s[0].data_ptr() + s * mb),
-                                                 ctypes.c_void_p(self.s[1].data_ptr() + s * mb), None, None, 0, 1,
+                                                 ctypes.c_void_p(self.s[1].data_ptr() + s * mb), None, None, 0, 1, 0,
                                                  _ptr(xs), T, _ptr(hs), T, None, _ptr(self.sh_tiles),
                                                  _ptr(self.sh_ntiles), self.sh_tiles.shape[0], I, H, 0, _ptr(self.err),
                                                  st), "shared gate/up")
                 _lib.check(L.ck_moe_expert_gemm(0, ctypes.c_void_p(self.s[2].data_ptr() + s * mb), None, None, None, 0,
-                                                 1, _ptr(hs), T, _ptr(ys), T, None, _ptr(self.sh_tiles),
+                                                 1, 0, _ptr(hs), T, _ptr(ys), T, None, _ptr(self.sh_tiles),
                                                  _ptr(self.sh_ntiles), self.sh_tiles.shape[0], H, I, 0, _ptr(self.err),
                                                  st), "shared down")
         recv_counts_e = torch.empty_like(self.counts)
@@ -320,11 +321,11 @@ class ExpertParallelMoE:
                                         _ptr(self.counts2), _ptr(self.tiles2), _ptr(self.ntiles2),
                                         _ptr(self.perm_ws2), st), "regroup")
             _lib.check(L.ck_moe_expert_gemm(1, _ptr(self.w[0]), _ptr(self.w[1]), None, None, sp.matrix_bytes, self.el,
-                                             _ptr(self.xp2), nrecv, _ptr(self.h2), nrecv, _ptr(self.row_w2),
+                                             0, _ptr(self.xp2), nrecv, _ptr(self.h2), nrecv, _ptr(self.row_w2),
                                              _ptr(self.tiles2), _ptr(self.ntiles2), self.mt2, I, H, 0, _ptr(self.err),
                                              st), "expert gate/up")
             _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, None, None, sp.matrix_bytes, self.el,
-                                             _ptr(self.h2), nrecv, _ptr(self.y2), nrecv, None, _ptr(self.tiles2),
+                                             0, _ptr(self.h2), nrecv, _ptr(self.y2), nrecv, None, _ptr(self.tiles2),
                                              _ptr(self.ntiles2), self.mt2, H, I, 1, _ptr(self.err), st), "expert down")
             _lib.check(L.ck_gather_rows(_ptr(self.y2), _ptr(self.pair_pos2), _ptr(self.y_recv), nrecv, H * 2, st),
                        "restore order")

@@ -119,7 +119,7 @@ int ck_moe_permute(const int32_t *ids_dev, const float *wts_dev, const void *x_b
                    void *xp_bf16_dev, float *row_w_dev, int32_t *pair_pos_dev, int32_t *counts_dev,
                    void *tiles_dev, int32_t *ntiles_dev, void *workspace_dev, void *stream);
 int ck_moe_expert_gemm(int dual, const void *w0_dev, const void *w1_dev, const void *s0_dev, const void *s1_dev,
-                       uint64_t w_stride, uint32_t n_routed, const void *x_bf16_dev, uint32_t x_rows,
+                       uint64_t w_stride, uint32_t n_routed, uint32_t n_shared, const void *x_bf16_dev, uint32_t x_rows,
                        void *out_bf16_dev, uint32_t out_rows, const float *row_w_dev, const void *tiles_dev,
                        const int32_t *ntiles_dev, uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow,
                        int *err_dev, void *stream);
