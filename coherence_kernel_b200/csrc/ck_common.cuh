@@ -23,16 +23,20 @@ CK_DEV float f16_bits_to_float(uint32_t bits) {
 }
 
 // get_scale_min_k4 over the 12 packed scale bytes held as three little-endian words.
-CK_DEV void q4k_scale_min(const uint32_t s[3], int j, int &sc, int &mn) {
-    auto byte = [&](int i) -> int { return (int)((s[i >> 2] >> ((i & 3) * 8)) & 0xFFu); };
+// The three scale words are taken by value and picked apart with shifts: indexing an array of
+// them with the run-time sub-block j would put it in local memory.
+CK_DEV void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, int &sc, int &mn) {
+    const int sh = (j & 3) * 8;
+    const int b0 = (int)((s0 >> sh) & 0xFFu), b1 = (int)((s1 >> sh) & 0xFFu), b2 = (int)((s2 >> sh) & 0xFFu);
     if (j < 4) {
-        sc = byte(j) & 63;
-        mn = byte(j + 4) & 63;
+        sc = b0 & 63;  // scales[j]
+        mn = b1 & 63;  // scales[j + 4]
     } else {
-        sc = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
-        mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+        sc = (b2 & 0xF) | ((b0 >> 6) << 4);  // scales[j + 4] low nibble, scales[j - 4] top bits
+        mn = (b2 >> 4) | ((b1 >> 6) << 4);   // scales[j + 4] high nibble, scales[j] top bits
     }
 }
+CK_DEV void q4k_scale_min(const uint32_t s[3], int j, int &sc, int &mn) { q4k_scale_min(s[0], s[1], s[2], j, sc, mn); }
 
 CK_DEV uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

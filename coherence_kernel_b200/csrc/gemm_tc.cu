@@ -46,6 +46,26 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int P_HDR = BM * 16;  // superblock headers of the tile's rows
 constexpr int P_QS = BM * 32;   // the qs bytes of the K step's chunk
 constexpr int W_EPI0 = 2 + NDQ, W_PTMA = 2 + NDQ + NEPI;
+// ring depths (A: dequantized tiles, B: token tiles, P: packed weights) for the dual (gate/up) and
+// single forms; the defaults fill the shared memory of one CTA per SM
+#ifndef CK_DUAL_AST
+#define CK_DUAL_AST 2
+#endif
+#ifndef CK_DUAL_BST
+#define CK_DUAL_BST 3
+#endif
+#ifndef CK_DUAL_PST
+#define CK_DUAL_PST 4
+#endif
+#ifndef CK_SINGLE_AST
+#define CK_SINGLE_AST 3
+#endif
+#ifndef CK_SINGLE_BST
+#define CK_SINGLE_BST 4
+#endif
+#ifndef CK_SINGLE_PST
+#define CK_SINGLE_PST 6
+#endif
 
 template <int DUAL, int DENSE, int PT>
 struct Cfg {
@@ -56,11 +76,11 @@ struct Cfg {
     static constexpr int DENSE_ACC = 8;
     static constexpr int DENSE_TILE = 64;
     static constexpr int DENSE_B_BYTES = DENSE_TILE * BK * 2;
-    static constexpr int A_ST = DENSE ? 0 : (DUAL ? 2 : 3);
+    static constexpr int A_ST = DENSE ? 0 : (DUAL ? CK_DUAL_AST : CK_SINGLE_AST);
     static constexpr int A_STAGE = NMAT * A_BYTES;
-    static constexpr int B_ST = DENSE ? 6 : (DUAL ? 3 : 4);
+    static constexpr int B_ST = DENSE ? 6 : (DUAL ? CK_DUAL_BST : CK_SINGLE_BST);
     static constexpr int B_STAGE = DENSE ? A_BYTES + DENSE_B_BYTES : B_BYTES;
-    static constexpr int P_ST = (DENSE || !PT) ? 0 : (DUAL ? 4 : 6);
+    static constexpr int P_ST = (DENSE || !PT) ? 0 : (DUAL ? CK_DUAL_PST : CK_SINGLE_PST);
     static constexpr int P_STAGE = NMAT * (P_HDR + P_QS);
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_ST * A_STAGE;
@@ -111,14 +131,13 @@ CK_DEV uint32_t deq_pair(uint32_t pp, int hi, __nv_bfloat162 ds2, __nv_bfloat162
 // cc ^ (r & 7) (the 128-byte swizzle the MMA descriptor names).
 CK_DEV void dequant_half(const Packed &p, uint8_t *a, int r, int half) {
     const float d = f16_bits_to_float(p.hdr.x & 0xFFFF), dmin = f16_bits_to_float(p.hdr.x >> 16);
-    uint32_t s[3] = {p.hdr.y, p.hdr.z, p.hdr.w};
     int sc, mn;
-    q4k_scale_min(s, 2 * p.c + half, sc, mn);
+    q4k_scale_min(p.hdr.y, p.hdr.z, p.hdr.w, 2 * p.c + half, sc, mn);
     const float ds = d * (float)sc, dm = dmin * (float)mn;  // both exact in fp32
     const __nv_bfloat162 ds2 = __floats2bfloat162_rn(ds, ds), ndm2 = __floats2bfloat162_rn(-dm, -dm);
-    const uint32_t qw[8] = {p.q0.x, p.q0.y, p.q0.z, p.q0.w, p.q1.x, p.q1.y, p.q1.z, p.q1.w};
     uint8_t *row = a + r * 128;
     const int sw = r & 7;
+    const uint32_t qw[8] = {p.q0.x, p.q0.y, p.q0.z, p.q0.w, p.q1.x, p.q1.y, p.q1.z, p.q1.w};
 #pragma unroll
     for (int c4 = 0; c4 < 4; ++c4) {
         const uint32_t w0 = qw[2 * c4], w1 = qw[2 * c4 + 1];
@@ -228,7 +247,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp == W_PTMA) {
         // ------------------------------------------------------------ P ring producer (TMA)
-        if (PT && !DENSE && lane == 0) {
+        if constexpr (PT && !DENSE) if (lane == 0) {
             int it = 0;
             bool ok = true;
             const uint32_t row_bytes = p.K / 256 * Q4K_BYTES;
@@ -319,7 +338,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int part = di >> 7;
         const int mat = DUAL ? part : 0;
         int it = 0;
-        if (PT) {
+        if constexpr (PT && !DENSE) {
             bool ok = true;
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
                 for (int kb = 0; kb < nk; ++kb, ++it) {
@@ -335,7 +354,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     pk.q0 = *reinterpret_cast<const uint4 *>(ps + P_HDR + r * 32);
                     pk.q1 = *reinterpret_cast<const uint4 *>(ps + P_HDR + r * 32 + 16);
                     pk.c = kb & 3;
-                    mbar_arrive(&p_empty[sp]);  // the packed bytes are in registers now
                     uint8_t *a = smem + C::A_OFF + sa * C::A_STAGE;
                     if (DUAL) {
                         dequant_half(pk, a + mat * A_BYTES, r, 0);
@@ -343,11 +361,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     } else {
                         dequant_half(pk, a, r, part);
                     }
+                    // One proxy fence orders both this thread's generic reads of the P stage
+                    // before the TMA that refills it and its generic writes of the A tile before
+                    // the MMA that reads it.  Without it the TMA write (async proxy) may land
+                    // before the reads are done, even after the mbarrier release.
                     fence_proxy_async_smem();
+                    mbar_arrive(&p_empty[sp]);
                     mbar_arrive(&a_full[sa]);
                 }
             }
-        } else {
+        } else if constexpr (!DENSE) {
             // rows that straddle superblocks: each thread loads its packed fields, one step ahead
             Packed cur, nxt;
             int u = blockIdx.x, kb = 0;
@@ -397,11 +420,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int sp = warp & 3;  // TMEM sub-partition this warp may read
         int ut = 0;
         __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(p.out);
+        // lane j holds the route weight of token cb*32 + j of the current chunk (shuffled out
+        // below); the next chunk's weight is loaded one chunk ahead, the first before the wait
+        auto route_w = [&](const Tile &t, int cb) -> float {
+            return (DUAL && p.row_w && cb * 32 + lane < t.ntok) ? p.row_w[t.orow + cb * 32 + lane] : 1.0f;
+        };
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ut) {
             const Tile t = load_tile(p.tiles, u / nrt);
             const int n0 = (u % nrt) * BM;
             const int ab = ut % C::NBUF;
             const uint32_t aph = (uint32_t)(ut / C::NBUF) & 1u;
+            float rw_lane = route_w(t, 0);
             if (!mbar_wait_bounded(&acc_full[ab], aph, p.err, 6)) break;
             tc_fence_after();
             const uint32_t row = (uint32_t)(n0 + 32 * sp + lane);
@@ -410,13 +439,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 uint32_t g[32], v[32];
                 tmem_ld32(tbase + cb * 32, g);
                 if (DUAL) tmem_ld32(tbase + BN + cb * 32, v);
-                // lane j fetches the route weight of token cb*32 + j; shuffled out below
-                const float rw_lane = (DUAL && p.row_w && cb * 32 + lane < t.ntok) ? p.row_w[t.orow + cb * 32 + lane] : 1.0f;
+                const float rw_next = route_w(t, cb + 1);
                 tmem_ld_wait();
                 if (DENSE) {
-                    // sum the K-chunk accumulators in fp32, in chunk order
+                    // sum the K-chunk accumulators in fp32, in chunk order; with fewer than
+                    // DENSE_ACC K steps per chunk only the first ceil(nk / chunk) were written
+                    const int kchunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
+                    const int nacc = (nk + kchunk - 1) / kchunk;
 #pragma unroll 1
-                    for (int a = 1; a < C::DENSE_ACC; ++a) {
+                    for (int a = 1; a < nacc; ++a) {
                         tmem_ld32(tbase + a * C::DENSE_TILE + cb * 32, v);
                         tmem_ld_wait();
 #pragma unroll
@@ -430,8 +461,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (tok < t.ntok && row < p.N) {
                         float val = __uint_as_float(g[j]);
                         if (DUAL) {
+                            // silu(g) = g / (1 + e^-g); where e^-g overflows the quotient is
+                            // the limit 0, which __fdividef returns for divisors past 2^126
                             const float up = __uint_as_float(v[j]);
-                            val = (val / (1.0f + __expf(-val))) * up * rw;
+                            val = __fdividef(val, 1.0f + __expf(-val)) * up * rw;
                         }
                         if (DENSE)
                             p.out_f32[(uint64_t)(t.orow + tok) * p.N + row] = val;
@@ -439,6 +472,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             out[(uint64_t)(t.orow + tok) * p.N + row] = __float2bfloat16_rn(val);
                     }
                 }
+                rw_lane = rw_next;
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[ab]);
