@@ -39,6 +39,7 @@ SIGNATURES = {
     "ck_q4k_matmul_batch_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
     "ck_q4k_gemm_workspace_bytes": (_sz, [_u32]),
     "ck_q4k_gemm_bf16": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p, _sz, _p]),
+    "ck_q4k_gemm_bf16_noalloc": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
     "ck_f16_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_route_softmax_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _i32, _p]),
     "ck_route_dsv4_f32": (_i32, [_p, _p, _p, _p, _u32, _u32, _f, _u32, _p]),

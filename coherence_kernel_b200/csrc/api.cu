@@ -3,6 +3,7 @@
 #include "ck_common.cuh"
 #include "ck_launch.h"
 
+#include <mutex>
 #include <stdio.h>
 #include <string.h>
 
@@ -389,3 +390,82 @@ int ck_moe_layer_status(const ck_moe_config *c, uint32_t ntok, const void *ws, v
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------- no-allocation GEMM
+// ck_q4k_gemm_bf16 takes its scratch (the token-tile table, the table's length and the device
+// error word) from a caller workspace.  Some callers cannot provide one: a host runtime that keeps
+// its own arenas and has no CUDA-aware allocator (the reference's C runtime is one), a serving
+// loop that must not allocate between requests, or code that runs while holding a lock the
+// allocator may also take.  ck_q4k_gemm_bf16_noalloc keeps that scratch in one fixed array in
+// device memory instead, sized for CK_Q4K_GEMM_NOALLOC_MAX_TOKENS tokens (about 65 KB), so no call
+// allocates: no cudaMalloc, no cudaFree, no allocating library call.
+//
+// The array is shared by every call on a device and keeps whatever the last call left in it; each
+// call rewrites the tile table and its length and clears the error word before its kernels run.
+// Two calls in flight at the same time on one device (different streams, or host threads) race on
+// it and must be serialized by the caller.
+namespace {
+constexpr size_t kNoallocTileBytes = ((size_t)CK_Q4K_GEMM_NOALLOC_MAX_TOKENS / 16 + 2) * 16;
+constexpr size_t kNoallocTileRegion = (kNoallocTileBytes + 255) & ~(size_t)255;
+constexpr size_t kNoallocBytes = kNoallocTileRegion + 256 + 256;  // + table length + error word
+constexpr int kNoallocMaxDevices = 64;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kNoallocMaxDevices];
+
+// The array's device address on the current device, looked up once per device (the first call on
+// a device does this; it may load the module, so make that first call before any stream capture).
+int noalloc_scratch(void **out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= kNoallocMaxDevices) return CK_ENODEV;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return (int)e;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return 0;
+}
+}  // namespace
+
+extern "C" int ck_q4k_gemm_bf16_noalloc(const void *qb, const void *x, void *y, uint32_t rows, uint32_t cols,
+                                        uint32_t ntok, void *s) {
+    if (!qb || !x || !y) return fail(CK_EARG, "ck_q4k_gemm_bf16_noalloc");
+    if (ntok > CK_Q4K_GEMM_NOALLOC_MAX_TOKENS) {
+        static thread_local char what[160];
+        snprintf(what, sizeof(what), "ck_q4k_gemm_bf16_noalloc: %u tokens, the fixed scratch holds at most %u",
+                 ntok, (unsigned)CK_Q4K_GEMM_NOALLOC_MAX_TOKENS);
+        return fail(CK_ESHAPE, what);
+    }
+    void *base = nullptr;
+    int rc = noalloc_scratch(&base);
+    if (rc) return fail(rc, "ck_q4k_gemm_bf16_noalloc scratch address");
+    if (ntok == 0) return 0;
+    uint8_t *b = (uint8_t *)base;
+    int4 *tiles = (int4 *)b;
+    int32_t *ntiles = (int32_t *)(b + kNoallocTileRegion);
+    int *err = (int *)(b + kNoallocTileRegion + 256);
+    cudaError_t e = cudaMemsetAsync(err, 0, 4, S(s));  // the one field that must start at zero
+    if (e != cudaSuccess) return fail((int)e, "ck_q4k_gemm_bf16_noalloc");
+    rc = ck::launch_single_tiles(tiles, ntiles, ntok, 256, S(s));
+    if (rc) return fail(rc, "ck_q4k_gemm_bf16_noalloc tiles");
+    ck::GemmParams p = {};
+    p.w0 = (const uint8_t *)qb;
+    p.x = x;
+    p.x_rows = ntok;
+    p.out = y;
+    p.out_rows = ntok;
+    p.tiles = tiles;
+    p.ntiles = ntiles;
+    p.max_tiles = (uint32_t)(ntok / 16 + 2);
+    p.n_routed = 1;
+    p.N = rows;
+    p.K = cols;
+    p.err = err;
+    return fail(ck::launch_gemm_q4k(p, S(s)), "ck_q4k_gemm_bf16_noalloc");
+}

@@ -60,6 +60,18 @@ size_t ck_q4k_gemm_workspace_bytes(uint32_t ntok);
 int ck_q4k_gemm_bf16(const void *qb_dev, const void *x_bf16_dev, void *y_bf16_dev, uint32_t rows, uint32_t cols,
                      uint32_t ntok, void *workspace_dev, size_t workspace_bytes, void *stream);
 
+/* The same GEMM for callers that cannot allocate or hand over a workspace (a host runtime with its
+ * own arenas and no CUDA-aware allocator, a serving loop that must not allocate per request).  No
+ * counterpart in the reference, whose matmul kernels take no scratch.  The scratch lives in one
+ * fixed array in device memory (about 65 KB), so ntok <= CK_Q4K_GEMM_NOALLOC_MAX_TOKENS; larger
+ * ntok fails with CK_ESHAPE.  The first call on a device looks the array up (it may load the
+ * module): make it, with any ntok including 0, before stream capture.  Every call on a device
+ * shares the array and leaves its contents behind; calls that overlap in time on one device race
+ * on it and must be serialized by the caller. */
+#define CK_Q4K_GEMM_NOALLOC_MAX_TOKENS 65536u
+int ck_q4k_gemm_bf16_noalloc(const void *qb_dev, const void *x_bf16_dev, void *y_bf16_dev, uint32_t rows,
+                             uint32_t cols, uint32_t ntok, void *stream);
+
 /* ---- small kernels of the reference's MoE decode (moe-msl.fk:114-140, dsv4-moe-msl.fk:87-88,
  *      dsv4-router-msl.fk:103-106, moe-route-wide-msl.fk) -- one routing per token, ntok tokens */
 int ck_f16_matvec_f32(const void *w_f16_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
