@@ -20,8 +20,9 @@
 // Warps:
 //   0       TMA producer of the B ring (and of the A operand in the dense form)
 //   1       TMEM allocator and the single MMA-issuing thread (tcgen05.mma kind::f16, M = 128)
-//   2-9     dequant: two threads per weight row; prmt + magic-exponent nibble decode, one exact
-//           bf16x2 subtract and one bf16x2 FMA per weight pair, stores into the A ring
+//   2-9     dequant: two groups of 128 threads taking alternate K steps, one thread per weight
+//           row; prmt + magic-exponent nibble decode, one exact bf16x2 subtract and one bf16x2
+//           FMA per weight pair, stores into the A ring
 //   10-13   epilogue: tcgen05.ld of the fp32 accumulators, SwiGLU x route weight, stores
 //   14      TMA producer of the P ring
 // Every wait is bounded (about one second); on a timeout the kernel records a code in *err and
@@ -38,7 +39,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int BN = 256;
-constexpr int NDQ = 8;   // dequant warps (two threads per weight row)
+constexpr int NDQ = 8;   // dequant warps (two groups of one thread per weight row)
 constexpr int NEPI = 4;  // epilogue warps
 constexpr int NTHREADS = (2 + NDQ + NEPI + 1) * 32;
 constexpr int A_BYTES = BM * BK * 2;
@@ -82,10 +83,13 @@ struct Cfg {
     static constexpr int B_STAGE = DENSE ? A_BYTES + DENSE_B_BYTES : B_BYTES;
     static constexpr int P_ST = (DENSE || !PT) ? 0 : (DUAL ? CK_DUAL_PST : CK_SINGLE_PST);
     static constexpr int P_STAGE = NMAT * (P_HDR + P_QS);
+    // per epilogue warp, one 32-token x 32-row bf16 chunk of the output, token-major
+    static constexpr int EPI_STAGE = 32 * 32 * 2;
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_ST * A_STAGE;
     static constexpr int P_OFF = B_OFF + B_ST * B_STAGE;
-    static constexpr int BAR_OFF = P_OFF + P_ST * P_STAGE;
+    static constexpr int EPI_OFF = P_OFF + P_ST * P_STAGE;
+    static constexpr int BAR_OFF = EPI_OFF + (DENSE ? 0 : NEPI * EPI_STAGE);
     static constexpr int ACC_COLS = DENSE ? 512 : NMAT * BN;
     static constexpr int NBUF = 512 / ACC_COLS;
     static constexpr int SMEM = BAR_OFF + 512 + 1024;
@@ -191,12 +195,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < 8; ++s) {
             mbar_init(&p_full[s], 1);
-            mbar_init(&p_empty[s], NDQ * 32);
+            mbar_init(&p_empty[s], NDQ * 16);  // one dequant group per stage
             mbar_init(&b_full[s], 1);
             mbar_init(&b_empty[s], 1);
         }
         for (int s = 0; s < 4; ++s) {
-            mbar_init(&a_full[s], NDQ * 32);
+            mbar_init(&a_full[s], NDQ * 16);
             mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -331,35 +335,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp < W_EPI0 && !DENSE) {
         // ------------------------------------------------------------ dequant producers
-        // 256 threads: thread i owns row (i & 127) of the tile; part = i >> 7 selects the matrix
-        // (dual: gate or up, both halves of the 64-weight chunk) or the nibble half (single).
+        // 256 threads in two groups of 128; thread i owns row (i & 127) of the tile and group
+        // i >> 7 takes every other K step (items it with it % 2 == group), converting the whole
+        // 64-weight chunk of its row in every matrix.  Two stages are in flight at once and each
+        // thread's barrier waits and proxy fence are spread over 64 x NMAT weights.
         const int di = threadIdx.x - 64;
         const int r = di & (BM - 1);
-        const int part = di >> 7;
-        const int mat = DUAL ? part : 0;
-        int it = 0;
+        const int grp = di >> 7;
         if constexpr (PT && !DENSE) {
+            int it = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
                 for (int kb = 0; kb < nk; ++kb, ++it) {
+                    if ((it & 1) != grp) continue;
                     const int sp = it % C::P_ST, sa = it % C::A_ST;
                     const uint32_t php = (uint32_t)(it / C::P_ST) & 1u, pha = (uint32_t)(it / C::A_ST) & 1u;
                     if (!mbar_wait_bounded(&p_full[sp], php, p.err, 8) || !mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) {
                         ok = false;
                         break;
                     }
-                    const uint8_t *ps = smem + C::P_OFF + sp * C::P_STAGE + mat * (P_HDR + P_QS);
-                    Packed pk;
-                    pk.hdr = *reinterpret_cast<const uint4 *>(ps + r * 16);
-                    pk.q0 = *reinterpret_cast<const uint4 *>(ps + P_HDR + r * 32);
-                    pk.q1 = *reinterpret_cast<const uint4 *>(ps + P_HDR + r * 32 + 16);
-                    pk.c = kb & 3;
+                    const uint8_t *ps = smem + C::P_OFF + sp * C::P_STAGE;
                     uint8_t *a = smem + C::A_OFF + sa * C::A_STAGE;
-                    if (DUAL) {
-                        dequant_half(pk, a + mat * A_BYTES, r, 0);
-                        dequant_half(pk, a + mat * A_BYTES, r, 1);
-                    } else {
-                        dequant_half(pk, a, r, part);
+#pragma unroll
+                    for (int m = 0; m < C::NMAT; ++m) {
+                        const uint8_t *pm_ = ps + m * (P_HDR + P_QS);
+                        Packed pk;
+                        pk.hdr = *reinterpret_cast<const uint4 *>(pm_ + r * 16);
+                        pk.q0 = *reinterpret_cast<const uint4 *>(pm_ + P_HDR + r * 32);
+                        pk.q1 = *reinterpret_cast<const uint4 *>(pm_ + P_HDR + r * 32 + 16);
+                        pk.c = kb & 3;
+                        dequant_half(pk, a + m * A_BYTES, r, 0);
+                        dequant_half(pk, a + m * A_BYTES, r, 1);
                     }
                     // One proxy fence orders both this thread's generic reads of the P stage
                     // before the TMA that refills it and its generic writes of the A tile before
@@ -371,46 +377,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
         } else if constexpr (!DENSE) {
-            // rows that straddle superblocks: each thread loads its packed fields, one step ahead
-            Packed cur, nxt;
-            int u = blockIdx.x, kb = 0;
-            auto base_of = [&](int uu, uint64_t &rowflat) -> const uint8_t * {
+            // rows that straddle superblocks: each thread loads the packed fields of its next own
+            // item (two items ahead) while it converts the current one
+            auto advance = [&](int &uu, int &kk) {
+                if (++kk == nk) {
+                    kk = 0;
+                    uu += gridDim.x;
+                }
+            };
+            auto load_item = [&](int uu, int kk, Packed (&pk)[C::NMAT]) {
                 const Tile t = load_tile(p.tiles, uu / nrt);
                 const int n0 = (uu % nrt) * BM;
                 const uint32_t row = min((uint32_t)(n0 + r), p.N - 1);
                 const bool shared = (uint32_t)t.g >= p.n_routed;
                 const uint64_t g = shared ? (uint64_t)(t.g - p.n_routed) : (uint64_t)t.g;
-                const uint8_t *b = (DUAL && part) ? (shared ? p.s1 : p.w1) : (shared ? p.s0 : p.w0);
-                rowflat = (uint64_t)row * p.K;
-                return b + g * p.w_stride;
-            };
-            const uint8_t *b = nullptr;
-            uint64_t rowflat = 0;
-            if (u < nunits) {
-                b = base_of(u, rowflat);
-                load_packed(nxt, b, rowflat);
-            }
-            while (u < nunits) {
-                cur = nxt;
-                int nu = u, nkb = kb + 1;
-                if (nkb == nk) { nkb = 0; nu = u + gridDim.x; }
-                if (nu < nunits) {
-                    if (nu != u) b = base_of(nu, rowflat);
-                    load_packed(nxt, b, rowflat + (uint64_t)nkb * BK);
+#pragma unroll
+                for (int m = 0; m < C::NMAT; ++m) {
+                    const uint8_t *b = m ? (shared ? p.s1 : p.w1) : (shared ? p.s0 : p.w0);
+                    load_packed(pk[m], b + g * p.w_stride, (uint64_t)row * p.K + (uint64_t)kk * BK);
                 }
+            };
+            Packed cur[C::NMAT], nxt[C::NMAT];
+            int u = blockIdx.x, kb = 0, it = grp;
+            if (grp) advance(u, kb);
+            if (u < nunits) load_item(u, kb, nxt);
+            while (u < nunits) {
+#pragma unroll
+                for (int m = 0; m < C::NMAT; ++m) cur[m] = nxt[m];
+                int nu = u, nkb = kb;
+                advance(nu, nkb);
+                advance(nu, nkb);
+                if (nu < nunits) load_item(nu, nkb, nxt);
                 const int sa = it % C::A_ST;
                 const uint32_t pha = (uint32_t)(it / C::A_ST) & 1u;
                 if (!mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) break;
                 uint8_t *a = smem + C::A_OFF + sa * C::A_STAGE;
-                if (DUAL) {
-                    dequant_half(cur, a + part * A_BYTES, r, 0);
-                    dequant_half(cur, a + part * A_BYTES, r, 1);
-                } else {
-                    dequant_half(cur, a, r, part);
+#pragma unroll
+                for (int m = 0; m < C::NMAT; ++m) {
+                    dequant_half(cur[m], a + m * A_BYTES, r, 0);
+                    dequant_half(cur[m], a + m * A_BYTES, r, 1);
                 }
                 fence_proxy_async_smem();
                 mbar_arrive(&a_full[sa]);
-                ++it;
+                it += 2;
                 u = nu;
                 kb = nkb;
             }
@@ -420,6 +429,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int sp = warp & 3;  // TMEM sub-partition this warp may read
         int ut = 0;
         __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(p.out);
+        uint8_t *epi_stage = smem + C::EPI_OFF + (warp - W_EPI0) * C::EPI_STAGE;
+        const bool vec_out = !DENSE && p.N % 8 == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
         // lane j holds the route weight of token cb*32 + j of the current chunk (shuffled out
         // below); the next chunk's weight is loaded one chunk ahead, the first before the wait
         auto route_w = [&](const Tile &t, int cb) -> float {
@@ -434,6 +445,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!mbar_wait_bounded(&acc_full[ab], aph, p.err, 6)) break;
             tc_fence_after();
             const uint32_t row = (uint32_t)(n0 + 32 * sp + lane);
+            // this warp's 32 rows are all inside N and every 8-row group starts 16-byte aligned
+            const bool vec_rows = vec_out && (uint32_t)(n0 + 32 * sp + 32) <= p.N;
             const uint32_t tbase = tmem_base + ((uint32_t)(32 * sp) << 16) + (uint32_t)(ab * C::ACC_COLS);
             for (int cb = 0; cb * 32 < t.ntok; ++cb) {
                 uint32_t g[32], v[32];
@@ -454,22 +467,46 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         for (int j = 0; j < 32; ++j) g[j] = __float_as_uint(__uint_as_float(g[j]) + __uint_as_float(v[j]));
                     }
                 }
+                if (!DENSE && vec_rows) {
+                    // the chunk goes through shared memory, token-major (64 bytes per token), and
+                    // leaves as 16-byte stores: lane l writes rows 8(l%4).. of token 8q + l/4
+                    __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(epi_stage);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int tok = cb * 32 + j;
-                    const float rw = __shfl_sync(0xffffffffu, rw_lane, j);
-                    if (tok < t.ntok && row < p.N) {
+                    for (int j = 0; j < 32; ++j) {
                         float val = __uint_as_float(g[j]);
                         if (DUAL) {
                             // silu(g) = g / (1 + e^-g); where e^-g overflows the quotient is
                             // the limit 0, which __fdividef returns for divisors past 2^126
-                            const float up = __uint_as_float(v[j]);
-                            val = __fdividef(val, 1.0f + __expf(-val)) * up * rw;
+                            const float rw = __shfl_sync(0xffffffffu, rw_lane, j);
+                            val = __fdividef(val, 1.0f + __expf(-val)) * __uint_as_float(v[j]) * rw;
                         }
-                        if (DENSE)
-                            p.out_f32[(uint64_t)(t.orow + tok) * p.N + row] = val;
-                        else
-                            out[(uint64_t)(t.orow + tok) * p.N + row] = __float2bfloat16_rn(val);
+                        st[j * 32 + lane] = __float2bfloat16_rn(val);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int tl = q * 8 + (lane >> 2), seg = lane & 3;
+                        const uint4 o = *reinterpret_cast<const uint4 *>(epi_stage + q * 512 + lane * 16);
+                        if (cb * 32 + tl < t.ntok)
+                            *reinterpret_cast<uint4 *>(out + (uint64_t)(t.orow + cb * 32 + tl) * p.N + n0 + 32 * sp + 8 * seg) = o;
+                    }
+                    __syncwarp();
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int tok = cb * 32 + j;
+                        const float rw = __shfl_sync(0xffffffffu, rw_lane, j);
+                        if (tok < t.ntok && row < p.N) {
+                            float val = __uint_as_float(g[j]);
+                            if (DUAL) {
+                                const float up = __uint_as_float(v[j]);
+                                val = __fdividef(val, 1.0f + __expf(-val)) * up * rw;
+                            }
+                            if (DENSE)
+                                p.out_f32[(uint64_t)(t.orow + tok) * p.N + row] = val;
+                            else
+                                out[(uint64_t)(t.orow + tok) * p.N + row] = __float2bfloat16_rn(val);
+                        }
                     }
                 }
                 rw_lane = rw_next;

@@ -40,47 +40,90 @@ CK_DEV double ref_exp(double x) {
 }
 CK_DEV double ref_sigmoid(double x) { return __ddiv_rn(1.0, __dadd_rn(1.0, ref_exp(__dsub_rn(0.0, x)))); }
 
-constexpr int XL_TOK = 8;    // flagged tokens per work item
+constexpr int XL_TOK = 16;   // flagged tokens per work item
 constexpr int XL_EXP = 64;   // experts per work item
 constexpr int XL_J = 32;     // columns per shared-memory tile
+constexpr int XL_TPT = 4;    // tokens (independent fold chains) per thread
 
 // out[f * ne + e] = right fold of router row e with flagged token f's activations, fp64.
+// The product of an fp32 weight and a bf16 activation has at most 32 significant bits, so it is
+// exact in fp64 and fma(w, x, acc) rounds once exactly as acc + (w * x) does: one DFMA per term.
+// 256 threads = 64 experts x 4 token groups; each thread folds 4 tokens.  The W and x tiles are
+// converted to double once per tile into shared memory, double-buffered: the next tile's global
+// loads are in registers while the current tile is folded.
 __global__ void __launch_bounds__(256) k_exact_logits(const uint16_t *__restrict__ x, const float *__restrict__ W,
                                                       const uint32_t *__restrict__ flag_list,
                                                       const uint32_t *__restrict__ flag_count, double *__restrict__ out,
                                                       uint32_t ne, uint32_t hidden) {
-    __shared__ float wt[XL_EXP][XL_J + 1];
-    __shared__ double xt[XL_TOK][XL_J];
+    __shared__ double wt[2][XL_EXP][XL_J + 1];
+    __shared__ __align__(16) double xt[2][XL_TOK][XL_J];
     const uint32_t nflag = *flag_count;
-    const int el = threadIdx.x & (XL_EXP - 1);
-    const int q = threadIdx.x / XL_EXP;  // 0..3: this thread folds tokens 2q and 2q+1 of the item
+    const int tid = threadIdx.x;
+    const int el = tid & (XL_EXP - 1);
+    const int q = tid / XL_EXP;  // 0..3: this thread folds tokens 4q .. 4q+3 of the item
     const uint32_t ntg = (nflag + XL_TOK - 1) / XL_TOK, neg = (ne + XL_EXP - 1) / XL_EXP;
+    const int ntile = (int)(hidden / XL_J);
+    constexpr int WPT = XL_EXP * XL_J / 256;  // W floats each thread stages per tile (8)
+    constexpr int XPT = XL_TOK * XL_J / 256;  // x values each thread stages per tile (2)
     for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
         const uint32_t f0 = (item / neg) * XL_TOK, e0 = (item % neg) * XL_EXP;
-        double a0 = 0.0, a1 = 0.0;
-        for (int j0 = (int)hidden - XL_J; j0 >= 0; j0 -= XL_J) {
+        const float *wrow[WPT];
+        const uint16_t *xrow[XPT];
+#pragma unroll
+        for (int k = 0; k < WPT; ++k) {
+            const uint32_t e = e0 + (uint32_t)((tid + 256 * k) / XL_J);
+            wrow[k] = e < ne ? W + (size_t)e * hidden : nullptr;
+        }
+#pragma unroll
+        for (int k = 0; k < XPT; ++k) {
+            const uint32_t f = min(f0 + (uint32_t)((tid + 256 * k) / XL_J), nflag - 1);
+            xrow[k] = x + (size_t)flag_list[f] * hidden;
+        }
+        const int jc = tid % XL_J;
+        float wv[WPT];
+        uint16_t xv[XPT];
+        auto fetch = [&](int tile) {  // tile t covers columns hidden - 32 (t + 1) .. hidden - 32 t - 1
+            const int j0 = (int)hidden - XL_J * (tile + 1);
+#pragma unroll
+            for (int k = 0; k < WPT; ++k) wv[k] = wrow[k] ? __ldg(wrow[k] + j0 + jc) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < XPT; ++k) xv[k] = __ldg(xrow[k] + j0 + jc);
+        };
+        auto stage = [&](int b) {
+#pragma unroll
+            for (int k = 0; k < WPT; ++k) wt[b][(tid + 256 * k) / XL_J][jc] = (double)wv[k];
+#pragma unroll
+            for (int k = 0; k < XPT; ++k) xt[b][(tid + 256 * k) / XL_J][jc] = (double)bf16_bits_to_float(xv[k]);
+        };
+        fetch(0);
+        stage(0);
+        __syncthreads();
+        double a[XL_TPT];
+#pragma unroll
+        for (int t = 0; t < XL_TPT; ++t) a[t] = 0.0;
+        for (int tile = 0; tile < ntile; ++tile) {
+            const int b = tile & 1;
+            if (tile + 1 < ntile) fetch(tile + 1);
+#pragma unroll
+            for (int jj = XL_J - 2; jj >= 0; jj -= 2) {  // columns jj + 1, then jj: descending j
+                const double w1 = wt[b][el][jj + 1], w0 = wt[b][el][jj];
+#pragma unroll
+                for (int t = 0; t < XL_TPT; ++t) {
+                    const double2 xx = *reinterpret_cast<const double2 *>(&xt[b][XL_TPT * q + t][jj]);
+                    a[t] = __fma_rn(w1, xx.y, a[t]);
+                    a[t] = __fma_rn(w0, xx.x, a[t]);
+                }
+            }
+            if (tile + 1 < ntile) stage(b ^ 1);
             __syncthreads();
-            for (int i = threadIdx.x; i < XL_EXP * XL_J; i += blockDim.x) {
-                const uint32_t e = e0 + (i / XL_J);
-                wt[i / XL_J][i % XL_J] = e < ne ? W[(size_t)e * hidden + j0 + (i % XL_J)] : 0.0f;
-            }
-            {
-                const int tq = threadIdx.x / XL_J, j = threadIdx.x % XL_J;  // 8 tokens x 32 columns
-                const uint32_t f = min(f0 + tq, nflag - 1);
-                xt[tq][j] = (double)bf16_bits_to_float(x[(size_t)flag_list[f] * hidden + j0 + j]);
-            }
-            __syncthreads();
-#pragma unroll 8
-            for (int j = XL_J - 1; j >= 0; --j) {
-                const double w = (double)wt[el][j];
-                a0 = __dadd_rn(__dmul_rn(w, xt[2 * q][j]), a0);
-                a1 = __dadd_rn(__dmul_rn(w, xt[2 * q + 1][j]), a1);
-            }
         }
         const uint32_t e = e0 + el;
         if (e < ne) {
-            if (f0 + 2 * q < nflag) out[(size_t)(f0 + 2 * q) * ne + e] = a0;
-            if (f0 + 2 * q + 1 < nflag) out[(size_t)(f0 + 2 * q + 1) * ne + e] = a1;
+#pragma unroll
+            for (int t = 0; t < XL_TPT; ++t) {
+                const uint32_t f = f0 + XL_TPT * q + t;
+                if (f < nflag) out[(size_t)f * ne + e] = a[t];
+            }
         }
     }
 }
@@ -233,7 +276,7 @@ int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    k_exact_logits<<<nsm * 4, 256, 0, s>>>(x, w, flag_list, flag_count, scratch, p.ne, p.hidden);
+    k_exact_logits<<<nsm * 2, 256, 0, s>>>(x, w, flag_list, flag_count, scratch, p.ne, p.hidden);
     k_exact_select<<<nsm * 2, 256, 0, s>>>(scratch, bias, ids, wts, flag_list, flag_count, p);
     return (int)cudaGetLastError();
 }
