@@ -72,7 +72,7 @@ ck::PermuteParams perm_params(const ck_moe_config *c, uint32_t ntok) {
     p.n_experts = c->n_experts;
     p.n_shared = c->n_shared;
     p.hidden = c->hidden;
-    p.bn = 256;
+    p.bn = ck::GEMM_TILE_TOKENS;
     p.weight_in_mid = c->mode == 4 ? 1 : 0;
     return p;
 }
@@ -174,7 +174,7 @@ int ck_q4k_gemm_bf16(const void *qb, const void *x, void *y, uint32_t rows, uint
     int32_t *ntiles = (int32_t *)(b + tb);
     int *err = (int *)(b + tb + 256);
     cudaMemsetAsync(err, 0, 4, S(s));
-    int rc = ck::launch_single_tiles(tiles, ntiles, ntok, 256, S(s));
+    int rc = ck::launch_single_tiles(tiles, ntiles, ntok, ck::GEMM_TILE_TOKENS, S(s));
     if (rc) return fail(rc, "ck_q4k_gemm_bf16 tiles");
     ck::GemmParams p = {};
     p.w0 = (const uint8_t *)qb;
@@ -292,7 +292,7 @@ int ck_moe_route_flagged(const ck_moe_config *c, uint32_t ntok, const void *ws, 
 int ck_moe_permute(const int32_t *ids, const float *wts, const void *x, uint32_t ntok, uint32_t nsel,
                    uint32_t n_experts, uint32_t n_shared, uint32_t hidden, int weight_in_mid, void *xp, float *row_w,
                    int32_t *pair_pos, int32_t *counts, void *tiles, int32_t *ntiles, void *ws, void *s) {
-    ck::PermuteParams p = {ntok, nsel, n_experts, n_shared, hidden, 256, (uint32_t)(weight_in_mid ? 1 : 0)};
+    ck::PermuteParams p = {ntok, nsel, n_experts, n_shared, hidden, ck::GEMM_TILE_TOKENS, (uint32_t)(weight_in_mid ? 1 : 0)};
     return fail(ck::launch_permute(ids, wts, (const uint16_t *)x, (uint16_t *)xp, row_w, pair_pos, counts,
                                    (int4 *)tiles, ntiles, ws, p, S(s)),
                 "ck_moe_permute");
@@ -329,14 +329,14 @@ int ck_moe_expert_gemm(int dual, const void *w0, const void *w1, const void *s0,
 int ck_moe_combine(const void *y, const int32_t *ids, const float *wts, const int32_t *pair_pos, uint32_t ntok,
                    uint32_t nsel, uint32_t n_shared, uint32_t hidden, int order_by_expert, void *out, float *out_f32,
                    void *s) {
-    ck::PermuteParams p = {ntok, nsel, 0, n_shared, hidden, 256, 0};
+    ck::PermuteParams p = {ntok, nsel, 0, n_shared, hidden, ck::GEMM_TILE_TOKENS, 0};
     return fail(ck::launch_combine((const uint16_t *)y, ids, wts, pair_pos, (uint16_t *)out, out_f32, p,
                                    order_by_expert, S(s)),
                 "ck_moe_combine");
 }
 
 int ck_token_tiles(void *tiles, int32_t *ntiles, uint32_t ntok, void *s) {
-    return fail(ck::launch_single_tiles((int4 *)tiles, ntiles, ntok, 256, S(s)), "ck_token_tiles");
+    return fail(ck::launch_single_tiles((int4 *)tiles, ntiles, ntok, ck::GEMM_TILE_TOKENS, S(s)), "ck_token_tiles");
 }
 
 int ck_gather_rows(const void *src, const int32_t *idx, void *dst, uint32_t nrows, uint32_t row_bytes, void *s) {
@@ -452,7 +452,7 @@ extern "C" int ck_q4k_gemm_bf16_noalloc(const void *qb, const void *x, void *y, 
     int *err = (int *)(b + kNoallocTileRegion + 256);
     cudaError_t e = cudaMemsetAsync(err, 0, 4, S(s));  // the one field that must start at zero
     if (e != cudaSuccess) return fail((int)e, "ck_q4k_gemm_bf16_noalloc");
-    rc = ck::launch_single_tiles(tiles, ntiles, ntok, 256, S(s));
+    rc = ck::launch_single_tiles(tiles, ntiles, ntok, ck::GEMM_TILE_TOKENS, S(s));
     if (rc) return fail(rc, "ck_q4k_gemm_bf16_noalloc tiles");
     ck::GemmParams p = {};
     p.w0 = (const uint8_t *)qb;

@@ -45,6 +45,10 @@ int launch_route_exact(const uint16_t *x_bf16, const float *w, const float *bias
                        const uint32_t *flag_list, const uint32_t *flag_count, double *scratch, const RouteParams &p,
                        cudaStream_t s);
 
+// The grouped GEMM's largest token tile: its accumulators (gate and up, or two buffers) and its
+// tensor-memory A stages share the 512 TMEM columns.  Every token-tile table is built with it.
+constexpr uint32_t GEMM_TILE_TOKENS = 192;
+
 // MoE permute / combine (moe_kernels.cu)
 struct PermuteParams {
     uint32_t ntok, nsel, n_experts, n_shared, hidden;

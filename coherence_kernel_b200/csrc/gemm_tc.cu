@@ -10,19 +10,25 @@
 // A third form, dense = 1, reads a bf16 A operand through TMA instead of dequantizing and writes
 // fp32: the router logits, with the fp32 router split into three bf16 terms along K.
 //
-// One persistent CTA per SM, warp-specialised, three shared-memory rings:
+// One persistent CTA per SM, warp-specialised.  The dequantized weights never touch shared
+// memory: the dequant threads write them straight into tensor memory (tcgen05.st) and the MMA
+// reads its A operand from there, so shared-memory bandwidth goes to the token tiles and the packed
+// weights only.  Tensor memory (512 columns) holds the fp32 accumulators (token tiles of at most
+// BN = 192 columns; gate and up in the dual form, two buffers in the single form) and the A
+// stages (32 columns per matrix per 64-wide K step).  Shared-memory rings:
 //   P ring  packed Q4_K bytes of the 128-row weight tile per K step -- each row's superblock
 //           header (16 B) and the 32 qs bytes of its 64-weight chunk -- brought in by TMA (3D maps
 //           over [expert, row, byte]) several steps ahead, when every row starts on a superblock
 //           (K % 256 == 0); otherwise the dequant threads load the bytes themselves.
-//   A ring  the dequantized bf16 weight tile(s), 128-byte swizzled (the MMA's A operand)
-//   B ring  the bf16 token tile (BN x 64, 128-byte swizzle) by TMA (the MMA's B operand)
+//   B ring  the bf16 token tile (up to 192 x 64, 128-byte swizzle) by TMA in boxes of 64 tokens,
+//           only as many boxes as the tile has tokens (the MMA's B operand)
 // Warps:
 //   0       TMA producer of the B ring (and of the A operand in the dense form)
 //   1       TMEM allocator and the single MMA-issuing thread (tcgen05.mma kind::f16, M = 128)
-//   2-9     dequant: two groups of 128 threads taking alternate K steps, one thread per weight
-//           row; prmt + magic-exponent nibble decode, one exact bf16x2 subtract and one bf16x2
-//           FMA per weight pair, stores into the A ring
+//   2-9     dequant: warps 2-5 and 6-9 take alternate K steps; thread `lane` of warp w owns row
+//           32 (w % 4) + lane (the TMEM lanes its warp may write); prmt + magic-exponent nibble
+//           decode, one exact bf16x2 subtract and one bf16x2 FMA per weight pair, 32 columns per
+//           matrix stored with tcgen05.st
 //   10-13   epilogue: tcgen05.ld of the fp32 accumulators, SwiGLU x route weight, stores
 //   14      TMA producer of the P ring
 // Every wait is bounded (about one second); on a timeout the kernel records a code in *err and
@@ -38,7 +44,8 @@ namespace ck {
 namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int BN = 256;
+constexpr int BN = (int)GEMM_TILE_TOKENS;  // largest token tile (accumulator columns)
+constexpr int B_BOX = 64;                   // token rows per TMA box of the B ring
 constexpr int NDQ = 8;   // dequant warps (two groups of one thread per weight row)
 constexpr int NEPI = 4;  // epilogue warps
 constexpr int NTHREADS = (2 + NDQ + NEPI + 1) * 32;
@@ -47,25 +54,19 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int P_HDR = BM * 16;  // superblock headers of the tile's rows
 constexpr int P_QS = BM * 32;   // the qs bytes of the K step's chunk
 constexpr int W_EPI0 = 2 + NDQ, W_PTMA = 2 + NDQ + NEPI;
-// ring depths (A: dequantized tiles, B: token tiles, P: packed weights) for the dual (gate/up) and
-// single forms; the defaults fill the shared memory of one CTA per SM
-#ifndef CK_DUAL_AST
-#define CK_DUAL_AST 2
-#endif
+// shared-memory ring depths (B: token tiles, P: packed weights) for the dual (gate/up) and single
+// forms; the defaults fill the shared memory of one CTA per SM
 #ifndef CK_DUAL_BST
-#define CK_DUAL_BST 3
+#define CK_DUAL_BST 5
 #endif
 #ifndef CK_DUAL_PST
-#define CK_DUAL_PST 4
-#endif
-#ifndef CK_SINGLE_AST
-#define CK_SINGLE_AST 3
+#define CK_DUAL_PST 6
 #endif
 #ifndef CK_SINGLE_BST
-#define CK_SINGLE_BST 4
+#define CK_SINGLE_BST 6
 #endif
 #ifndef CK_SINGLE_PST
-#define CK_SINGLE_PST 6
+#define CK_SINGLE_PST 8
 #endif
 
 template <int DUAL, int DENSE, int PT>
@@ -77,31 +78,36 @@ struct Cfg {
     static constexpr int DENSE_ACC = 8;
     static constexpr int DENSE_TILE = 64;
     static constexpr int DENSE_B_BYTES = DENSE_TILE * BK * 2;
-    static constexpr int A_ST = DENSE ? 0 : (DUAL ? CK_DUAL_AST : CK_SINGLE_AST);
-    static constexpr int A_STAGE = NMAT * A_BYTES;
+    // tensor memory: accumulators first, then the A stages
+    static constexpr int ACC_COLS = DENSE ? 512 : NMAT * BN;
+    static constexpr int NBUF = (DENSE || DUAL) ? 1 : 2;
+    static constexpr int A_TCOLS = 32 * NMAT;  // one 64-wide K step of every matrix, bf16x2 per column
+    static constexpr int A_TOFF = NBUF * ACC_COLS;
+    static constexpr int A_ST = DENSE ? 0 : (512 - A_TOFF) / A_TCOLS;
+    static_assert(DENSE || (A_ST >= 2 && A_ST <= 4), "tensor-memory A stages");
     static constexpr int B_ST = DENSE ? 6 : (DUAL ? CK_DUAL_BST : CK_SINGLE_BST);
     static constexpr int B_STAGE = DENSE ? A_BYTES + DENSE_B_BYTES : B_BYTES;
     static constexpr int P_ST = (DENSE || !PT) ? 0 : (DUAL ? CK_DUAL_PST : CK_SINGLE_PST);
     static constexpr int P_STAGE = NMAT * (P_HDR + P_QS);
     // per epilogue warp, one 32-token x 32-row bf16 chunk of the output, token-major
     static constexpr int EPI_STAGE = 32 * 32 * 2;
-    static constexpr int A_OFF = 0;
-    static constexpr int B_OFF = A_ST * A_STAGE;
+    static constexpr int B_OFF = 0;
     static constexpr int P_OFF = B_OFF + B_ST * B_STAGE;
     static constexpr int EPI_OFF = P_OFF + P_ST * P_STAGE;
     static constexpr int BAR_OFF = EPI_OFF + (DENSE ? 0 : NEPI * EPI_STAGE);
-    static constexpr int ACC_COLS = DENSE ? 512 : NMAT * BN;
-    static constexpr int NBUF = 512 / ACC_COLS;
     static constexpr int SMEM = BAR_OFF + 512 + 1024;
+    static_assert(B_ST <= 8 && P_ST <= 8, "barrier arrays");
     static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct Tile {
     int g, xrow, orow, ntok;
 };
+// A tile longer than the largest token tile is cut to BN tokens by every role alike (the MMA
+// thread also records the error); the tile builders never make one.
 CK_DEV Tile load_tile(const int4 *tiles, int i) {
     int4 v = tiles[i];
-    return Tile{v.x, v.y, v.z, v.w};
+    return Tile{v.x, v.y, v.z, min(v.w, BN)};
 }
 
 // The packed fields one thread needs for one K step of one matrix: the superblock header
@@ -129,28 +135,22 @@ CK_DEV uint32_t deq_pair(uint32_t pp, int hi, __nv_bfloat162 ds2, __nv_bfloat162
     return *reinterpret_cast<const uint32_t *>(&w);
 }
 
-// Dequantize one 32-weight half of the 64-weight chunk into the 128-byte swizzled smem row `r` of
-// tile `a`: half 0 = sub-block 2c (low nibbles, k = 0..31), half 1 = sub-block 2c+1 (high
-// nibbles, k = 32..63).  16-byte chunk cc of the row holds k = 8cc .. 8cc+7 and sits at position
-// cc ^ (r & 7) (the 128-byte swizzle the MMA descriptor names).
-CK_DEV void dequant_half(const Packed &p, uint8_t *a, int r, int half) {
+// Dequantize one 32-weight half of the 64-weight chunk into 16 bf16x2 words in K order: half 0 =
+// sub-block 2c (low nibbles, k = 0..31), half 1 = sub-block 2c+1 (high nibbles, k = 32..63).
+CK_DEV void dequant_words(const Packed &p, int half, uint32_t *w) {
     const float d = f16_bits_to_float(p.hdr.x & 0xFFFF), dmin = f16_bits_to_float(p.hdr.x >> 16);
     int sc, mn;
     q4k_scale_min(p.hdr.y, p.hdr.z, p.hdr.w, 2 * p.c + half, sc, mn);
     const float ds = d * (float)sc, dm = dmin * (float)mn;  // both exact in fp32
     const __nv_bfloat162 ds2 = __floats2bfloat162_rn(ds, ds), ndm2 = __floats2bfloat162_rn(-dm, -dm);
-    uint8_t *row = a + r * 128;
-    const int sw = r & 7;
     const uint32_t qw[8] = {p.q0.x, p.q0.y, p.q0.z, p.q0.w, p.q1.x, p.q1.y, p.q1.z, p.q1.w};
 #pragma unroll
     for (int c4 = 0; c4 < 4; ++c4) {
         const uint32_t w0 = qw[2 * c4], w1 = qw[2 * c4 + 1];
-        uint4 o;
-        o.x = deq_pair(__byte_perm(w0, 0u, 0x4140), half, ds2, ndm2);
-        o.y = deq_pair(__byte_perm(w0, 0u, 0x4342), half, ds2, ndm2);
-        o.z = deq_pair(__byte_perm(w1, 0u, 0x4140), half, ds2, ndm2);
-        o.w = deq_pair(__byte_perm(w1, 0u, 0x4342), half, ds2, ndm2);
-        *reinterpret_cast<uint4 *>(row + (((c4 + 4 * half) ^ sw) << 4)) = o;
+        w[4 * c4 + 0] = deq_pair(__byte_perm(w0, 0u, 0x4140), half, ds2, ndm2);
+        w[4 * c4 + 1] = deq_pair(__byte_perm(w0, 0u, 0x4342), half, ds2, ndm2);
+        w[4 * c4 + 2] = deq_pair(__byte_perm(w1, 0u, 0x4140), half, ds2, ndm2);
+        w[4 * c4 + 3] = deq_pair(__byte_perm(w1, 0u, 0x4342), half, ds2, ndm2);
     }
 }
 
@@ -195,12 +195,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < 8; ++s) {
             mbar_init(&p_full[s], 1);
-            mbar_init(&p_empty[s], NDQ * 16);  // one dequant group per stage
+            mbar_init(&p_empty[s], DUAL ? NDQ * 32 : NDQ * 16);  // dequant threads per stage
             mbar_init(&b_full[s], 1);
             mbar_init(&b_empty[s], 1);
         }
         for (int s = 0; s < 4; ++s) {
-            mbar_init(&a_full[s], NDQ * 16);
+            mbar_init(&a_full[s], DUAL ? NDQ * 32 : NDQ * 16);
             mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -238,8 +238,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tma_load_2d(st, &tmap_a, &b_full[s], kb * BK, (u % nrt) * BM);
                         tma_load_2d(st + A_BYTES, &tmap_x, &b_full[s], (kb % nkx) * BK, t.xrow);
                     } else {
-                        mbar_arrive_expect_tx(&b_full[s], B_BYTES);
-                        tma_load_2d(st, &tmap_x, &b_full[s], kb * BK, p.xrow_is_orow ? t.orow : t.xrow);
+                        // only the boxes that hold the tile's tokens (the MMA reads round16(ntok))
+                        const int nbox = max(1, (min(t.ntok, BN) + B_BOX - 1) / B_BOX);
+                        const int row0 = p.xrow_is_orow ? t.orow : t.xrow;
+                        mbar_arrive_expect_tx(&b_full[s], (uint32_t)(nbox * B_BOX * BK * 2));
+                        for (int i = 0; i < nbox; ++i)
+                            tma_load_2d(st + i * B_BOX * BK * 2, &tmap_x, &b_full[s], kb * BK, row0 + i * B_BOX);
                     }
                 }
             }
@@ -285,11 +289,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            int it = 0, ut = 0;
+            // running ring positions and phases (no division in the loop); the B operand's
+            // descriptor is the stage's base descriptor plus 2 per 16-wide K slice (32 bytes)
+            int sb = 0, sa = 0, ut = 0;
+            uint32_t phb = 0, pha = 0;
             bool ok = true;
             const int chunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
+            const uint64_t bdesc0 = sdesc_k_sw128(smem_u32(smem + C::B_OFF) + (DENSE ? A_BYTES : 0));
+            const uint64_t adesc0 = sdesc_k_sw128(smem_u32(smem + C::B_OFF));  // dense form's A
+            const uint32_t atm0 = tmem_base + (uint32_t)C::A_TOFF;              // first A stage (TMEM)
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++ut) {
                 const Tile t = load_tile(p.tiles, u / nrt);
+                if (p.tiles[u / nrt].w > BN) atomicCAS(p.err, 0, 9);
                 int nmma = ((t.ntok + 15) / 16) * 16;
                 const int nmax = DENSE ? C::DENSE_TILE : BN;
                 nmma = nmma < 16 ? 16 : (nmma > nmax ? nmax : nmma);
@@ -299,32 +310,35 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!mbar_wait_bounded(&acc_empty[ab], aph ^ 1u, p.err, 2)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int sb = it % C::B_ST;
-                    const uint32_t phb = (uint32_t)(it / C::B_ST) & 1u;
-                    const int sa = DENSE ? 0 : it % C::A_ST;
-                    const uint32_t pha = DENSE ? 0u : (uint32_t)(it / C::A_ST) & 1u;
+                for (int kb = 0; kb < nk; ++kb) {
                     if ((!DENSE && !mbar_wait_bounded(&a_full[sa], pha, p.err, 3)) ||
                         !mbar_wait_bounded(&b_full[sb], phb, p.err, 4)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t bst = smem_u32(smem + C::B_OFF + sb * C::B_STAGE);
-                    const uint32_t a0 = DENSE ? bst : smem_u32(smem + C::A_OFF + sa * C::A_STAGE);
-                    const uint32_t b0 = DENSE ? bst + A_BYTES : bst;
-                    // dense form: K chunk kb / chunk accumulates into its own accumulator
-                    const uint32_t dd = DENSE ? d0 + (uint32_t)((kb / chunk) * C::DENSE_TILE) : d0;
-                    const int kfirst = DENSE ? kb % chunk : kb;
+                    const uint64_t bd = bdesc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
+                    if constexpr (DENSE) {
+                        // K chunk kb / chunk accumulates into its own accumulator
+                        const uint32_t dd = d0 + (uint32_t)((kb / chunk) * C::DENSE_TILE);
+                        const int kfirst = kb % chunk;
+                        const uint64_t ad = adesc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        const uint64_t bd = sdesc_k_sw128(b0 + k * 32);
-                        const uint32_t acc = (kfirst | k) != 0;
-                        umma_bf16(dd, sdesc_k_sw128(a0 + k * 32), bd, idesc, acc);
-                        if (DUAL) umma_bf16(d0 + BN, sdesc_k_sw128(a0 + A_BYTES + k * 32), bd, idesc, acc);
+                        for (int k = 0; k < BK / 16; ++k)
+                            umma_bf16(dd, ad + 2 * k, bd + 2 * k, idesc, (kfirst | k) != 0);
+                    } else {
+                        const uint32_t at = atm0 + (uint32_t)(sa * C::A_TCOLS);
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k) {
+                            const uint32_t acc = (kb | k) != 0;
+                            umma_bf16_ts(d0, at + 8 * k, bd + 2 * k, idesc, acc);
+                            if (DUAL) umma_bf16_ts(d0 + BN, at + 32 + 8 * k, bd + 2 * k, idesc, acc);
+                        }
+                        umma_commit(&a_empty[sa]);
+                        if (++sa == C::A_ST) { sa = 0; pha ^= 1u; }
                     }
-                    if (!DENSE) umma_commit(&a_empty[sa]);
                     umma_commit(&b_empty[sb]);
+                    if (++sb == C::B_ST) { sb = 0; phb ^= 1u; }
                 }
                 if (!ok) break;
                 umma_commit(&acc_full[ab]);
@@ -335,93 +349,96 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp < W_EPI0 && !DENSE) {
         // ------------------------------------------------------------ dequant producers
-        // 256 threads in two groups of 128; thread i owns row (i & 127) of the tile and group
-        // i >> 7 takes every other K step (items it with it % 2 == group), converting the whole
-        // 64-weight chunk of its row in every matrix.  Two stages are in flight at once and each
-        // thread's barrier waits and proxy fence are spread over 64 x NMAT weights.
-        const int di = threadIdx.x - 64;
-        const int r = di & (BM - 1);
-        const int grp = di >> 7;
-        if constexpr (PT && !DENSE) {
-            int it = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    if ((it & 1) != grp) continue;
-                    const int sp = it % C::P_ST, sa = it % C::A_ST;
-                    const uint32_t php = (uint32_t)(it / C::P_ST) & 1u, pha = (uint32_t)(it / C::A_ST) & 1u;
-                    if (!mbar_wait_bounded(&p_full[sp], php, p.err, 8) || !mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint8_t *ps = smem + C::P_OFF + sp * C::P_STAGE;
-                    uint8_t *a = smem + C::A_OFF + sa * C::A_STAGE;
-#pragma unroll
-                    for (int m = 0; m < C::NMAT; ++m) {
-                        const uint8_t *pm_ = ps + m * (P_HDR + P_QS);
+        // Warps 2-5 form group 0 and warps 6-9 group 1.  Dual form: group g converts matrix g
+        // (gate or up) of every K step, so a stage is ready one half-item after its slot frees --
+        // the dual form has only two A stages.  Single form: the groups take alternate K steps
+        // (items it with it % 2 == group) over its four stages, spreading each thread's waits and
+        // fences over the whole 64-weight chunk.  A warp may write only the 32 TMEM lanes of its
+        // sub-partition (warp % 4): thread `lane` owns weight row 32 (warp % 4) + lane and stores
+        // its 64-weight chunk of matrix m as 32 bf16x2 columns at A_TOFF + stage * A_TCOLS + 32 m.
+        if constexpr (!DENSE) {
+            const int sub = warp & 3;
+            const int r = 32 * sub + lane;
+            const int grp = (warp - 2) >> 2;
+            constexpr int ISTEP = DUAL ? 1 : 2;  // items between two of this thread's items
+            const int m = DUAL ? grp : 0;         // the matrix this thread converts
+            const uint32_t trow = tmem_base + ((uint32_t)(32 * sub) << 16) + (uint32_t)C::A_TOFF;
+            auto convert_store = [&](const Packed &pk, int sa, int m) {
+                uint32_t w[32];
+                dequant_words(pk, 0, w);
+                dequant_words(pk, 1, w + 16);
+                tmem_st32(trow + (uint32_t)(sa * C::A_TCOLS + 32 * m), w);
+            };
+            if constexpr (PT) {
+                int it = 0;
+                bool ok = true;
+                for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+                    for (int kb = 0; kb < nk; ++kb, ++it) {
+                        if (!DUAL && (it & 1) != grp) continue;
+                        const int sp = it % C::P_ST, sa = it % C::A_ST;
+                        const uint32_t php = (uint32_t)(it / C::P_ST) & 1u, pha = (uint32_t)(it / C::A_ST) & 1u;
+                        if (!mbar_wait_bounded(&p_full[sp], php, p.err, 8) ||
+                            !mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();  // after the MMAs that read this A stage
+                        const uint8_t *pm_ = smem + C::P_OFF + sp * C::P_STAGE + m * (P_HDR + P_QS);
                         Packed pk;
                         pk.hdr = *reinterpret_cast<const uint4 *>(pm_ + r * 16);
                         pk.q0 = *reinterpret_cast<const uint4 *>(pm_ + P_HDR + r * 32);
                         pk.q1 = *reinterpret_cast<const uint4 *>(pm_ + P_HDR + r * 32 + 16);
                         pk.c = kb & 3;
-                        dequant_half(pk, a + m * A_BYTES, r, 0);
-                        dequant_half(pk, a + m * A_BYTES, r, 1);
+                        convert_store(pk, sa, m);
+                        tmem_st_wait();
+                        // The proxy fence orders this thread's generic reads of the P stage before
+                        // the TMA that refills it: without it the TMA write (async proxy) may land
+                        // before the reads are done, even after the mbarrier release.
+                        fence_proxy_async_smem();
+                        tc_fence_before();
+                        mbar_arrive(&p_empty[sp]);
+                        mbar_arrive(&a_full[sa]);
                     }
-                    // One proxy fence orders both this thread's generic reads of the P stage
-                    // before the TMA that refills it and its generic writes of the A tile before
-                    // the MMA that reads it.  Without it the TMA write (async proxy) may land
-                    // before the reads are done, even after the mbarrier release.
-                    fence_proxy_async_smem();
-                    mbar_arrive(&p_empty[sp]);
-                    mbar_arrive(&a_full[sa]);
                 }
-            }
-        } else if constexpr (!DENSE) {
-            // rows that straddle superblocks: each thread loads the packed fields of its next own
-            // item (two items ahead) while it converts the current one
-            auto advance = [&](int &uu, int &kk) {
-                if (++kk == nk) {
-                    kk = 0;
-                    uu += gridDim.x;
-                }
-            };
-            auto load_item = [&](int uu, int kk, Packed (&pk)[C::NMAT]) {
-                const Tile t = load_tile(p.tiles, uu / nrt);
-                const int n0 = (uu % nrt) * BM;
-                const uint32_t row = min((uint32_t)(n0 + r), p.N - 1);
-                const bool shared = (uint32_t)t.g >= p.n_routed;
-                const uint64_t g = shared ? (uint64_t)(t.g - p.n_routed) : (uint64_t)t.g;
-#pragma unroll
-                for (int m = 0; m < C::NMAT; ++m) {
+            } else {
+                // rows that straddle superblocks: each thread loads the packed fields of its next
+                // own item (two items ahead) while it converts the current one
+                auto advance = [&](int &uu, int &kk) {
+                    if (++kk == nk) {
+                        kk = 0;
+                        uu += gridDim.x;
+                    }
+                };
+                auto load_item = [&](int uu, int kk, Packed &pk) {
+                    const Tile t = load_tile(p.tiles, uu / nrt);
+                    const int n0 = (uu % nrt) * BM;
+                    const uint32_t row = min((uint32_t)(n0 + r), p.N - 1);
+                    const bool shared = (uint32_t)t.g >= p.n_routed;
+                    const uint64_t g = shared ? (uint64_t)(t.g - p.n_routed) : (uint64_t)t.g;
                     const uint8_t *b = m ? (shared ? p.s1 : p.w1) : (shared ? p.s0 : p.w0);
-                    load_packed(pk[m], b + g * p.w_stride, (uint64_t)row * p.K + (uint64_t)kk * BK);
+                    load_packed(pk, b + g * p.w_stride, (uint64_t)row * p.K + (uint64_t)kk * BK);
+                };
+                Packed cur, nxt;
+                int u = blockIdx.x, kb = 0, it = DUAL ? 0 : grp;
+                if (it) advance(u, kb);
+                if (u < nunits) load_item(u, kb, nxt);
+                while (u < nunits) {
+                    cur = nxt;
+                    int nu = u, nkb = kb;
+                    for (int i = 0; i < ISTEP; ++i) advance(nu, nkb);
+                    if (nu < nunits) load_item(nu, nkb, nxt);
+                    const int sa = it % C::A_ST;
+                    const uint32_t pha = (uint32_t)(it / C::A_ST) & 1u;
+                    if (!mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) break;
+                    tc_fence_after();
+                    convert_store(cur, sa, m);
+                    tmem_st_wait();
+                    tc_fence_before();
+                    mbar_arrive(&a_full[sa]);
+                    it += ISTEP;
+                    u = nu;
+                    kb = nkb;
                 }
-            };
-            Packed cur[C::NMAT], nxt[C::NMAT];
-            int u = blockIdx.x, kb = 0, it = grp;
-            if (grp) advance(u, kb);
-            if (u < nunits) load_item(u, kb, nxt);
-            while (u < nunits) {
-#pragma unroll
-                for (int m = 0; m < C::NMAT; ++m) cur[m] = nxt[m];
-                int nu = u, nkb = kb;
-                advance(nu, nkb);
-                advance(nu, nkb);
-                if (nu < nunits) load_item(nu, nkb, nxt);
-                const int sa = it % C::A_ST;
-                const uint32_t pha = (uint32_t)(it / C::A_ST) & 1u;
-                if (!mbar_wait_bounded(&a_empty[sa], pha ^ 1u, p.err, 5)) break;
-                uint8_t *a = smem + C::A_OFF + sa * C::A_STAGE;
-#pragma unroll
-                for (int m = 0; m < C::NMAT; ++m) {
-                    dequant_half(cur[m], a + m * A_BYTES, r, 0);
-                    dequant_half(cur[m], a + m * A_BYTES, r, 1);
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(&a_full[sa]);
-                it += 2;
-                u = nu;
-                kb = nkb;
             }
         }
     } else if (warp >= W_EPI0 && warp < W_PTMA) {
@@ -584,7 +601,7 @@ static int launch_t(const GemmParams &p, cudaStream_t s) {
         attr = true;
     }
     CUtensorMap mx, ma;
-    int rc = make_map(&mx, p.x, p.x_rows, DENSE && p.kx ? p.kx : p.K, DENSE ? C::DENSE_TILE : BN);
+    int rc = make_map(&mx, p.x, p.x_rows, DENSE && p.kx ? p.kx : p.K, DENSE ? C::DENSE_TILE : B_BOX);
     if (rc) return rc;
     if (DENSE) {
         rc = make_map(&ma, p.a_dense, p.N, p.K, BM);
