@@ -1,0 +1,97 @@
+"""Expert parallelism over NCCL on two GPUs: the expert-parallel layer's output, ids and weights
+equal the single-GPU layer's bit for bit (each token row is computed by the same kernels in the
+same K order whichever tile it lands in, and the combine keeps the reference's order).
+
+Runs as two spawned ranks when the box has at least two GPUs; skipped otherwise.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SPECS = {
+    "dsv4": dict(hidden=1024, inter=512, n_experts=16, n_shared=1, nsel=4, mode=4, ngroups=4, topk_groups=2,
+                 wscale=2.5),
+    "softmax": dict(hidden=1024, inter=768, n_experts=8, n_shared=2, nsel=3, mode=3),
+}
+NTOK = 512
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank(rank, world, port, name, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from coherence_kernel_b200 import workloads
+    from coherence_kernel_b200.moe import ExpertParallelMoE, MoELayer, MoeSpec
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        spec = MoeSpec(**SPECS[name])
+        el = spec.n_experts // world
+        w = workloads.make_moe(spec, NTOK, seed=11, experts=list(range(rank * el, (rank + 1) * el)))
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        T = NTOK // world
+        x = t(w["x"][rank * T:(rank + 1) * T].view(np.int16))
+        lay = ExpertParallelMoE(spec, t(w["gate"]), t(w["up"]), t(w["down"]), t(w["s_gate"]), t(w["s_up"]),
+                                t(w["s_down"]), t(w["router"]), t(w["bias"]), max_tokens=T)
+        out, ids, wts, _ = lay(x)
+        lay.check()
+        outs = [torch.empty_like(out) for _ in range(world)]
+        idss = [torch.empty_like(ids) for _ in range(world)]
+        wtss = [torch.empty_like(wts) for _ in range(world)]
+        dist.all_gather(outs, out)
+        dist.all_gather(idss, ids)
+        dist.all_gather(wtss, wts)
+        torch.cuda.synchronize()
+        if rank == 0:
+            wf = workloads.make_moe(spec, NTOK, seed=11)
+            ref = MoELayer(spec, t(wf["gate"]), t(wf["up"]), t(wf["down"]), t(wf["s_gate"]), t(wf["s_up"]),
+                           t(wf["s_down"]), t(wf["router"]), t(wf["bias"]), max_tokens=NTOK)
+            rout, rids, rwts, _ = ref(t(wf["x"].view(np.int16)))
+            ref.status(NTOK)
+            same = (torch.equal(torch.cat(outs).view(torch.int16), rout.view(torch.int16)) and
+                    torch.equal(torch.cat(idss), rids) and torch.equal(torch.cat(wtss), rwts))
+            q.put(("ok" if same else "differs", lay.last_recv_rows))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put(("error", repr(e)))
+        raise
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("name", sorted(SPECS))
+def test_expert_parallel_matches_single_gpu(name):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, name, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    verdict, info = q.get(timeout=5)
+    assert verdict == "ok", info
