@@ -266,8 +266,10 @@ class ExpertParallelMoE:
         self.wts_dummy = torch.ones(1, dtype=torch.float32, device=dev)
         self.last_recv_rows = 0
 
-    def forward(self, x, out=None):
+    def forward(self, x, out=None, marks=None):
+        """`marks(name)` is called between phases (a benchmark records CUDA events there)."""
         sp, L, dist = self.spec, _lib.load(), self.dist
+        mark = marks or (lambda name: None)
         T, H, I, K, E = x.shape[0], sp.hidden, sp.inter, sp.nsel, sp.n_experts
         if T > self.max_tokens:
             raise ValueError("more tokens than the layer was sized for")
@@ -278,12 +280,15 @@ class ExpertParallelMoE:
         wts = torch.empty((T, K), dtype=torch.float32, device=dev)
         out = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         self.err.zero_()
+        mark("start")
         _lib.check(L.ck_moe_route(ctypes.byref(self._cfg), _ptr(x), T, _ptr(self.router_w), _ptr(self.bias),
                                   _ptr(self.logits), _ptr(ids), _ptr(wts), _ptr(self.route_ws),
                                   self.route_ws.numel(), st), "ck_moe_route")
+        mark("route")
         _lib.check(L.ck_moe_permute(_ptr(ids), _ptr(wts), _ptr(x), T, K, E, sp.n_shared, H, int(sp.mode == 4),
                                     _ptr(self.xp), _ptr(self.row_w), _ptr(self.pair_pos), _ptr(self.counts),
                                     _ptr(self.tiles), _ptr(self.ntiles), _ptr(self.perm_ws), st), "ck_moe_permute")
+        mark("permute")
         # shared expert(s) on the local tokens (rows A.. of xp), into y rows A + s*T ..
         if sp.n_shared:
             mb = sp.matrix_bytes
@@ -301,6 +306,7 @@ class ExpertParallelMoE:
                                                  1, 0, _ptr(hs), T, _ptr(ys), T, None, _ptr(self.sh_tiles),
                                                  _ptr(self.sh_ntiles), self.sh_tiles.shape[0], H, I, 0, _ptr(self.err),
                                                  st), "shared down")
+        mark("shared")
         recv_counts_e = torch.empty_like(self.counts)
         dist.all_to_all_single(recv_counts_e, self.counts, group=self.group)  # [src, local expert]
         sc, rc = ep_split_sizes(self.counts, recv_counts_e, self.world)
@@ -313,6 +319,7 @@ class ExpertParallelMoE:
                                    group=self.group)
         else:
             self.recv_w[:nrecv].fill_(1.0)
+        mark("dispatch")
         self.recv_e[:nrecv] = ep_recv_local_experts(recv_counts_e, self.world, nrecv)
         # regroup by local expert (a stable counting sort), grouped GEMMs, restore arrival order
         if nrecv:
@@ -329,10 +336,13 @@ class ExpertParallelMoE:
                                              _ptr(self.ntiles2), self.mt2, H, I, 1, _ptr(self.err), st), "expert down")
             _lib.check(L.ck_gather_rows(_ptr(self.y2), _ptr(self.pair_pos2), _ptr(self.y_recv), nrecv, H * 2, st),
                        "restore order")
+        mark("experts")
         dist.all_to_all_single(self.y[:A], self.y_recv[:nrecv], output_split_sizes=sc, input_split_sizes=rc,
                                group=self.group)
+        mark("return")
         _lib.check(L.ck_moe_combine(_ptr(self.y), _ptr(ids), _ptr(wts), _ptr(self.pair_pos), T, K, sp.n_shared, H,
                                     int(sp.mode == 3), _ptr(out), None, st), "combine")
+        mark("combine")
         return out, ids, wts, self.counts
 
     __call__ = forward
