@@ -90,6 +90,150 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _graph_us(torch, fn, reps, copies):
+    """Device time of one call of fn(i), i cycling over `copies` weight copies, from a CUDA graph of
+    `reps` back-to-back calls (host launch overhead excluded)."""
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        fn(0)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                fn(i % copies)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(5):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) * 1e3 / (5 * reps)
+
+
+def _roof(bound, achieved, peak, unit):
+    return {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": unit, "frac": round(achieved / peak, 4)}
+
+
+def zipf_bias(rng, spec, slope=1.1, c=1.0):
+    """A per-expert selection bias c*log(p(rank)), p(rank) ~ rank^-slope over a seeded ranking."""
+    rank = rng.permutation(spec.n_experts) + 1
+    p = rank.astype(np.float64) ** -slope
+    return (c * np.log(p / p.sum())).astype(np.float32)
+
+
+def sub_benchmarks(torch, dev, hbm, tc_burst):
+    """The other configurations on one GPU: Q8_0 decode matvec 4096^2, Q4_K prefill 11008x4096 at
+    each M, the small MoE layer, and the decode-shaped sweep (dense stand-in + the DSv3 layer at
+    batch 1, 4, 16, 64 with Zipf(1.1) expert load).  Small kernels are timed as CUDA-graph replays
+    over rotating weight copies (more bytes than L2)."""
+    from coherence_kernel_b200 import ops, synth, workloads
+    from coherence_kernel_b200.moe import MoELayer
+    out = {}
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    # config 1: Q8_0 matvec 4096 x 4096
+    R = C = 4096
+    q8 = [t(synth.make_q8_0(np.random.default_rng([0, i]), R * C)) for i in range(16)]
+    x = t(np.random.default_rng(1).standard_normal(C).astype(np.float32))
+    y = torch.empty(R, device=dev)
+    us = _graph_us(torch, lambda i: ops.q8_0_matvec(q8[i], x, R, C, out=y), 64, 16)
+    nb = R * C // 32 * 34 + 4 * (R + C)
+    out["q8_0_matvec_4096"] = {"us": round(us, 2), "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
+    del q8
+    # dense decode stand-in: Q4_K matvec 7168 x 7168
+    R = C = 7168
+    q4 = [t(synth.make_q4k(np.random.default_rng([2, i]), R * C)) for i in range(16)]
+    x = t(np.random.default_rng(3).standard_normal(C).astype(np.float32))
+    y = torch.empty(R, device=dev)
+    us = _graph_us(torch, lambda i: ops.q4k_matvec(q4[i], x, R, C, out=y), 64, 16)
+    nb = R * C // 256 * 144 + 4 * (R + C)
+    out["q4k_matvec_7168"] = {"us": round(us, 2), "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
+    dense_us = us
+    # config 2: Q4_K prefill 11008 x 4096
+    R, C = workloads.Q4K_PREFILL
+    qp = [t(synth.make_q4k(np.random.default_rng([4, i]), R * C)) for i in range(8)]
+    wbytes = R * C // 256 * 144
+    for M in workloads.Q4K_PREFILL_M:
+        xb = t(synth.make_bf16(np.random.default_rng([5, M]), (M, C)).view(np.int16))
+        gs = [ops.Q4KGemm(q, R, C, max_tokens=M) for q in qp]
+        yb = torch.empty((M, R), dtype=torch.bfloat16, device=dev)
+        us = _graph_us(torch, lambda i: gs[i](xb, out=yb), 16 if M >= 512 else 32, 8)
+        nb, fl = wbytes + 2 * M * (R + C), 2.0 * M * R * C
+        e = {"M": M, "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "gbs": round(nb / us / 1e3, 1)}
+        e["roofline"] = (_roof("hbm", nb / us / 1e3, hbm, "GB/s") if M <= 64
+                         else _roof("tensor", fl / us / 1e6, tc_burst, "TFLOP/s"))
+        if M == 1:  # the decode matvec on the same weights (fp32 x, fp32 y)
+            xf = torch.randn(C, device=dev)
+            yf = torch.empty(R, device=dev)
+            us1 = _graph_us(torch, lambda i: ops.q4k_matvec(qp[i], xf, R, C, out=yf), 32, 8)
+            e["matvec_us"] = round(us1, 2)
+            e["matvec_roofline"] = _roof("hbm", (wbytes + 4 * (R + C)) / us1 / 1e3, hbm, "GB/s")
+        out[f"q4k_prefill_M{M}"] = e
+    del qp
+    # config 3: the small MoE layer, 4096 tokens
+    sp, T = workloads.MOE_SMALL, workloads.MOE_SMALL_TOKENS
+    w = workloads.make_moe(sp, T, seed=0)
+    lay = MoELayer(sp, t(w["gate"]), t(w["up"]), t(w["down"]), t(w["s_gate"]), t(w["s_up"]), t(w["s_down"]),
+                   t(w["router"]), t(w["bias"]), T)
+    xx = t(w["x"].view(np.int16))
+    o = torch.empty((T, sp.hidden), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        lay(xx, out=o)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(20):
+        lay(xx, out=o)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / 20
+    fl = T * sp.flops_per_token()
+    out["moe_small_4096"] = {"ms": round(ms, 4), "tokens_per_s": round(T / ms * 1e3, 1),
+                             "roofline": _roof("tensor", fl / ms / 1e9, tc_burst, "TFLOP/s")}
+    del lay, w
+    # config 5: decode sweep -- four dense 7168^2 Q4_K matvecs + the DSv3 layer at batch b, with a
+    # Zipf(1.1) expert load from a seeded selection bias
+    sp = workloads.MOE_DSV3
+    w = workloads.make_moe(sp, 64, seed=0)
+    zb = zipf_bias(np.random.default_rng(7), sp)
+    bias = t(w["bias"] + zb)
+    lay = MoELayer(sp, t(w["gate"]), t(w["up"]), t(w["down"]), t(w["s_gate"]), t(w["s_up"]), t(w["s_down"]),
+                   t(w["router"]), bias, 64)
+    sweep = {}
+    for bsz in (1, 4, 16, 64):
+        xx = t(w["x"][:bsz].view(np.int16))
+        o = torch.empty((bsz, sp.hidden), dtype=torch.bfloat16, device=dev)
+
+        def step(k):
+            for j in range(4):
+                ops.q4k_matvec(q4[(4 * k + j) % 16], x, 7168, 7168, out=y)
+            return lay(xx, out=o)
+        for k in range(3):
+            step(k)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for k in range(20):
+            step(k)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / 20
+        _, ids, _, _ = step(0)
+        U = len(set(ids.cpu().numpy().reshape(-1).tolist()))
+        nb = 4 * (7168 * 7168 // 256 * 144) + (U + 1) * 3 * sp.matrix_bytes
+        sweep[f"b{bsz}"] = {"us_per_step": round(us, 1), "experts_touched": U, "bytes_per_token": nb // bsz,
+                            "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
+    out["decode_sweep"] = {"steps": sweep, "dense_matvec_us": round(dense_us, 2),
+                           "zipf": "selection bias log(rank^-1.1), seeded ranking"}
+    del lay, w, q4
+    torch.cuda.synchronize()
+    return out
+
+
 def cpu_baseline(spec, w, tokens=2):
     """The oracle (fp64 C restatement of the reference's Form recipes) on a bounded sample: `tokens`
     whole tokens of the layer, one per host thread."""
@@ -157,6 +301,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ck", choices=["ck", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="skip the other configurations' sub-benchmarks")
     ap.add_argument("--shard", type=int, default=1,
                     help="run one GPU's share of an N-way expert-parallel layer on one GPU (256/N experts, "
                          "8192/N tokens): the small case a profiler capture uses")
@@ -297,6 +442,11 @@ def main():
         e2e = {"value": T_all / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(xh.numel() * 2),
                "d2h_bytes_per_step": int(oh.numel() * 2), "ms_per_step": round(e_ms, 4)}
 
+    subs = None
+    if world == 1 and args.shard == 1 and not args.no_sub:
+        del layer, wg, wu, wd
+        torch.cuda.empty_cache()
+        subs = sub_benchmarks(torch, dev, hbm, tc_burst)
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -316,6 +466,7 @@ def main():
                 "algorithmic_tflops": round(T_all * spec.flops_per_token() / (ms_step / 1e3) / 1e12, 1),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "router_exact_tokens": flagged,
+                "sub_benchmarks": subs,
                 "gpu_launches": launches_per_step * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
