@@ -27,6 +27,10 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "Q4_K MoE-layer tokens/s + weight-stream HBM GB/s at 1/2/4/8 B200 vs roofline"
+# DRAM bytes of one grouped gate/up launch per routed-or-shared token row, from an ncu capture of
+# the reduced layer (32 routed + 1 shared experts, 1024 tokens: 798.3 MB over 9216 rows); the
+# traffic grows with the rows processed, so a launch over R rows moves about R times this.
+GATEUP_DRAM_BYTES_PER_ROW = 86_620
 WORKLOAD = "dsv3-moe-layer: 256 routed + 1 shared Q4_K SwiGLU experts, hidden 7168, inter 2048, top-8 of 4/8 groups"
 
 
@@ -234,19 +238,25 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
     return out
 
 
-def cpu_baseline(spec, w, tokens=2):
-    """The oracle (fp64 C restatement of the reference's Form recipes) on a bounded sample: `tokens`
-    whole tokens of the layer, one per host thread."""
+def cpu_baseline(spec, w, target_s=12.0):
+    """The oracle (fp64 C restatement of the reference's Form recipes) on a bounded sample of whole
+    tokens of the layer, one token per host thread at a time: one token per thread first to size
+    the sample, then enough tokens per thread for about `target_s` seconds of work."""
     from oracle import oracle as O
     cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
                     spec.topk_groups, spec.wscale)
-    toks = np.arange(tokens)
+    nth = max(1, min(os.cpu_count() or 1, 16))
     t0 = time.perf_counter()
-    O.moe_layer(cfg, w, w["x"], toks, nthreads=tokens)
+    O.moe_layer(cfg, w, w["x"], np.arange(nth), nthreads=nth)
+    per = time.perf_counter() - t0
+    k = int(max(1, min(64, target_s / max(per, 1e-3))))
+    toks = np.arange(nth, nth + nth * k) % w["x"].shape[0]
+    t0 = time.perf_counter()
+    O.moe_layer(cfg, w, w["x"], toks, nthreads=nth)
     dt = time.perf_counter() - t0
-    return {"value": tokens / dt, "unit": "tokens/s", "cores": tokens, "kind": "port",
-            "sample": f"{tokens} tokens of the layer end to end (router over 256 experts, 8 routed + 1 shared "
-                      f"SwiGLU experts, combine) on the oracle, one token per thread, {dt:.1f} s"}
+    return {"value": len(toks) / dt, "unit": "tokens/s", "cores": nth, "kind": "port",
+            "sample": f"{len(toks)} tokens of the layer end to end (router over 256 experts, 8 routed + 1 "
+                      f"shared SwiGLU experts, combine) on the oracle, {nth} host threads, {dt:.1f} s"}
 
 
 def run_reference(args, rank, world):
@@ -414,7 +424,7 @@ def main():
         flops_gu = 2.0 * (A + spec.n_shared * T) * 2 * spec.inter * spec.hidden
         ach = flops_gu / (gu_ms / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_sust, "unit": "TFLOP/s",
-                "frac": round(ach / tc_sust, 4), "traffic": None,
+                "frac": round(ach / tc_sust, 4), "traffic": int(GATEUP_DRAM_BYTES_PER_ROW * (A + spec.n_shared * T)),
                 "kernel": "k_gemm_q4k<1> (grouped gate/up GEMM + SwiGLU)", "peak_source": f"{peak_src} sustained",
                 "kernel_ms": round(gu_ms, 4), "down_ms": round(sum(dn) / len(dn), 4),
                 "step_split_ms": {k: round(sum(r[b].elapsed_time(r[k]) for r in evs) / len(evs), 4)
@@ -450,7 +460,7 @@ def main():
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(spec, {k: w[k] for k in w}, tokens=2) if len(experts) == spec.n_experts else None
+            cpu = cpu_baseline(spec, {k: w[k] for k in w}) if len(experts) == spec.n_experts else None
         # our kernels per step: route 6 (split, tiles, logits GEMM, select, exact logits, exact
         # select), permute 3, GEMM 2, combine 1; expert-parallel adds the shared tiles + 2 GEMMs per
         # shared expert, the regroup permute 3 and the row restore 1
