@@ -264,6 +264,7 @@ class ExpertParallelMoE:
         self.y2 = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
         self.y_recv = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
         self.wts_dummy = torch.ones(1, dtype=torch.float32, device=dev)
+        self.side = torch.cuda.Stream(device=dev)  # the shared expert, beside the dispatch
         self.last_recv_rows = 0
 
     def forward(self, x, out=None, marks=None):
@@ -289,10 +290,21 @@ class ExpertParallelMoE:
                                     _ptr(self.xp), _ptr(self.row_w), _ptr(self.pair_pos), _ptr(self.counts),
                                     _ptr(self.tiles), _ptr(self.ntiles), _ptr(self.perm_ws), st), "ck_moe_permute")
         mark("permute")
-        # shared expert(s) on the local tokens (rows A.. of xp), into y rows A + s*T ..
+        # the counts first: the host waits for the split sizes only behind route and permute
+        recv_counts_e = torch.empty_like(self.counts)
+        dist.all_to_all_single(recv_counts_e, self.counts, group=self.group)  # [src, local expert]
+        sc, rc = ep_split_sizes(self.counts, recv_counts_e, self.world)
+        nrecv = int(sum(rc))
+        self.last_recv_rows = nrecv
+        # shared expert(s) on the local tokens (rows A.. of xp, into y rows A + s*T ..) on a side
+        # stream, overlapping the dispatch and the expert GEMMs; the combine waits for it
+        main = torch.cuda.current_stream()
+        side_done = None
         if sp.n_shared:
+            self.side.wait_stream(main)
+            sst = ctypes.c_void_p(self.side.cuda_stream)
             mb = sp.matrix_bytes
-            _lib.check(L.ck_token_tiles(_ptr(self.sh_tiles), _ptr(self.sh_ntiles), T, st), "ck_token_tiles")
+            _lib.check(L.ck_token_tiles(_ptr(self.sh_tiles), _ptr(self.sh_ntiles), T, sst), "ck_token_tiles")
             for s in range(sp.n_shared):
                 xs = self.xp[A:A + T]
                 hs = self.h_sh[s * T:(s + 1) * T]
@@ -301,17 +313,14 @@ class ExpertParallelMoE:
                                                  ctypes.c_void_p(self.s[1].data_ptr() + s * mb), None, None, 0, 1, 0,
                                                  _ptr(xs), T, _ptr(hs), T, None, _ptr(self.sh_tiles),
                                                  _ptr(self.sh_ntiles), self.sh_tiles.shape[0], I, H, 0, _ptr(self.err),
-                                                 st), "shared gate/up")
+                                                 sst), "shared gate/up")
                 _lib.check(L.ck_moe_expert_gemm(0, ctypes.c_void_p(self.s[2].data_ptr() + s * mb), None, None, None, 0,
                                                  1, 0, _ptr(hs), T, _ptr(ys), T, None, _ptr(self.sh_tiles),
                                                  _ptr(self.sh_ntiles), self.sh_tiles.shape[0], H, I, 0, _ptr(self.err),
-                                                 st), "shared down")
+                                                 sst), "shared down")
+            side_done = torch.cuda.Event()
+            side_done.record(self.side)
         mark("shared")
-        recv_counts_e = torch.empty_like(self.counts)
-        dist.all_to_all_single(recv_counts_e, self.counts, group=self.group)  # [src, local expert]
-        sc, rc = ep_split_sizes(self.counts, recv_counts_e, self.world)
-        nrecv = int(sum(rc))
-        self.last_recv_rows = nrecv
         dist.all_to_all_single(self.recv_x[:nrecv], self.xp[:A], output_split_sizes=rc, input_split_sizes=sc,
                                group=self.group)
         if sp.mode == 4:
@@ -340,6 +349,8 @@ class ExpertParallelMoE:
         dist.all_to_all_single(self.y[:A], self.y_recv[:nrecv], output_split_sizes=sc, input_split_sizes=rc,
                                group=self.group)
         mark("return")
+        if side_done is not None:
+            main.wait_event(side_done)
         _lib.check(L.ck_moe_combine(_ptr(self.y), _ptr(ids), _ptr(wts), _ptr(self.pair_pos), T, K, sp.n_shared, H,
                                     int(sp.mode == 3), _ptr(out), None, st), "combine")
         mark("combine")
