@@ -20,8 +20,8 @@ int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows
                       cudaStream_t s);
 int launch_q80_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
 // HBM-streaming decode matvec (gemv_stream.cu): kind 12 = Q4_K, 8 = Q8_0; cols % 256 == 0,
-// cols <= 8192, weights 16-byte aligned
-bool gemv_stream_ok(const void *qb, uint32_t cols);
+// cols <= 8192, weights and x 16-byte aligned
+bool gemv_stream_ok(const void *qb, const float *x, uint32_t cols);
 int launch_gemv_stream(int kind, const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols,
                        cudaStream_t s);
 int launch_f16_matvec(const uint16_t *w, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);

@@ -290,7 +290,7 @@ int launch_matvec_ordered(int kind, const uint8_t *qb, const float *x, float *y,
 int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
                       cudaStream_t s) {
     if (cols % 64 != 0) return CK_ERR_SHAPE;
-    if (ntok == 1 && gemv_stream_ok(qb, cols)) {
+    if (ntok == 1 && gemv_stream_ok(qb, x, cols)) {
         return launch_gemv_stream(12, qb, x, y, rows, cols, s);
     } else if (ntok == 1) {
         k_q4k_matvec_fast<1><<<dim3(nblk(rows, 8), 1), 256, 0, s>>>(qb, x, y, rows, cols, 1);
@@ -301,7 +301,7 @@ int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows
 }
 int launch_q80_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s) {
     if (cols % 32 != 0) return CK_ERR_SHAPE;
-    if (gemv_stream_ok(qb, cols)) {
+    if (gemv_stream_ok(qb, x, cols)) {
         return launch_gemv_stream(8, qb, x, y, rows, cols, s);
     } else if (cols % 256 == 0 && (size_t)cols / 32 * Q80_BYTES * 8 <= 200 * 1024) {
         size_t smem = (size_t)cols / 32 * Q80_BYTES * 8;

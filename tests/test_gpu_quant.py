@@ -66,7 +66,8 @@ def test_matvec_golden():
         assert np.all(np.abs(yo - y) <= (2 * c + 1) * U * b)
 
 
-@pytest.mark.parametrize("rows,cols", [(4096, 4096), (512, 1408), (7168, 7168), (300, 2048)])
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (512, 1408), (7168, 7168), (300, 2048), (1000, 256), (777, 768),
+                                       (130, 8192), (5, 512)])
 def test_q4k_matvec_sizes(rows, cols):
     rng = np.random.default_rng(rows + cols)
     q = synth.make_q4k(rng, rows * cols)
@@ -80,7 +81,8 @@ def test_q4k_matvec_sizes(rows, cols):
         assert abs(y[r] - ref) <= 1e-3 * np.abs(w * x).sum(), r
 
 
-@pytest.mark.parametrize("rows,cols", [(4096, 4096), (64, 96), (1000, 2048)])
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (64, 96), (1000, 2048), (999, 256), (513, 7168), (64, 8192),
+                                       (3, 1280)])
 def test_q8_0_matvec_sizes(rows, cols):
     rng = np.random.default_rng(rows * 7 + cols)
     q = synth.make_q8_0(rng, rows * cols)
