@@ -200,13 +200,44 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
                              "roofline": _roof("tensor", fl / ms / 1e9, tc_burst, "TFLOP/s")}
     del lay, w
     # config 5: decode sweep -- four dense 7168^2 Q4_K matvecs + the DSv3 layer at batch b, with a
-    # Zipf(1.1) expert load from a seeded selection bias
+    # Zipf(1.1) expert load from a seeded selection bias c*log(p(rank)); c is calibrated on 4096
+    # routed tokens so that the measured rank/frequency slope is -1.1
     sp = workloads.MOE_DSV3
-    w = workloads.make_moe(sp, 64, seed=0)
-    zb = zipf_bias(np.random.default_rng(7), sp)
-    bias = t(w["bias"] + zb)
+    ncal = 4096
+    w = workloads.make_moe(sp, ncal, seed=0)
+    base = w["bias"].copy()
+    bias = t(base)
     lay = MoELayer(sp, t(w["gate"]), t(w["up"]), t(w["down"]), t(w["s_gate"]), t(w["s_up"]), t(w["s_down"]),
-                   t(w["router"]), bias, 64)
+                   t(w["router"]), bias, ncal)
+    xcal = t(w["x"].view(np.int16))
+
+    def slope_for(c):
+        # log-log fit of load against rank over the experts that drew >= 8 of the tokens (the
+        # ranks below that are counting noise at this sample size)
+        bias.copy_(t(base + zipf_bias(np.random.default_rng(7), sp, c=c)))
+        counts = lay(xcal)[3].cpu().numpy()
+        cnt = np.sort(counts)[::-1].astype(np.float64)
+        r = np.arange(1, cnt.size + 1, dtype=np.float64)[cnt >= 8]
+        cnt = cnt[cnt >= 8]
+        return float(np.polyfit(np.log(r), np.log(cnt), 1)[0])
+    # the first c on a rising grid whose slope passes -1.1, then bisection inside that step
+    lo, hi = 0.0, None
+    for c in np.arange(0.125, 6.01, 0.125):
+        if slope_for(float(c)) <= -1.1:
+            hi = float(c)
+            break
+        lo = float(c)
+    if hi is None:
+        hi = lo
+    for _ in range(8):
+        mid = 0.5 * (lo + hi)
+        if slope_for(mid) > -1.1:
+            lo = mid
+        else:
+            hi = mid
+    zipf_c = 0.5 * (lo + hi)
+    zipf_slope = slope_for(zipf_c)
+    del xcal
     sweep = {}
     for bsz in (1, 4, 16, 64):
         xx = t(w["x"][:bsz].view(np.int16))
@@ -232,7 +263,9 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
         sweep[f"b{bsz}"] = {"us_per_step": round(us, 1), "experts_touched": U, "bytes_per_token": nb // bsz,
                             "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
     out["decode_sweep"] = {"steps": sweep, "dense_matvec_us": round(dense_us, 2),
-                           "zipf": "selection bias log(rank^-1.1), seeded ranking"}
+                           "zipf": {"bias": "c*log(rank^-1.1), seeded ranking", "c": round(zipf_c, 3),
+                                    "measured_slope": round(zipf_slope, 3), "tokens": ncal,
+                                    "fit": "log load vs log rank over experts with >= 8 tokens"}}
     del lay, w, q4
     torch.cuda.synchronize()
     return out
