@@ -175,32 +175,54 @@ def _align(n, a=256):
     return (n + a - 1) // a * a
 
 
-def ep_split_sizes(counts, recv_counts_e, world):
-    """Row counts of the dispatch all-to-all.  `counts` [E] is this rank's rows per (global) expert,
-    sorted by expert and therefore by destination rank (rank r owns experts r*E/W ..); after the
-    counts all-to-all, `recv_counts_e` [W * E/W] is, per source rank, its rows per local expert.
-    Returns (send sizes per destination, receive sizes per source) as Python lists."""
-    send = counts.view(world, -1).sum(dim=1)
-    recv = recv_counts_e.view(world, -1).sum(dim=1)
-    return send.tolist(), recv.tolist()
+def ep_dispatch_counts(ids, el, world):
+    """The sizes of the deduplicated dispatch.  A token crosses to each rank that holds at least one
+    of its experts once, however many of them live there.  Returns (destination rank of every slot
+    [T, K], the token/rank incidence [T, W] bool, rows per destination rank [W], (token, slot)
+    pairs per destination rank [W])."""
+    er = torch.div(ids, el, rounding_mode="floor").long()
+    mask = torch.zeros((ids.shape[0], world), dtype=torch.bool, device=ids.device)
+    mask.scatter_(1, er, True)
+    return er, mask, mask.sum(0), torch.bincount(er.reshape(-1), minlength=world)
 
 
-def ep_recv_local_experts(recv_counts_e, world, nrecv):
-    """The local expert of every received row: each source's block arrives sorted by expert."""
-    el = recv_counts_e.numel() // world
-    eidx = torch.arange(el, device=recv_counts_e.device, dtype=torch.int32).repeat(world)
-    return torch.repeat_interleave(eidx, recv_counts_e.to(torch.int64), output_size=nrecv)
+def ep_dispatch_rows(ids, wts, er, mask, el, nrows):
+    """The rows of the deduplicated dispatch, in (destination rank, token) order: the source token
+    of every row [S] int32, the local expert of each of its slots [S, K] int32 (-1 where the slot's
+    expert lives on another rank) and the slots' route weights [S, K] (0 there).  `nrows` is the
+    row total, known on the host from the size exchange, so no step waits for the device."""
+    dt = torch.nonzero_static(mask.t(), size=nrows)
+    d, t = dt[:, 0], dt[:, 1]
+    sel = er[t] == d.unsqueeze(1)
+    me = torch.where(sel, ids[t].long() - (d * el).unsqueeze(1), torch.full_like(er[t], -1)).to(torch.int32)
+    mw = torch.where(sel, wts[t], torch.zeros_like(wts[t]))
+    return t.to(torch.int32), me, mw
+
+
+def ep_return_positions(ids, el):
+    """Where the return all-to-all leaves every (token, slot) pair's output row: the pairs sent to
+    rank d come back as one block, in (token, slot) order, and the blocks arrive in rank order --
+    the pairs' order after a stable sort by destination rank, so the position of a pair is its
+    index in that sort."""
+    er = torch.div(ids, el, rounding_mode="floor").reshape(-1)
+    order = torch.argsort(er, stable=True)
+    pos = torch.empty_like(order)
+    pos[order] = torch.arange(order.numel(), device=ids.device)
+    return pos.to(torch.int32)
 
 
 class ExpertParallelMoE:
     """The MoE layer with experts sharded over the ranks of a process group (one GPU per rank).
 
     Rank r holds experts [r*E/W, (r+1)*E/W) and a replica of the router and the shared expert(s).
-    Each rank routes its own tokens, sorts the (token, slot) pairs by expert -- which also sorts
-    them by destination rank -- and exchanges the rows with one all-to-all (NCCL over NVLink).
-    The receiver regroups the rows by local expert, runs the grouped GEMMs, restores the arrival
-    order and sends the rows back with a second all-to-all; the source combines in the
-    reference's order.  The shared expert runs on the local tokens.
+    Each rank routes its own tokens and sends every token once to each rank that holds at least
+    one of its experts (with group-limited routing a token reaches at most topk_groups ranks),
+    together with a small row naming the slots' local experts and weights; one all-to-all of the
+    activation rows and one of the metadata (NCCL over NVLink).  The receiver regroups the
+    (row, slot) pairs by local expert, runs the grouped GEMMs and returns every pair's output row,
+    in (row, slot) order, with a second all-to-all; the source combines them in the reference's
+    order, so the output equals the single-GPU layer's bit for bit.  The shared expert runs on
+    the local tokens on a side stream, beside the exchange.
     """
 
     def __init__(self, spec: MoeSpec, local_w_gate, local_w_up, local_w_down, s_gate, s_up, s_down, router_w, bias,
@@ -224,7 +246,7 @@ class ExpertParallelMoE:
         self.max_tokens = max_tokens
         self._cfg = sp.cfg()
         dev = router_w.device
-        T, K, H, I, E = max_tokens, sp.nsel, sp.hidden, sp.inter, sp.n_experts
+        T, K, H, I, E, W = max_tokens, sp.nsel, sp.hidden, sp.inter, sp.n_experts, self.world
         A = T * K
         L = _lib.load()
         self.dev = dev
@@ -232,46 +254,39 @@ class ExpertParallelMoE:
         self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
         self.route_ws = torch.empty(_align(L.ck_moe_route_workspace_bytes(ctypes.byref(self._cfg), T)),
                                     dtype=torch.uint8, device=dev)
-        self.xp = torch.empty((A + T, H), dtype=torch.bfloat16, device=dev)
-        self.row_w = torch.empty(A + sp.n_shared * T, dtype=torch.float32, device=dev)
-        self.pair_pos = torch.empty(A, dtype=torch.int32, device=dev)
-        self.counts = torch.empty(E, dtype=torch.int32, device=dev)
-        self.mt = L.ck_moe_max_tiles(T, K, E, sp.n_shared)
-        self.tiles = torch.empty((self.mt, 4), dtype=torch.int32, device=dev)
-        self.ntiles = torch.empty(1, dtype=torch.int32, device=dev)
-        self.perm_ws = torch.empty(_align(L.ck_moe_permute_workspace_bytes(T, K, E)), dtype=torch.uint8, device=dev)
+        self.send_x = torch.empty((T * min(W, K), H), dtype=torch.bfloat16, device=dev)
         self.y = torch.empty((A + sp.n_shared * T, H), dtype=torch.bfloat16, device=dev)
         self.h_sh = torch.empty((max(1, sp.n_shared) * T, I), dtype=torch.bfloat16, device=dev)
         self.sh_tiles = torch.empty((T // 16 + 2, 4), dtype=torch.int32, device=dev)
         self.sh_ntiles = torch.empty(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        # receiver side: at most every rank's pairs could land here
-        R = A * self.world
-        self.R = R
+        self.counts = torch.empty(E, dtype=torch.int32, device=dev)
+        # receiver side: every rank may send each of its tokens here once
+        R = T * W
         self.recv_x = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
-        self.recv_w = torch.empty(R, dtype=torch.float32, device=dev)
-        self.recv_e = torch.empty(R, dtype=torch.int32, device=dev)
-        self.xp2 = torch.empty((R + 1, H), dtype=torch.bfloat16, device=dev)
-        self.row_w2 = torch.empty(R + 1, dtype=torch.float32, device=dev)
-        self.pair_pos2 = torch.empty(R, dtype=torch.int32, device=dev)
+        self.recv_meta = torch.empty((R, 2 * K), dtype=torch.int32, device=dev)
+        P = R * K
+        self.xp2 = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
+        self.row_w2 = torch.empty(P, dtype=torch.float32, device=dev)
+        self.pair_pos2 = torch.empty(P, dtype=torch.int32, device=dev)
         self.counts2 = torch.empty(self.el, dtype=torch.int32, device=dev)
-        self.mt2 = L.ck_moe_max_tiles(R, 1, self.el, 0)
+        self.mt2 = L.ck_moe_max_tiles(R, K, self.el, 0)
         self.tiles2 = torch.empty((self.mt2, 4), dtype=torch.int32, device=dev)
         self.ntiles2 = torch.empty(1, dtype=torch.int32, device=dev)
-        self.perm_ws2 = torch.empty(_align(L.ck_moe_permute_workspace_bytes(R, 1, self.el)), dtype=torch.uint8,
+        self.perm_ws2 = torch.empty(_align(L.ck_moe_permute_workspace_bytes(R, K, self.el)), dtype=torch.uint8,
                                     device=dev)
-        self.h2 = torch.empty((R, I), dtype=torch.bfloat16, device=dev)
-        self.y2 = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
-        self.y_recv = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
-        self.wts_dummy = torch.ones(1, dtype=torch.float32, device=dev)
-        self.side = torch.cuda.Stream(device=dev)  # the shared expert, beside the dispatch
+        self.h2 = torch.empty((P, I), dtype=torch.bfloat16, device=dev)
+        self.y2 = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
+        self.y_recv = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
+        self.side = torch.cuda.Stream(device=dev)  # the shared expert, beside the exchange
         self.last_recv_rows = 0
+        self.last_recv_pairs = 0
 
     def forward(self, x, out=None, marks=None):
         """`marks(name)` is called between phases (a benchmark records CUDA events there)."""
         sp, L, dist = self.spec, _lib.load(), self.dist
         mark = marks or (lambda name: None)
-        T, H, I, K, E = x.shape[0], sp.hidden, sp.inter, sp.nsel, sp.n_experts
+        T, H, I, K, E, W = x.shape[0], sp.hidden, sp.inter, sp.nsel, sp.n_experts, self.world
         if T > self.max_tokens:
             raise ValueError("more tokens than the layer was sized for")
         A = T * K
@@ -286,18 +301,23 @@ class ExpertParallelMoE:
                                   _ptr(self.logits), _ptr(ids), _ptr(wts), _ptr(self.route_ws),
                                   self.route_ws.numel(), st), "ck_moe_route")
         mark("route")
-        _lib.check(L.ck_moe_permute(_ptr(ids), _ptr(wts), _ptr(x), T, K, E, sp.n_shared, H, int(sp.mode == 4),
-                                    _ptr(self.xp), _ptr(self.row_w), _ptr(self.pair_pos), _ptr(self.counts),
-                                    _ptr(self.tiles), _ptr(self.ntiles), _ptr(self.perm_ws), st), "ck_moe_permute")
+        # the sizes first: the host waits for them only behind the route
+        er, mask, srow, spair = ep_dispatch_counts(ids, self.el, W)
+        self.counts.copy_(torch.bincount(ids.reshape(-1), minlength=E))
+        sizes = torch.stack([srow, spair], dim=1).to(torch.int64)
+        rsizes = torch.empty_like(sizes)
+        dist.all_to_all_single(rsizes, sizes, group=self.group)  # [src, (rows, pairs)]
+        srow_l, spair_l, rrow_l, rpair_l = torch.cat([sizes.t(), rsizes.t()]).tolist()
+        S, R, P = int(sum(srow_l)), int(sum(rrow_l)), int(sum(rpair_l))
+        self.last_recv_rows, self.last_recv_pairs = R, P
+        # one row per (destination rank, token) with its slots' local experts and weights
+        send_tok, me, mw = ep_dispatch_rows(ids, wts, er, mask, self.el, S)
+        if S:
+            _lib.check(L.ck_gather_rows(_ptr(x), _ptr(send_tok), _ptr(self.send_x), S, H * 2, st), "dispatch rows")
+        meta = torch.cat([me, mw.view(torch.int32)], dim=1)
         mark("permute")
-        # the counts first: the host waits for the split sizes only behind route and permute
-        recv_counts_e = torch.empty_like(self.counts)
-        dist.all_to_all_single(recv_counts_e, self.counts, group=self.group)  # [src, local expert]
-        sc, rc = ep_split_sizes(self.counts, recv_counts_e, self.world)
-        nrecv = int(sum(rc))
-        self.last_recv_rows = nrecv
-        # shared expert(s) on the local tokens (rows A.. of xp, into y rows A + s*T ..) on a side
-        # stream, overlapping the dispatch and the expert GEMMs; the combine waits for it
+        # shared expert(s) on the local tokens, into y rows A + s*T .., on a side stream that
+        # overlaps the exchange and the expert GEMMs; the combine waits for it
         main = torch.cuda.current_stream()
         side_done = None
         if sp.n_shared:
@@ -306,12 +326,11 @@ class ExpertParallelMoE:
             mb = sp.matrix_bytes
             _lib.check(L.ck_token_tiles(_ptr(self.sh_tiles), _ptr(self.sh_ntiles), T, sst), "ck_token_tiles")
             for s in range(sp.n_shared):
-                xs = self.xp[A:A + T]
                 hs = self.h_sh[s * T:(s + 1) * T]
                 ys = self.y[A + s * T:A + (s + 1) * T]
                 _lib.check(L.ck_moe_expert_gemm(1, ctypes.c_void_p(self.s[0].data_ptr() + s * mb),
                                                  ctypes.c_void_p(self.s[1].data_ptr() + s * mb), None, None, 0, 1, 0,
-                                                 _ptr(xs), T, _ptr(hs), T, None, _ptr(self.sh_tiles),
+                                                 _ptr(x), T, _ptr(hs), T, None, _ptr(self.sh_tiles),
                                                  _ptr(self.sh_ntiles), self.sh_tiles.shape[0], I, H, 0, _ptr(self.err),
                                                  sst), "shared gate/up")
                 _lib.check(L.ck_moe_expert_gemm(0, ctypes.c_void_p(self.s[2].data_ptr() + s * mb), None, None, None, 0,
@@ -321,37 +340,38 @@ class ExpertParallelMoE:
             side_done = torch.cuda.Event()
             side_done.record(self.side)
         mark("shared")
-        dist.all_to_all_single(self.recv_x[:nrecv], self.xp[:A], output_split_sizes=rc, input_split_sizes=sc,
+        dist.all_to_all_single(self.recv_x[:R], self.send_x[:S], output_split_sizes=rrow_l, input_split_sizes=srow_l,
                                group=self.group)
-        if sp.mode == 4:
-            dist.all_to_all_single(self.recv_w[:nrecv], self.row_w[:A], output_split_sizes=rc, input_split_sizes=sc,
-                                   group=self.group)
-        else:
-            self.recv_w[:nrecv].fill_(1.0)
+        dist.all_to_all_single(self.recv_meta[:R], meta, output_split_sizes=rrow_l, input_split_sizes=srow_l,
+                               group=self.group)
         mark("dispatch")
-        self.recv_e[:nrecv] = ep_recv_local_experts(recv_counts_e, self.world, nrecv)
-        # regroup by local expert (a stable counting sort), grouped GEMMs, restore arrival order
-        if nrecv:
-            _lib.check(L.ck_moe_permute(_ptr(self.recv_e), _ptr(self.recv_w), _ptr(self.recv_x), nrecv, 1, self.el, 0,
-                                        H, 1, _ptr(self.xp2), _ptr(self.row_w2), _ptr(self.pair_pos2),
+        # regroup the received (row, slot) pairs by local expert (a stable counting sort that skips
+        # the -1 slots), grouped GEMMs, then every pair's row back in (row, slot) order
+        if P:
+            rme = self.recv_meta[:R, :K].contiguous()
+            rmw = self.recv_meta[:R, K:].contiguous().view(torch.float32)
+            _lib.check(L.ck_moe_permute(_ptr(rme), _ptr(rmw), _ptr(self.recv_x), R, K, self.el, 0, H,
+                                        int(sp.mode == 4), _ptr(self.xp2), _ptr(self.row_w2), _ptr(self.pair_pos2),
                                         _ptr(self.counts2), _ptr(self.tiles2), _ptr(self.ntiles2),
                                         _ptr(self.perm_ws2), st), "regroup")
             _lib.check(L.ck_moe_expert_gemm(1, _ptr(self.w[0]), _ptr(self.w[1]), None, None, sp.matrix_bytes, self.el,
-                                             0, _ptr(self.xp2), nrecv, _ptr(self.h2), nrecv, _ptr(self.row_w2),
+                                             0, _ptr(self.xp2), P, _ptr(self.h2), P, _ptr(self.row_w2),
                                              _ptr(self.tiles2), _ptr(self.ntiles2), self.mt2, I, H, 0, _ptr(self.err),
                                              st), "expert gate/up")
             _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, None, None, sp.matrix_bytes, self.el,
-                                             0, _ptr(self.h2), nrecv, _ptr(self.y2), nrecv, None, _ptr(self.tiles2),
+                                             0, _ptr(self.h2), P, _ptr(self.y2), P, None, _ptr(self.tiles2),
                                              _ptr(self.ntiles2), self.mt2, H, I, 1, _ptr(self.err), st), "expert down")
-            _lib.check(L.ck_gather_rows(_ptr(self.y2), _ptr(self.pair_pos2), _ptr(self.y_recv), nrecv, H * 2, st),
-                       "restore order")
+            pp = self.pair_pos2[:R * K]
+            vidx = pp[torch.nonzero_static(pp >= 0, size=P).squeeze(1)]
+            _lib.check(L.ck_gather_rows(_ptr(self.y2), _ptr(vidx), _ptr(self.y_recv), P, H * 2, st), "pair order")
         mark("experts")
-        dist.all_to_all_single(self.y[:A], self.y_recv[:nrecv], output_split_sizes=sc, input_split_sizes=rc,
+        pair_pos = ep_return_positions(ids, self.el)
+        dist.all_to_all_single(self.y[:A], self.y_recv[:P], output_split_sizes=spair_l, input_split_sizes=rpair_l,
                                group=self.group)
         mark("return")
         if side_done is not None:
             main.wait_event(side_done)
-        _lib.check(L.ck_moe_combine(_ptr(self.y), _ptr(ids), _ptr(wts), _ptr(self.pair_pos), T, K, sp.n_shared, H,
+        _lib.check(L.ck_moe_combine(_ptr(self.y), _ptr(ids), _ptr(wts), _ptr(pair_pos), T, K, sp.n_shared, H,
                                     int(sp.mode == 3), _ptr(out), None, st), "combine")
         mark("combine")
         return out, ids, wts, self.counts

@@ -1,9 +1,11 @@
-"""Expert-parallel dispatch/return bookkeeping on CPU ranks (gloo, world size 2).
+"""Expert-parallel dispatch/return bookkeeping on CPU ranks (gloo, world size 2 and 4).
 
-The expert-parallel layer's host logic -- the split sizes of the two all-to-alls and the local
-expert of every received row -- exercised with the same helpers ExpertParallelMoE uses, around a
-CPU stand-in for the GPU steps (stable counting sort by expert = a stable argsort; the "expert"
-multiplies a row by its global expert id + 1).  The result must equal the direct computation.
+The expert-parallel layer's host logic -- the deduplicated dispatch plan (one row per
+(destination rank, token) with the slots' local experts and weights), the split sizes of the
+all-to-alls and the position of every returned (token, slot) row -- exercised with the same
+helpers ExpertParallelMoE uses, around a CPU stand-in for the GPU steps (the "expert" multiplies a
+row by its global expert id + 1 and by the slot's route weight).  The result must equal the direct
+computation, and every token must cross to each rank at most once.
 """
 import os
 import socket
@@ -13,7 +15,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from coherence_kernel_b200.moe import ep_recv_local_experts, ep_split_sizes
+from coherence_kernel_b200.moe import ep_dispatch_counts, ep_dispatch_rows, ep_return_positions
 
 
 def _free_port():
@@ -29,41 +31,47 @@ def _worker(rank, world, port, E, K, T, H, ret):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        el = E // world
         g = torch.Generator().manual_seed(0)
         ids_all = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T * world)]).to(torch.int32)
+        wts_all = torch.rand(T * world, K, generator=g)
         x_all = torch.randn(T * world, H, generator=g)
-        ids, x = ids_all[rank * T:(rank + 1) * T], x_all[rank * T:(rank + 1) * T]
-        flat = ids.reshape(-1)
-        order = torch.argsort(flat, stable=True)          # ck_moe_permute's stable counting sort
-        xp = x[order // K]
-        counts = torch.bincount(flat, minlength=E).to(torch.int32)
-        recv_counts_e = torch.empty_like(counts)
-        dist.all_to_all_single(recv_counts_e, counts)
-        sc, rc = ep_split_sizes(counts, recv_counts_e, world)
-        nrecv = int(sum(rc))
-        recv = torch.empty(nrecv, H)
-        dist.all_to_all_single(recv, xp, output_split_sizes=rc, input_split_sizes=sc)
-        le = ep_recv_local_experts(recv_counts_e, world, nrecv)
-        o2 = torch.argsort(le, stable=True)               # the receiver's regroup
-        y2 = recv[o2] * (le[o2].float() + 1 + rank * (E // world)).unsqueeze(1)
-        y_recv = torch.empty_like(y2)
-        y_recv[o2] = y2                                   # restore arrival order
+        sl = slice(rank * T, (rank + 1) * T)
+        ids, wts, x = ids_all[sl], wts_all[sl], x_all[sl]
+        er, mask, srow, spair = ep_dispatch_counts(ids, el, world)
+        sizes = torch.stack([srow, spair], dim=1).to(torch.int64)
+        rsizes = torch.empty_like(sizes)
+        dist.all_to_all_single(rsizes, sizes)
+        srow_l, spair_l, rrow_l, rpair_l = torch.cat([sizes.t(), rsizes.t()]).tolist()
+        S, R, P = sum(srow_l), sum(rrow_l), sum(rpair_l)
+        send_tok, me, mw = ep_dispatch_rows(ids, wts, er, mask, el, S)
+        distinct = sum(len(set((ids[t] // el).tolist())) for t in range(T))
+        ok = S == distinct and int(spair.sum()) == T * K
+        meta = torch.cat([me, mw.view(torch.int32)], dim=1)
+        recv_x = torch.empty(R, H)
+        recv_meta = torch.empty(R, 2 * K, dtype=torch.int32)
+        dist.all_to_all_single(recv_x, x[send_tok.long()], output_split_sizes=rrow_l, input_split_sizes=srow_l)
+        dist.all_to_all_single(recv_meta, meta, output_split_sizes=rrow_l, input_split_sizes=srow_l)
+        rme, rmw = recv_meta[:, :K], recv_meta[:, K:].contiguous().view(torch.float32)
+        # the receiver: every valid (row, slot) pair in (row, slot) order
+        rows, slots = torch.nonzero(rme >= 0, as_tuple=True)
+        ok = ok and rows.numel() == P
+        gexp = rme[rows, slots].float() + rank * el + 1
+        y_recv = recv_x[rows] * (gexp * rmw[rows, slots]).unsqueeze(1)
         y_back = torch.empty(T * K, H)
-        dist.all_to_all_single(y_back, y_recv, output_split_sizes=sc, input_split_sizes=rc)
-        y_pair = torch.empty_like(y_back)
-        y_pair[order] = y_back
-        out = y_pair.view(T, K, H).sum(1)
-        ref = (x.unsqueeze(1) * (ids.float() + 1).unsqueeze(2)).sum(1)
-        ret[rank] = bool(torch.allclose(out, ref)) and nrecv == int(recv_counts_e.sum())
+        dist.all_to_all_single(y_back, y_recv, output_split_sizes=spair_l, input_split_sizes=rpair_l)
+        pos = ep_return_positions(ids, el).long()
+        out = y_back[pos].view(T, K, H).sum(1)
+        ref = (x.unsqueeze(1) * ((ids.float() + 1) * wts).unsqueeze(2)).sum(1)
+        ret[rank] = bool(ok and torch.allclose(out, ref, rtol=1e-5, atol=1e-5))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("E,K,T,H", [(8, 2, 16, 4), (32, 8, 64, 8)])
-def test_ep_exchange_round_trip_gloo(E, K, T, H):
-    world = 2
+@pytest.mark.parametrize("world,E,K,T,H", [(2, 8, 2, 16, 4), (2, 32, 8, 64, 8), (4, 64, 8, 48, 4)])
+def test_ep_exchange_round_trip_gloo(world, E, K, T, H):
     mgr = mp.get_context("spawn").Manager()
     ret = mgr.dict()
     mp.start_processes(_worker, args=(world, _free_port(), E, K, T, H, ret), nprocs=world, join=True,
                        start_method="spawn")
-    assert dict(ret) == {0: True, 1: True}
+    assert dict(ret) == {r: True for r in range(world)}
