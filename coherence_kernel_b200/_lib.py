@@ -61,6 +61,7 @@ SIGNATURES = {
     "ck_moe_combine": (_i32, [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _i32, _p, _p, _p]),
     "ck_token_tiles": (_i32, [_p, _p, _u32, _p]),
     "ck_gather_rows": (_i32, [_p, _p, _p, _u32, _u32, _p]),
+    "ck_ep_dispatch_plan": (_i32, [_p, _p, _u32, _u32, _u32, _u32, _p, _p, _p, _p, _p, _p]),
     # the handle door
     "fk_metal_pipeline_external": (_ll, [ctypes.c_char_p, _ll, ctypes.c_char_p, _ll]),
     "fk_metal_buf_alloc_external": (_ll, [_ll]),

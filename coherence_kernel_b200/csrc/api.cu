@@ -339,6 +339,14 @@ int ck_token_tiles(void *tiles, int32_t *ntiles, uint32_t ntok, void *s) {
     return fail(ck::launch_single_tiles((int4 *)tiles, ntiles, ntok, ck::GEMM_TILE_TOKENS, S(s)), "ck_token_tiles");
 }
 
+int ck_ep_dispatch_plan(const int32_t *ids, const float *wts, uint32_t ntok, uint32_t nsel, uint32_t n_experts,
+                        uint32_t world, int32_t *counts, int64_t *sizes, int32_t *send_tok, int32_t *meta,
+                        int32_t *ret_pos, void *s) {
+    return fail(ck::launch_ep_plan(ids, wts, ntok, nsel, n_experts, world, counts, (long long *)sizes, send_tok,
+                                   meta, ret_pos, S(s)),
+                "ck_ep_dispatch_plan");
+}
+
 int ck_gather_rows(const void *src, const int32_t *idx, void *dst, uint32_t nrows, uint32_t row_bytes, void *s) {
     return fail(ck::launch_gather_rows(src, idx, dst, nrows, row_bytes, S(s)), "ck_gather_rows");
 }

@@ -65,6 +65,9 @@ int launch_permute(const int32_t *ids, const float *wts, const uint16_t *x_bf16,
                    int32_t *pair_pos, int32_t *counts, int4 *tiles, int32_t *ntiles, void *workspace,
                    const PermuteParams &p, cudaStream_t s);
 int launch_single_tiles(int4 *tiles, int32_t *ntiles, uint32_t ntok, uint32_t bn, cudaStream_t s);
+int launch_ep_plan(const int32_t *ids, const float *wts, uint32_t ntok, uint32_t nsel, uint32_t n_experts,
+                   uint32_t world, int32_t *counts, long long *sizes, int32_t *send_tok, int32_t *meta,
+                   int32_t *ret_pos, cudaStream_t s);
 int launch_gather_rows(const void *src, const int32_t *idx, void *dst, uint32_t nrows, uint32_t row_bytes,
                        cudaStream_t s);
 int launch_combine(const uint16_t *y, const int32_t *ids, const float *wts, const int32_t *pair_pos, uint16_t *out,

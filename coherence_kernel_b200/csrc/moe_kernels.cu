@@ -234,6 +234,147 @@ int launch_gather_rows(const void *src, const int32_t *idx, void *dst, uint32_t 
     return (int)cudaGetLastError();
 }
 
+// Expert-parallel dispatch plan, one CTA (the reference runs its MoE on one device; there is no
+// counterpart).  Rank d owns experts [d*el, (d+1)*el).  A token crosses to each rank that holds
+// at least one of its experts once: the rows of the dispatch are the (rank, token) pairs in
+// (rank, token) order, each carrying its slots' local experts (-1 for slots whose expert lives
+// elsewhere) and route weights (0 there) as one metadata row of 2K int32.  The (token, slot) pairs
+// come back rank by rank, in (token, slot) order inside a rank; ret_pos gives each pair's row in
+// that return.  Pass 1 totals rows and pairs per rank (and pairs per expert) with shared-memory
+// atomics; pass 2 walks the tokens in chunks of 1024 in order and places every row and pair with
+// warp ballots / scans and a scan over the warps, so all positions follow token order exactly.
+constexpr int PLAN_THREADS = 1024;
+constexpr uint32_t PLAN_MAX_RANKS = 32, PLAN_MAX_SLOTS = 16;
+__global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(const int32_t *__restrict__ ids, const float *__restrict__ wts,
+                                                       uint32_t T, uint32_t K, uint32_t E, uint32_t W,
+                                                       int32_t *__restrict__ counts, long long *__restrict__ sizes,
+                                                       int32_t *__restrict__ send_tok, int32_t *__restrict__ meta,
+                                                       int32_t *__restrict__ ret_pos) {
+    __shared__ int cnt[MAX_EXPERTS];
+    __shared__ int tot_rows[PLAN_MAX_RANKS], tot_pairs[PLAN_MAX_RANKS], base_rows[PLAN_MAX_RANKS],
+        base_pairs[PLAN_MAX_RANKS];
+    __shared__ int wrow[PLAN_THREADS / 32][PLAN_MAX_RANKS], wpair[PLAN_THREADS / 32][PLAN_MAX_RANKS];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t el = E / W;
+    for (uint32_t e = tid; e < E; e += PLAN_THREADS) cnt[e] = 0;
+    if (tid < (int)PLAN_MAX_RANKS) tot_rows[tid] = tot_pairs[tid] = 0;
+    __syncthreads();
+    for (uint32_t t = tid; t < T; t += PLAN_THREADS) {
+        uint32_t seen = 0;
+        for (uint32_t k = 0; k < K; ++k) {
+            const int e = ids[(size_t)t * K + k];
+            if (e < 0 || (uint32_t)e >= E) continue;
+            const uint32_t d = (uint32_t)e / el;
+            atomicAdd(&cnt[e], 1);
+            atomicAdd(&tot_pairs[d], 1);
+            seen |= 1u << d;
+        }
+        for (; seen; seen &= seen - 1) atomicAdd(&tot_rows[__ffs(seen) - 1], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int r = 0, q = 0;
+        for (uint32_t d = 0; d < W; ++d) {
+            base_rows[d] = r;
+            base_pairs[d] = q;
+            sizes[2 * d] = tot_rows[d];
+            sizes[2 * d + 1] = tot_pairs[d];
+            r += tot_rows[d];
+            q += tot_pairs[d];
+        }
+    }
+    for (uint32_t e = tid; e < E; e += PLAN_THREADS) counts[e] = cnt[e];
+    __syncthreads();
+    const unsigned lt = (1u << lane) - 1u;
+    for (uint32_t c0 = 0; c0 < T; c0 += PLAN_THREADS) {
+        const uint32_t t = c0 + tid;
+        int er[PLAN_MAX_SLOTS];
+#pragma unroll
+        for (uint32_t k = 0; k < PLAN_MAX_SLOTS; ++k) {
+            const int e = (t < T && k < K) ? ids[(size_t)t * K + k] : -1;
+            er[k] = (e >= 0 && (uint32_t)e < E) ? (int)((uint32_t)e / el) : -1;
+        }
+        // per rank: this warp's rows and pairs
+        for (uint32_t d = 0; d < W; ++d) {
+            int c = 0;
+#pragma unroll
+            for (uint32_t k = 0; k < PLAN_MAX_SLOTS; ++k) c += er[k] == (int)d;
+            const unsigned bal = __ballot_sync(0xffffffffu, c > 0);
+            int sc = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, sc, o);
+                if (lane >= o) sc += v;
+            }
+            if (lane == 31) {
+                wrow[warp][d] = __popc(bal);
+                wpair[warp][d] = sc;
+            }
+        }
+        __syncthreads();
+        int cr = 0, cp = 0;  // this chunk's totals for rank tid
+        if (tid < (int)W) {
+            for (int w = 0; w < PLAN_THREADS / 32; ++w) {
+                const int a = wrow[w][tid], b = wpair[w][tid];
+                wrow[w][tid] = cr;
+                wpair[w][tid] = cp;
+                cr += a;
+                cp += b;
+            }
+        }
+        __syncthreads();
+        for (uint32_t d = 0; d < W; ++d) {
+            int c = 0;
+#pragma unroll
+            for (uint32_t k = 0; k < PLAN_MAX_SLOTS; ++k) c += er[k] == (int)d;
+            const unsigned bal = __ballot_sync(0xffffffffu, c > 0);
+            int sc = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, sc, o);
+                if (lane >= o) sc += v;
+            }
+            if (c > 0) {
+                const int row = base_rows[d] + wrow[warp][d] + __popc(bal & lt);
+                send_tok[row] = (int32_t)t;
+                int32_t *m = meta + (size_t)row * 2 * K;
+                int q = base_pairs[d] + wpair[warp][d] + (sc - c);
+#pragma unroll
+                for (uint32_t k = 0; k < PLAN_MAX_SLOTS; ++k) {
+                    if (k >= K) break;
+                    const bool mine = er[k] == (int)d;
+                    const size_t i = (size_t)t * K + k;
+                    m[k] = mine ? ids[i] - (int)(d * el) : -1;
+                    m[K + k] = mine ? __float_as_int(wts[i]) : 0;
+                    if (mine) ret_pos[i] = q++;
+                }
+            }
+        }
+        if (t < T) {
+#pragma unroll
+            for (uint32_t k = 0; k < PLAN_MAX_SLOTS; ++k)
+                if (k < K && er[k] < 0) ret_pos[(size_t)t * K + k] = -1;
+        }
+        __syncthreads();
+        if (tid < (int)W) {
+            base_rows[tid] += cr;
+            base_pairs[tid] += cp;
+        }
+        __syncthreads();
+    }
+}
+int launch_ep_plan(const int32_t *ids, const float *wts, uint32_t ntok, uint32_t nsel, uint32_t n_experts,
+                   uint32_t world, int32_t *counts, long long *sizes, int32_t *send_tok, int32_t *meta,
+                   int32_t *ret_pos, cudaStream_t s) {
+    if (world == 0 || world > PLAN_MAX_RANKS || nsel == 0 || nsel > PLAN_MAX_SLOTS || n_experts == 0 ||
+        n_experts > (uint32_t)MAX_EXPERTS || n_experts % world)
+        return CK_ERR_SHAPE;
+    if (!ids || !wts || !counts || !sizes || !send_tok || !meta || !ret_pos) return CK_ERR_ARG;
+    k_ep_plan<<<1, PLAN_THREADS, 0, s>>>(ids, wts, ntok, nsel, n_experts, world, counts, sizes, send_tok, meta,
+                                         ret_pos);
+    return (int)cudaGetLastError();
+}
+
 // Combine: one block per token.  order_by_expert = 1 is moe-mix (moe-gate.fk:32-37): the chosen
 // experts in ascending index, acc + g*y.  order_by_expert = 0 is dsv4-moe-acc
 // (dsv4-forward.fk:100-103): the slots in list order, acc + y (the weight was applied inside the

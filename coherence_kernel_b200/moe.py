@@ -255,6 +255,10 @@ class ExpertParallelMoE:
         self.route_ws = torch.empty(_align(L.ck_moe_route_workspace_bytes(ctypes.byref(self._cfg), T)),
                                     dtype=torch.uint8, device=dev)
         self.send_x = torch.empty((T * min(W, K), H), dtype=torch.bfloat16, device=dev)
+        self.send_tok = torch.empty(T * min(W, K), dtype=torch.int32, device=dev)
+        self.send_meta = torch.empty((T * min(W, K), 2 * K), dtype=torch.int32, device=dev)
+        self.sizes = torch.empty((W, 2), dtype=torch.int64, device=dev)
+        self.ret_pos = torch.empty(A, dtype=torch.int32, device=dev)
         self.y = torch.empty((A + sp.n_shared * T, H), dtype=torch.bfloat16, device=dev)
         self.h_sh = torch.empty((max(1, sp.n_shared) * T, I), dtype=torch.bfloat16, device=dev)
         self.sh_tiles = torch.empty((T // 16 + 2, 4), dtype=torch.int32, device=dev)
@@ -301,23 +305,15 @@ class ExpertParallelMoE:
                                   _ptr(self.logits), _ptr(ids), _ptr(wts), _ptr(self.route_ws),
                                   self.route_ws.numel(), st), "ck_moe_route")
         mark("route")
-        # the sizes first: the host waits for them only behind the route
-        er, mask, srow, spair = ep_dispatch_counts(ids, self.el, W)
-        self.counts.copy_(torch.bincount(ids.reshape(-1), minlength=E))
-        sizes = torch.stack([srow, spair], dim=1).to(torch.int64)
-        rsizes = torch.empty_like(sizes)
-        dist.all_to_all_single(rsizes, sizes, group=self.group)  # [src, (rows, pairs)]
-        srow_l, spair_l, rrow_l, rpair_l = torch.cat([sizes.t(), rsizes.t()]).tolist()
-        S, R, P = int(sum(srow_l)), int(sum(rrow_l)), int(sum(rpair_l))
-        self.last_recv_rows, self.last_recv_pairs = R, P
-        # one row per (destination rank, token) with its slots' local experts and weights
-        send_tok, me, mw = ep_dispatch_rows(ids, wts, er, mask, self.el, S)
-        if S:
-            _lib.check(L.ck_gather_rows(_ptr(x), _ptr(send_tok), _ptr(self.send_x), S, H * 2, st), "dispatch rows")
-        meta = torch.cat([me, mw.view(torch.int32)], dim=1)
+        # the plan on the device: pairs per expert, (rows, pairs) per destination rank, the dispatch
+        # rows with their metadata, and every pair's row in the return exchange
+        _lib.check(L.ck_ep_dispatch_plan(_ptr(ids), _ptr(wts), T, K, E, W, _ptr(self.counts), _ptr(self.sizes),
+                                         _ptr(self.send_tok), _ptr(self.send_meta), _ptr(self.ret_pos), st),
+                   "ck_ep_dispatch_plan")
         mark("permute")
-        # shared expert(s) on the local tokens, into y rows A + s*T .., on a side stream that
-        # overlaps the exchange and the expert GEMMs; the combine waits for it
+        # shared expert(s) on the local tokens, into y rows A + s*T .., on a side stream: launched
+        # before the host waits for the split sizes, it overlaps the exchange and the expert GEMMs;
+        # the combine waits for it
         main = torch.cuda.current_stream()
         side_done = None
         if sp.n_shared:
@@ -340,10 +336,19 @@ class ExpertParallelMoE:
             side_done = torch.cuda.Event()
             side_done.record(self.side)
         mark("shared")
+        # the sizes: the one point where the host waits for the device
+        rsizes = torch.empty_like(self.sizes)
+        dist.all_to_all_single(rsizes, self.sizes, group=self.group)  # [src, (rows, pairs)]
+        srow_l, spair_l, rrow_l, rpair_l = torch.cat([self.sizes.t(), rsizes.t()]).tolist()
+        S, R, P = int(sum(srow_l)), int(sum(rrow_l)), int(sum(rpair_l))
+        self.last_recv_rows, self.last_recv_pairs = R, P
+        if S:
+            _lib.check(L.ck_gather_rows(_ptr(x), _ptr(self.send_tok), _ptr(self.send_x), S, H * 2, st),
+                       "dispatch rows")
         dist.all_to_all_single(self.recv_x[:R], self.send_x[:S], output_split_sizes=rrow_l, input_split_sizes=srow_l,
                                group=self.group)
-        dist.all_to_all_single(self.recv_meta[:R], meta, output_split_sizes=rrow_l, input_split_sizes=srow_l,
-                               group=self.group)
+        dist.all_to_all_single(self.recv_meta[:R], self.send_meta[:S], output_split_sizes=rrow_l,
+                               input_split_sizes=srow_l, group=self.group)
         mark("dispatch")
         # regroup the received (row, slot) pairs by local expert (a stable counting sort that skips
         # the -1 slots), grouped GEMMs, then every pair's row back in (row, slot) order
@@ -365,13 +370,12 @@ class ExpertParallelMoE:
             vidx = pp[torch.nonzero_static(pp >= 0, size=P).squeeze(1)]
             _lib.check(L.ck_gather_rows(_ptr(self.y2), _ptr(vidx), _ptr(self.y_recv), P, H * 2, st), "pair order")
         mark("experts")
-        pair_pos = ep_return_positions(ids, self.el)
         dist.all_to_all_single(self.y[:A], self.y_recv[:P], output_split_sizes=spair_l, input_split_sizes=rpair_l,
                                group=self.group)
         mark("return")
         if side_done is not None:
             main.wait_event(side_done)
-        _lib.check(L.ck_moe_combine(_ptr(self.y), _ptr(ids), _ptr(wts), _ptr(pair_pos), T, K, sp.n_shared, H,
+        _lib.check(L.ck_moe_combine(_ptr(self.y), _ptr(ids), _ptr(wts), _ptr(self.ret_pos), T, K, sp.n_shared, H,
                                     int(sp.mode == 3), _ptr(out), None, st), "combine")
         mark("combine")
         return out, ids, wts, self.counts

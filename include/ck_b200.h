@@ -143,6 +143,18 @@ int ck_moe_combine(const void *y_bf16_dev, const int32_t *ids_dev, const float *
 int ck_token_tiles(void *tiles_dev, int32_t *ntiles_dev, uint32_t ntok, void *stream);
 int ck_gather_rows(const void *src_dev, const int32_t *idx_dev, void *dst_dev, uint32_t nrows, uint32_t row_bytes,
                    void *stream);
+/* Expert-parallel dispatch plan (no counterpart in the reference, whose MoE runs on one device).
+ * Rank d of `world` owns experts [d*E/world, (d+1)*E/world).  From the routed ids/wts
+ * [ntok, nsel] (one CTA, stream-ordered): counts [E] pairs per expert; sizes [world][2] int64 =
+ * (rows, pairs) sent to each rank; send_tok [rows] the token of every dispatch row, one row per
+ * (rank, token) with at least one of the token's experts there, in (rank, token) order; meta
+ * [rows][2*nsel] int32 = the slots' local experts (-1 for slots owned elsewhere) then their
+ * route weights as float bits (0 there); ret_pos [ntok*nsel] the row of every (token, slot)
+ * pair in the return exchange (ranks in order, (token, slot) order inside a rank).  world <= 32,
+ * nsel <= 16, E <= 1024, E % world == 0; send_tok/meta hold up to ntok*min(world, nsel) rows. */
+int ck_ep_dispatch_plan(const int32_t *ids_dev, const float *wts_dev, uint32_t ntok, uint32_t nsel,
+                        uint32_t n_experts, uint32_t world, int32_t *counts_dev, int64_t *sizes_dev,
+                        int32_t *send_tok_dev, int32_t *meta_dev, int32_t *ret_pos_dev, void *stream);
 
 #ifdef __cplusplus
 }

@@ -95,3 +95,35 @@ def test_expert_parallel_matches_single_gpu(name):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     verdict, info = q.get(timeout=5)
     assert verdict == "ok", info
+
+
+@pytest.mark.parametrize("world,E,K,T", [(2, 16, 4, 300), (8, 256, 8, 1500), (4, 64, 8, 2048), (3, 48, 6, 1025)])
+def test_ep_dispatch_plan_matches_host_rules(world, E, K, T):
+    """The device plan (one CTA) equals the host rules the gloo test exercises: pairs per expert,
+    rows and pairs per rank, the dispatch rows in (rank, token) order with their metadata, and the
+    return position of every (token, slot) pair."""
+    import ctypes
+
+    from coherence_kernel_b200 import _lib
+    from coherence_kernel_b200.moe import ep_dispatch_counts, ep_dispatch_rows, ep_return_positions
+    g = torch.Generator().manual_seed(T)
+    ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).to(torch.int32).cuda()
+    wts = torch.rand(T, K, generator=g).cuda()
+    el = E // world
+    rows_max = T * min(world, K)
+    counts = torch.empty(E, dtype=torch.int32, device="cuda")
+    sizes = torch.empty((world, 2), dtype=torch.int64, device="cuda")
+    send_tok = torch.full((rows_max,), -7, dtype=torch.int32, device="cuda")
+    meta = torch.full((rows_max, 2 * K), -7, dtype=torch.int32, device="cuda")
+    ret_pos = torch.full((T * K,), -7, dtype=torch.int32, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    _lib.check(_lib.load().ck_ep_dispatch_plan(p(ids), p(wts), T, K, E, world, p(counts), p(sizes), p(send_tok),
+                                               p(meta), p(ret_pos), None), "ck_ep_dispatch_plan")
+    er, mask, srow, spair = ep_dispatch_counts(ids, el, world)
+    S = int(srow.sum())
+    tok, me, mw = ep_dispatch_rows(ids, wts, er, mask, el, S)
+    assert torch.equal(counts.long(), torch.bincount(ids.reshape(-1).long(), minlength=E))
+    assert torch.equal(sizes[:, 0], srow) and torch.equal(sizes[:, 1], spair)
+    assert torch.equal(send_tok[:S], tok)
+    assert torch.equal(meta[:S], torch.cat([me, mw.view(torch.int32)], dim=1))
+    assert torch.equal(ret_pos, ep_return_positions(ids, el))
