@@ -32,7 +32,8 @@ struct RouteWs {
     int32_t *ntiles;
     int *err;
     uint32_t *flags;
-    double *exact;  // fp64 logits of the flagged tokens
+    double *exact;  // fp64 logits of the flagged tokens (and of every token on the decode-batch path)
+    float *sabs;    // sum |w x| per logit on the decode-batch path
     size_t total;
 };
 RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
@@ -46,6 +47,7 @@ RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
     w.err = (int *)take(4);
     w.flags = (uint32_t *)take(((size_t)ntok + 1) * 4);
     w.exact = (double *)take((size_t)ntok * c->n_experts * 8);
+    w.sabs = (float *)take((size_t)ntok * c->n_experts * 4);
     w.total = o;
     return w;
 }
@@ -251,29 +253,44 @@ int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const flo
     if (wsb < ck_moe_route_workspace_bytes(c, ntok)) return fail(CK_EARG, "ck_moe_route workspace");
     if (ntok == 0) return 0;
     RouteWs w = route_ws(c, ntok, ws);
-    // logits on the tensor cores: x . [W1 | W2 | W3]^T with the fp32 router split into bf16 terms
-    rc = ck::launch_split_bf16x3(rw, w.wsplit, c->n_experts, c->hidden, S(s));
-    if (!rc) rc = ck::launch_single_tiles(w.tiles, w.ntiles, ntok, 64, S(s));
-    if (rc) return fail(rc, "ck_moe_route split");
-    cudaMemsetAsync(w.err, 0, 4, S(s));
-    ck::GemmParams g = {};
-    g.a_dense = w.wsplit;
-    g.kx = c->hidden;
-    g.K = 3 * c->hidden;
-    g.N = c->n_experts;
-    g.x = x;
-    g.x_rows = ntok;
-    g.out_f32 = logits;
-    g.out_rows = ntok;
-    g.tiles = w.tiles;
-    g.ntiles = w.ntiles;
-    g.max_tiles = ntok / 16 + 2;
-    g.err = w.err;
-    rc = ck::launch_gemm_dense(g, S(s));
-    if (rc) return fail(rc, "ck_moe_route logits");
     ck::RouteParams p = {ntok, c->n_experts, c->nsel, c->hidden, c->mode, c->ngroups, c->topk_groups, c->wscale, c->tau};
-    rc = ck::launch_route_select(logits, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
-    if (rc) return fail(rc, "ck_moe_route select");
+    // A decode-sized batch (at most 64 tokens): the router as a matvec over all SMs with compensated
+    // sums, selected in fp64 with a margin sized by the dot's own rounding (about 1e-9 here), so in
+    // practice only exact ties take the fp64 re-route.  Otherwise the logits run on the tensor cores,
+    // x . [W1 | W2 | W3]^T with the fp32 router split into bf16 terms, and are selected in fp32
+    // with the margin tau.
+    rc = ntok <= 64 ? ck::launch_router_logits_few((const uint16_t *)x, rw, logits, w.exact, w.sabs, ntok,
+                                                   c->n_experts, c->hidden, S(s))
+                    : CK_ERR_SHAPE;
+    if (rc == 0) {
+        p.tau = 0.0f;
+        rc = ck::launch_route_select_d(w.exact, w.sabs, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
+        if (rc) return fail(rc, "ck_moe_route select");
+    } else if (rc == CK_ERR_SHAPE) {
+        rc = ck::launch_split_bf16x3(rw, w.wsplit, c->n_experts, c->hidden, S(s));
+        if (!rc) rc = ck::launch_single_tiles(w.tiles, w.ntiles, ntok, 64, S(s));
+        if (rc) return fail(rc, "ck_moe_route split");
+        cudaMemsetAsync(w.err, 0, 4, S(s));
+        ck::GemmParams g = {};
+        g.a_dense = w.wsplit;
+        g.kx = c->hidden;
+        g.K = 3 * c->hidden;
+        g.N = c->n_experts;
+        g.x = x;
+        g.x_rows = ntok;
+        g.out_f32 = logits;
+        g.out_rows = ntok;
+        g.tiles = w.tiles;
+        g.ntiles = w.ntiles;
+        g.max_tiles = ntok / 16 + 2;
+        g.err = w.err;
+        rc = ck::launch_gemm_dense(g, S(s));
+        if (rc) return fail(rc, "ck_moe_route logits");
+        rc = ck::launch_route_select(logits, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
+        if (rc) return fail(rc, "ck_moe_route select");
+    } else {
+        return fail(rc, "ck_moe_route logits");
+    }
     rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, w.flags + 1, w.flags, w.exact, p, S(s));
     return fail(rc, "ck_moe_route exact");
 }

@@ -43,6 +43,13 @@ struct RouteParams {
     float wscale;          // mode 4 weight scale
     float tau;             // decision margin below which a token is re-routed exactly in fp64
 };
+// router logits for at most 64 tokens (compensated sums over the fp32 router) in fp32 and fp64, with
+// sum |w x| per logit; ntok > 64 returns CK_ERR_SHAPE
+int launch_router_logits_few(const uint16_t *x, const float *w, float *L, double *Ld, float *sabs, uint32_t T,
+                             uint32_t E, uint32_t H, cudaStream_t s);
+// the fast selection over fp64 logits (the decode-batch form); its margin scales with sabs
+int launch_route_select_d(const double *L, const float *sabs, const float *bias, int32_t *ids, float *wts,
+                          uint32_t *flag_list, uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
 int launch_route_select(const float *logits, const float *bias, int32_t *ids, float *wts, uint32_t *flag_list,
                         uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
 // scratch: fp64 [ntok, ne] (the exact logits of the flagged tokens)

@@ -13,8 +13,9 @@
 // Explicit round-to-nearest intrinsics keep the compiler from contracting a multiply and an add.
 //
 // Two kernels: k_exact_logits spreads (token, expert) right folds over the whole GPU (each fold is a
-// 7168-long dependent chain, so many chains must be in flight); k_exact_select is one warp per
-// token.
+// 7168-long dependent chain, so many chains must be in flight) -- tiled over 16 tokens x 64 experts
+// when more than 32 tokens are flagged, one chain per lane fed by a cp.async ring
+// (k_exact_logits_few) when at most 32 are; k_exact_select is one CTA per token.
 #include "ck_common.cuh"
 #include "ck_launch.h"
 
@@ -51,6 +52,84 @@ constexpr int XL_TPT = 4;    // tokens (independent fold chains) per thread
 // 256 threads = 64 experts x 4 token groups; each thread folds 4 tokens.  The W and x tiles are
 // converted to double once per tile into shared memory, double-buffered: the next tile's global
 // loads are in registers while the current tile is folded.
+// Few flagged tokens (a decode step): the tiled form below would leave most of the GPU idle and fold
+// padding, so each warp takes one (token, 32 experts) item and every lane one fold chain.  A chain
+// is a dependent sequence of DFMAs, so its inputs must arrive far ahead: each lane copies its
+// router row's next columns eight at a time (two 16-byte cp.async) into a per-warp ring of
+// XF_NB stages in shared memory, lane 0 copies the token's eight activations beside them, and the
+// chain consumes stage i while stages i+1 .. i+XF_NB-1 are in flight.  Same fold, same bits.
+constexpr uint32_t XL_FEW = 32;
+constexpr int XF_NB = 24;       // ring stages per warp (8 columns each)
+constexpr int XF_WARPS = 4;     // warps per CTA in the few-token form
+struct XfRing {
+    float4 w[XF_NB][32][2];     // [stage][lane][columns 8j .. 8j+3, 8j+4 .. 8j+7]
+    uint4 x[XF_NB];             // the token's eight bf16 activations of the stage
+};
+CK_DEV void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+CK_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CK_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+CK_DEV void exact_logits_few(const uint16_t *__restrict__ x, const float *__restrict__ W,
+                             const uint32_t *__restrict__ flag_list, uint32_t nflag, double *__restrict__ out,
+                             uint32_t ne, uint32_t hidden, XfRing &r) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t neg = (ne + 31) / 32, nwarp = gridDim.x * (blockDim.x >> 5);
+    const int nst = (int)hidden / 8;
+    for (uint32_t item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < nflag * neg; item += nwarp) {
+        const uint32_t f = item / neg, e = (item % neg) * 32 + lane;
+        const bool live = e < ne;
+        const float *wr = W + (size_t)(live ? e : 0) * hidden;
+        const uint16_t *xr = x + (size_t)flag_list[f] * hidden;
+        // stage s holds columns 8 (nst-1-s) .. +7 (the fold runs from the last column down)
+        auto issue = [&](int s) {
+            if (s < nst) {
+                const int j = 8 * (nst - 1 - s), b = s % XF_NB;
+                cp_async16(&r.w[b][lane][0], wr + j);
+                cp_async16(&r.w[b][lane][1], wr + j + 4);
+                if (lane == 0) cp_async16(&r.x[b], xr + j);
+            }
+            cp_async_commit();  // an empty group past the end keeps the wait count uniform
+        };
+        __syncwarp();  // the previous item's reads of the ring are done
+        for (int s = 0; s < XF_NB - 1; ++s) issue(s);
+        double acc = 0.0;
+        for (int s = 0; s < nst; ++s) {
+            issue(s + XF_NB - 1);
+            cp_async_wait<XF_NB - 1>();
+            __syncwarp();
+            const int b = s % XF_NB;
+            const float4 lo = r.w[b][lane][0], hi = r.w[b][lane][1];
+            const uint4 xv = r.x[b];
+            acc = __fma_rn((double)hi.w, (double)__uint_as_float(xv.w & 0xFFFF0000u), acc);
+            acc = __fma_rn((double)hi.z, (double)__uint_as_float(xv.w << 16), acc);
+            acc = __fma_rn((double)hi.y, (double)__uint_as_float(xv.z & 0xFFFF0000u), acc);
+            acc = __fma_rn((double)hi.x, (double)__uint_as_float(xv.z << 16), acc);
+            acc = __fma_rn((double)lo.w, (double)__uint_as_float(xv.y & 0xFFFF0000u), acc);
+            acc = __fma_rn((double)lo.z, (double)__uint_as_float(xv.y << 16), acc);
+            acc = __fma_rn((double)lo.y, (double)__uint_as_float(xv.x & 0xFFFF0000u), acc);
+            acc = __fma_rn((double)lo.x, (double)__uint_as_float(xv.x << 16), acc);
+            __syncwarp();  // every lane has read stage b before issue() refills it next iteration
+        }
+        cp_async_wait<0>();
+        if (live) out[(size_t)f * ne + e] = acc;
+    }
+}
+__global__ void __launch_bounds__(XF_WARPS * 32) k_exact_logits_few(const uint16_t *__restrict__ x,
+                                                                    const float *__restrict__ W,
+                                                                    const uint32_t *__restrict__ flag_list,
+                                                                    const uint32_t *__restrict__ flag_count,
+                                                                    double *__restrict__ out, uint32_t ne,
+                                                                    uint32_t hidden) {
+    extern __shared__ __align__(16) uint8_t xf_smem[];
+    const uint32_t nflag = *flag_count;
+    if (nflag > XL_FEW) return;  // the tiled kernel takes them
+    XfRing &r = reinterpret_cast<XfRing *>(xf_smem)[threadIdx.x >> 5];
+    exact_logits_few(x, W, flag_list, nflag, out, ne, hidden, r);
+}
+
 __global__ void __launch_bounds__(256) k_exact_logits(const uint16_t *__restrict__ x, const float *__restrict__ W,
                                                       const uint32_t *__restrict__ flag_list,
                                                       const uint32_t *__restrict__ flag_count, double *__restrict__ out,
@@ -58,6 +137,7 @@ __global__ void __launch_bounds__(256) k_exact_logits(const uint16_t *__restrict
     __shared__ double wt[2][XL_EXP][XL_J + 1];
     __shared__ __align__(16) double xt[2][XL_TOK][XL_J];
     const uint32_t nflag = *flag_count;
+    if (nflag <= XL_FEW) return;  // k_exact_logits_few takes them
     const int tid = threadIdx.x;
     const int el = tid & (XL_EXP - 1);
     const int q = tid / XL_EXP;  // 0..3: this thread folds tokens 4q .. 4q+3 of the item
@@ -140,142 +220,169 @@ CK_DEV void warp_argmax_d(double &v, int &i) {
 }
 
 constexpr int XS_MAXR = 8;  // up to 256 experts: lane holds e = lane + 32 r
-__global__ void k_exact_select(const double *__restrict__ lg, const float *__restrict__ bias, int32_t *__restrict__ ids,
-                               float *__restrict__ wts, const uint32_t *__restrict__ flag_list,
-                               const uint32_t *__restrict__ flag_count, RouteParams p) {
-    __shared__ double sbuf[8][256];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const uint32_t nflag = *flag_count;
+// Warp 0's part of k_exact_select: the selection over the fp64 terms in `sprob`.
+CK_DEV void select_token(const double *sprob, const float *__restrict__ bias, int32_t *__restrict__ ids,
+                         float *__restrict__ wts, uint32_t t, const RouteParams &p, int lane) {
     const int ne = (int)p.ne, k = (int)p.nsel;
     const double NEG = -1000000000.0;  // dsv4-set-nth's sentinel
-    for (uint32_t f = blockIdx.x * (blockDim.x >> 5) + wib; f < nflag; f += gridDim.x * (blockDim.x >> 5)) {
+    double v[XS_MAXR], pr[XS_MAXR];
+    int sel[16];
+    double w[16];
+    if (p.mode == 4) {
+#pragma unroll
+        for (int r = 0; r < XS_MAXR; ++r) {
+            const int e = lane + 32 * r;
+            pr[r] = e < ne ? sprob[e] : 0.0;
+            v[r] = e < ne ? __dadd_rn(pr[r], (double)bias[e]) : -3.0e300;
+        }
+        // group scores: dsv4-topk-2 of the group (first max, then the first max of the rest),
+        // tn-sum over (second, best) = (0 + second) + best
+        const int gs = ne / (int)p.ngroups;
+        double gsc[32];
+        for (int g = 0; g < (int)p.ngroups; ++g) {
+            double b1 = -3.0e300;
+            int i1 = 1 << 30;
+#pragma unroll
+            for (int r = 0; r < XS_MAXR; ++r) {
+                const int e = lane + 32 * r;
+                if (e < ne && e / gs == g && (v[r] > b1 || (v[r] == b1 && e < i1))) { b1 = v[r]; i1 = e; }
+            }
+            warp_argmax_d(b1, i1);
+            double b2 = -3.0e300;
+            int i2 = 1 << 30;
+#pragma unroll
+            for (int r = 0; r < XS_MAXR; ++r) {
+                const int e = lane + 32 * r;
+                if (e < ne && e / gs == g && e != i1 && (v[r] > b2 || (v[r] == b2 && e < i2))) { b2 = v[r]; i2 = e; }
+            }
+            warp_argmax_d(b2, i2);
+            gsc[g] = __dadd_rn(__dadd_rn(0.0, b2), b1);
+        }
+        unsigned gon = 0;
+        for (int r = 0; r < (int)p.topk_groups; ++r) {
+            double best = -3.0e300;
+            int bi = 0;
+            for (int g = 0; g < (int)p.ngroups; ++g)
+                if (!(gon >> g & 1) && gsc[g] > best) { best = gsc[g]; bi = g; }
+            gon |= 1u << bi;
+        }
+#pragma unroll
+        for (int r = 0; r < XS_MAXR; ++r) {
+            const int e = lane + 32 * r;
+            if (e < ne && !(gon >> (e / gs) & 1)) v[r] = NEG;
+        }
+        // dsv4-topk over the masked scores: the picks listed last-first
+        for (int r = 0; r < k; ++r) {
+            double b = -3.0e300;
+            int bi = 1 << 30;
+#pragma unroll
+            for (int rr = 0; rr < XS_MAXR; ++rr) {
+                const int e = lane + 32 * rr;
+                if (e < ne && v[rr] > b) { b = v[rr]; bi = e; }
+            }
+            warp_argmax_d(b, bi);
+            sel[k - 1 - r] = bi;
+#pragma unroll
+            for (int rr = 0; rr < XS_MAXR; ++rr)
+                if (lane + 32 * rr == bi) v[rr] = NEG;
+        }
+        double s0 = 0.0;
+        for (int i = 0; i < k; ++i) {
+            double pe = 0.0;
+#pragma unroll
+            for (int rr = 0; rr < XS_MAXR; ++rr)
+                if (lane + 32 * rr == sel[i]) pe = pr[rr];
+            pe = __shfl_sync(0xffffffffu, pe, sel[i] & 31);
+            w[i] = pe;
+            s0 = __dadd_rn(s0, pe);
+        }
+        const double s = s0 < 0.00006103515625 ? 0.00006103515625 : s0;
+        const double scl = __ddiv_rn((double)p.wscale, s);
+        for (int i = 0; i < k; ++i) w[i] = __dmul_rn(w[i], scl);
+    } else {
+        // mm-softmax: mm-max over the tail from the head, tn-exp of (l - max) (both above), the sum
+        // as a left fold in index order, p = e * (1/sum); mm-topk keeps the first index on a tie
+        const double *buf = sprob;
+        double s = 0.0;
+        for (int e = 0; e < ne; ++e) s = __dadd_rn(s, buf[e]);
+        const double inv = __ddiv_rn(1.0, s);
+#pragma unroll
+        for (int r = 0; r < XS_MAXR; ++r) {
+            const int e = lane + 32 * r;
+            v[r] = e < ne ? __dmul_rn(buf[e], inv) : -3.0e300;
+        }
+        for (int r = 0; r < k; ++r) {
+            double b = -3.0e300;
+            int bi = 1 << 30;
+#pragma unroll
+            for (int rr = 0; rr < XS_MAXR; ++rr) {
+                const int e = lane + 32 * rr;
+                if (e < ne && v[rr] > b) { b = v[rr]; bi = e; }
+            }
+            warp_argmax_d(b, bi);
+            sel[r] = bi;
+            w[r] = b;
+#pragma unroll
+            for (int rr = 0; rr < XS_MAXR; ++rr)
+                if (lane + 32 * rr == bi) v[rr] = -3.0e300;
+        }
+    }
+    if (lane == 0)
+        for (int i = 0; i < k; ++i) {
+            ids[(size_t)t * k + i] = sel[i];
+            wts[(size_t)t * k + i] = (float)w[i];
+        }
+}
+
+
+// One CTA per flagged token: the 256 threads evaluate the expensive fp64 terms (ln-sigmoid, or
+// the softmax's tn-exp) one expert each into shared memory, then warp 0 makes the selection.
+__global__ void __launch_bounds__(256) k_exact_select(const double *__restrict__ lg, const float *__restrict__ bias,
+                                                      int32_t *__restrict__ ids, float *__restrict__ wts,
+                                                      const uint32_t *__restrict__ flag_list,
+                                                      const uint32_t *__restrict__ flag_count, RouteParams p) {
+    __shared__ double sbuf[256], sprob[256];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const uint32_t nflag = *flag_count;
+    const int ne = (int)p.ne;
+    for (uint32_t f = blockIdx.x; f < nflag; f += gridDim.x) {
         const uint32_t t = flag_list[f];
         const double *L = lg + (size_t)f * ne;
-        double v[XS_MAXR], pr[XS_MAXR];
-        int sel[16];
-        double w[16];
+        const int te = threadIdx.x;
         if (p.mode == 4) {
-#pragma unroll
-            for (int r = 0; r < XS_MAXR; ++r) {
-                const int e = lane + 32 * r;
-                pr[r] = e < ne ? ref_sigmoid(L[e]) : 0.0;
-                v[r] = e < ne ? __dadd_rn(pr[r], (double)bias[e]) : -3.0e300;
-            }
-            // group scores: dsv4-topk-2 of the group (first max, then the first max of the rest),
-            // tn-sum over (second, best) = (0 + second) + best
-            const int gs = ne / (int)p.ngroups;
-            double gsc[32];
-            for (int g = 0; g < (int)p.ngroups; ++g) {
-                double b1 = -3.0e300;
-                int i1 = 1 << 30;
-#pragma unroll
-                for (int r = 0; r < XS_MAXR; ++r) {
-                    const int e = lane + 32 * r;
-                    if (e < ne && e / gs == g && (v[r] > b1 || (v[r] == b1 && e < i1))) { b1 = v[r]; i1 = e; }
-                }
-                warp_argmax_d(b1, i1);
-                double b2 = -3.0e300;
-                int i2 = 1 << 30;
-#pragma unroll
-                for (int r = 0; r < XS_MAXR; ++r) {
-                    const int e = lane + 32 * r;
-                    if (e < ne && e / gs == g && e != i1 && (v[r] > b2 || (v[r] == b2 && e < i2))) { b2 = v[r]; i2 = e; }
-                }
-                warp_argmax_d(b2, i2);
-                gsc[g] = __dadd_rn(__dadd_rn(0.0, b2), b1);
-            }
-            unsigned gon = 0;
-            for (int r = 0; r < (int)p.topk_groups; ++r) {
-                double best = -3.0e300;
-                int bi = 0;
-                for (int g = 0; g < (int)p.ngroups; ++g)
-                    if (!(gon >> g & 1) && gsc[g] > best) { best = gsc[g]; bi = g; }
-                gon |= 1u << bi;
-            }
-#pragma unroll
-            for (int r = 0; r < XS_MAXR; ++r) {
-                const int e = lane + 32 * r;
-                if (e < ne && !(gon >> (e / gs) & 1)) v[r] = NEG;
-            }
-            // dsv4-topk over the masked scores: the picks listed last-first
-            for (int r = 0; r < k; ++r) {
-                double b = -3.0e300;
-                int bi = 1 << 30;
-#pragma unroll
-                for (int rr = 0; rr < XS_MAXR; ++rr) {
-                    const int e = lane + 32 * rr;
-                    if (e < ne && v[rr] > b) { b = v[rr]; bi = e; }
-                }
-                warp_argmax_d(b, bi);
-                sel[k - 1 - r] = bi;
-#pragma unroll
-                for (int rr = 0; rr < XS_MAXR; ++rr)
-                    if (lane + 32 * rr == bi) v[rr] = NEG;
-            }
-            double s0 = 0.0;
-            for (int i = 0; i < k; ++i) {
-                double pe = 0.0;
-#pragma unroll
-                for (int rr = 0; rr < XS_MAXR; ++rr)
-                    if (lane + 32 * rr == sel[i]) pe = pr[rr];
-                pe = __shfl_sync(0xffffffffu, pe, sel[i] & 31);
-                w[i] = pe;
-                s0 = __dadd_rn(s0, pe);
-            }
-            const double s = s0 < 0.00006103515625 ? 0.00006103515625 : s0;
-            const double scl = __ddiv_rn((double)p.wscale, s);
-            for (int i = 0; i < k; ++i) w[i] = __dmul_rn(w[i], scl);
+            if (te < ne) sprob[te] = ref_sigmoid(L[te]);
         } else {
-            // mm-softmax: mm-max over the tail from the head, tn-exp of (l - max), the sum as a left
-            // fold in index order, p = e * (1/sum); mm-topk keeps the first index on a tie
-            double *buf = sbuf[wib];
-            for (int e = lane; e < ne; e += 32) buf[e] = L[e];
-            __syncwarp();
-            double mx = buf[0];
+            // mm-max over the tail from the head (every thread scans the same row), then tn-exp
+            if (te < ne) sbuf[te] = L[te];
+            __syncthreads();
+            double mx = sbuf[0];
             for (int e = 1; e < ne; ++e)
-                if (buf[e] > mx) mx = buf[e];
-            for (int e = lane; e < ne; e += 32) buf[e] = ref_exp(__dsub_rn(buf[e], mx));
-            __syncwarp();
-            double s = 0.0;
-            for (int e = 0; e < ne; ++e) s = __dadd_rn(s, buf[e]);
-            const double inv = __ddiv_rn(1.0, s);
-#pragma unroll
-            for (int r = 0; r < XS_MAXR; ++r) {
-                const int e = lane + 32 * r;
-                v[r] = e < ne ? __dmul_rn(buf[e], inv) : -3.0e300;
-            }
-            __syncwarp();
-            for (int r = 0; r < k; ++r) {
-                double b = -3.0e300;
-                int bi = 1 << 30;
-#pragma unroll
-                for (int rr = 0; rr < XS_MAXR; ++rr) {
-                    const int e = lane + 32 * rr;
-                    if (e < ne && v[rr] > b) { b = v[rr]; bi = e; }
-                }
-                warp_argmax_d(b, bi);
-                sel[r] = bi;
-                w[r] = b;
-#pragma unroll
-                for (int rr = 0; rr < XS_MAXR; ++rr)
-                    if (lane + 32 * rr == bi) v[rr] = -3.0e300;
-            }
+                if (sbuf[e] > mx) mx = sbuf[e];
+            if (te < ne) sprob[te] = ref_exp(__dsub_rn(sbuf[te], mx));
         }
-        if (lane == 0)
-            for (int i = 0; i < k; ++i) {
-                ids[(size_t)t * k + i] = sel[i];
-                wts[(size_t)t * k + i] = (float)w[i];
-            }
+        __syncthreads();
+        if (wib == 0) select_token(sprob, bias, ids, wts, t, p, lane);
+        __syncthreads();  // the shared rows are reused by the next token
     }
 }
 
 int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int32_t *ids, float *wts,
                        const uint32_t *flag_list, const uint32_t *flag_count, double *scratch,
                        const RouteParams &p, cudaStream_t s) {
-    if (p.ne > 256 || p.hidden % XL_J != 0 || p.nsel > 16 || (p.mode == 4 && p.ngroups > 32)) return CK_ERR_SHAPE;
+    if (p.ne > 256 || p.hidden % XL_J != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) || p.nsel > 16 || (p.mode == 4 && p.ngroups > 32)) return CK_ERR_SHAPE;
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    static bool few_attr = false;
+    if (!few_attr) {
+        const cudaError_t e = cudaFuncSetAttribute(k_exact_logits_few, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)(XF_WARPS * sizeof(XfRing)));
+        if (e != cudaSuccess) return (int)e;
+        few_attr = true;
+    }
+    // both forms are launched; each returns at once unless the flagged count is its own
+    k_exact_logits_few<<<nsm, XF_WARPS * 32, XF_WARPS * sizeof(XfRing), s>>>(x, w, flag_list, flag_count, scratch,
+                                                                            p.ne, p.hidden);
     k_exact_logits<<<nsm * 2, 256, 0, s>>>(x, w, flag_list, flag_count, scratch, p.ne, p.hidden);
     k_exact_select<<<nsm * 2, 256, 0, s>>>(scratch, bias, ids, wts, flag_list, flag_count, p);
     return (int)cudaGetLastError();

@@ -71,75 +71,207 @@ __global__ void __launch_bounds__(256) k_router_logits(const uint16_t *__restric
         }
 }
 
+// Few tokens (a decode-sized batch, ntok <= RS_TMAX): the tensor-core form would put the whole
+// router on one or two CTAs, so here every expert's row is a CTA of its own and every dot is
+// carried as a float pair (s, c): each fp32 x bf16 product is split exactly (p = w*x,
+// e = fma(w, x, -p)) and added with Knuth's two-sum, so the pair tracks the sum to about 2^-44 of
+// its terms' magnitude -- fp64-like accuracy at fp32 throughput (this GPU's fp64 FMA is a slow
+// pipe).  Warp w takes the w-th eighth of the row; its lanes hold their slice of the router row in
+// registers for every token, and each token's activations are loaded two tokens ahead of their use
+// (the loop is bound by load latency).  The lanes' pairs are merged by two-sums in a fixed shuffle
+// tree and the eighths in order; the logit is written in fp64 (for the fp64 selection) and fp32,
+// with sum |w x| beside it (the scale of every rounding error in the dot).
+constexpr uint32_t RS_TMAX = 64;  // tokens
+constexpr uint32_t RS_IT = 8;     // float4 per lane of a warp's eighth of the row: hidden <= 8192
+// (explicit round-to-nearest intrinsics: a contracted multiply-add would break the two-sum)
+CK_DEV void two_sum_into(float &s, float &c, float p) {
+    const float t = __fadd_rn(s, p), z = __fsub_rn(t, s);
+    c = __fadd_rn(c, __fadd_rn(__fsub_rn(s, __fsub_rn(t, z)), __fsub_rn(p, z)));
+    s = t;
+}
+CK_DEV void dot_pair(float &s, float &c, float w, float x) {
+    const float p = __fmul_rn(w, x);
+    c = __fadd_rn(c, __fmaf_rn(w, x, -p));
+    two_sum_into(s, c, p);
+}
+__global__ void __launch_bounds__(256, 2) k_router_logits_few(const uint16_t *__restrict__ x,
+                                                              const float *__restrict__ w, float *__restrict__ L,
+                                                              double *__restrict__ Ld, float *__restrict__ sabs,
+                                                              uint32_t T, uint32_t E, uint32_t H) {
+    __shared__ double part[8][RS_TMAX];
+    __shared__ float apart[8][RS_TMAX];
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const uint32_t e = blockIdx.x, seg = H / 32, j0 = wp * seg;  // float4 per eighth, this warp's first
+    float4 wv[RS_IT];
+    const float4 *wr = reinterpret_cast<const float4 *>(w + (size_t)e * H) + j0;
+#pragma unroll
+    for (uint32_t i = 0; i < RS_IT; ++i) {
+        const uint32_t j = lane + 32 * i;
+        wv[i] = j < seg ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    auto load_x = [&](uint32_t t, uint2 (&xv)[RS_IT]) {
+        const uint2 *xr = reinterpret_cast<const uint2 *>(x + (size_t)(t < T ? t : 0) * H) + j0;
+#pragma unroll
+        for (uint32_t i = 0; i < RS_IT; ++i) {
+            const uint32_t j = lane + 32 * i;
+            xv[i] = (t < T && j < seg) ? __ldg(xr + j) : make_uint2(0u, 0u);
+        }
+    };
+    uint2 xa[RS_IT], xb[RS_IT], xc[RS_IT];
+    load_x(0, xa);
+    load_x(1, xb);
+    for (uint32_t t = 0; t < T; ++t) {
+        load_x(t + 2, xc);
+        float s = 0.0f, c = 0.0f, av = 0.0f;  // av: sum |w x|, the scale of every rounding error
+#pragma unroll
+        for (uint32_t i = 0; i < RS_IT; ++i) {
+            const float x0 = __uint_as_float(xa[i].x << 16), x1 = __uint_as_float(xa[i].x & 0xFFFF0000u);
+            const float x2 = __uint_as_float(xa[i].y << 16), x3 = __uint_as_float(xa[i].y & 0xFFFF0000u);
+            dot_pair(s, c, wv[i].x, x0);
+            dot_pair(s, c, wv[i].y, x1);
+            dot_pair(s, c, wv[i].z, x2);
+            dot_pair(s, c, wv[i].w, x3);
+            av += fabsf(wv[i].x * x0) + fabsf(wv[i].y * x1) + fabsf(wv[i].z * x2) + fabsf(wv[i].w * x3);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float os = __shfl_xor_sync(0xffffffffu, s, o), oc = __shfl_xor_sync(0xffffffffu, c, o);
+            c = __fadd_rn(c, oc);
+            two_sum_into(s, c, os);
+            av += __shfl_xor_sync(0xffffffffu, av, o);
+        }
+        if (lane == 0) {
+            part[wp][t] = (double)s + (double)c;
+            apart[wp][t] = av;
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < RS_IT; ++i) {
+            xa[i] = xb[i];
+            xb[i] = xc[i];
+        }
+    }
+    __syncthreads();
+    for (uint32_t t = threadIdx.x; t < T; t += blockDim.x) {
+        double v = part[0][t];
+        float av = apart[0][t];
+        for (int q = 1; q < 8; ++q) {  // the eighths in order
+            v += part[q][t];
+            av += apart[q][t];
+        }
+        L[(size_t)t * E + e] = (float)v;
+        Ld[(size_t)t * E + e] = v;
+        sabs[(size_t)t * E + e] = av;
+    }
+}
+int launch_router_logits_few(const uint16_t *x, const float *w, float *L, double *Ld, float *sabs, uint32_t T,
+                             uint32_t E, uint32_t H, cudaStream_t s) {
+    if (T > RS_TMAX || H % 32 || H > 32 * 32 * RS_IT || (reinterpret_cast<uintptr_t>(x) & 7) ||
+        (reinterpret_cast<uintptr_t>(w) & 15))
+        return CK_ERR_SHAPE;
+    if (!T || !E) return 0;
+    k_router_logits_few<<<E, 256, 0, s>>>(x, w, L, Ld, sabs, T, E, H);
+    return (int)cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ 2. fast selection
 // One warp per token; lane l holds experts e = 32*i + l.  At most 256 experts, 16 selections.
 constexpr int RMAX = 8;
-__global__ void k_route_select(const float *__restrict__ L, const float *__restrict__ bias, int32_t *__restrict__ ids,
-                               float *__restrict__ wts, uint32_t *__restrict__ flag_list,
-                               uint32_t *__restrict__ flag_count, RouteParams p) {
+CK_DEV float sel_exp(float v) { return expf(v); }
+CK_DEV double sel_exp(double v) { return exp(v); }
+template <typename T>
+CK_DEV T sel_max(T a, T b) { return a > b ? a : b; }
+template <typename T>
+CK_DEV T sel_min(T a, T b) { return a < b ? a : b; }
+template <typename T>
+CK_DEV void warp_argmax_t(T &v, int &i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const T ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+    }
+}
+template <typename T>
+CK_DEV T warp_sum_t(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// T = float: logits from the tensor cores, flagged below tau or 16 fp32 roundings of the largest
+// logit.  T = double: logits from the decode-batch matvec, accurate to about 2^-44 of sum|w x|
+// (`sabs` holds that sum per logit); the reference's own fold differs from the exact sum by at most
+// 7168 x 2^-53 of it, so a token is flagged only when its margin is below 16 x 2^-40 of its largest
+// sum|w x| -- in practice only exact ties take the fp64 re-route.
+template <typename T>
+__global__ void k_route_select(const T *__restrict__ L, const float *__restrict__ sabs,
+                               const float *__restrict__ bias, int32_t *__restrict__ ids, float *__restrict__ wts,
+                               uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p) {
     const int lane = threadIdx.x & 31;
     const uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (t >= p.ntok) return;
-    const float NEG = -3.0e38f;
-    float sc[RMAX], pr[RMAX];
+    const T NEG = (T)-3.0e38f;
+    T sc[RMAX], pr[RMAX];
     const int nreg = (int)((p.ne + 31) / 32);
+    float lmax = 0.0f;  // max |logit| (float form) or max sum|w x| (double form) of the token
 #pragma unroll
     for (int i = 0; i < RMAX; ++i) {
         const int e = 32 * i + lane;
         const bool v = i < nreg && e < (int)p.ne;
-        const float l = v ? L[(size_t)t * p.ne + e] : NEG;
+        const T l = v ? L[(size_t)t * p.ne + e] : NEG;
+        if (v) lmax = fmaxf(lmax, sabs ? sabs[(size_t)t * p.ne + e] : fabsf((float)l));
         if (p.mode == 4) {
-            pr[i] = v ? 1.0f / (1.0f + expf(-l)) : 0.0f;
-            sc[i] = v ? pr[i] + bias[e] : NEG;
+            pr[i] = v ? (T)1 / ((T)1 + sel_exp(-l)) : (T)0;
+            sc[i] = v ? pr[i] + (T)bias[e] : NEG;
         } else {
             pr[i] = l;
             sc[i] = l;
         }
     }
-    float margin = 3.0e38f;
+    T margin = (T)3.0e38f;
     bool allowed[RMAX];
 #pragma unroll
     for (int i = 0; i < RMAX; ++i) allowed[i] = true;
     if (p.mode == 4 && p.ngroups > 1) {
         // group score = sum of the group's two best scores (ties: lower index first, like dsv4-topk)
         const int gs = (int)(p.ne / p.ngroups);
-        float gsc[32];
+        T gsc[32];
         for (int g = 0; g < (int)p.ngroups; ++g) {
-            float b1 = NEG, b2 = NEG;
+            T b1 = NEG, b2 = NEG;
             int i1 = 1 << 30;
 #pragma unroll
             for (int i = 0; i < RMAX; ++i) {
                 const int e = 32 * i + lane;
                 if (e / gs == g && sc[i] > b1) { b1 = sc[i]; i1 = e; }
             }
-            float v = b1;
+            T v = b1;
             int vi = i1;
-            warp_argmax(v, vi);
-            const float best = v;
+            warp_argmax_t(v, vi);
+            const T best = v;
 #pragma unroll
             for (int i = 0; i < RMAX; ++i) {
                 const int e = 32 * i + lane;
                 if (e / gs == g && e != vi && sc[i] > b2) b2 = sc[i];
             }
             int dummy = 0;
-            warp_argmax(b2, dummy);
+            warp_argmax_t(b2, dummy);
             gsc[g] = b2 + best;  // tn-sum over (second, best): (0 + second) + best
         }
         // top groups by repeated argmax; the margin is min(chosen) - max(rejected)
         unsigned gmask = 0;
-        float gmin = 3.0e38f;
+        T gmin = (T)3.0e38f;
         for (int r = 0; r < (int)p.topk_groups; ++r) {
-            float bv = NEG;
+            T bv = NEG;
             int bi = 0;
             for (int g = 0; g < (int)p.ngroups; ++g)
                 if (!(gmask >> g & 1) && gsc[g] > bv) { bv = gsc[g]; bi = g; }
             gmask |= 1u << bi;
-            gmin = fminf(gmin, bv);
+            gmin = sel_min(gmin, bv);
         }
-        float gmax = NEG;
+        T gmax = NEG;
         for (int g = 0; g < (int)p.ngroups; ++g)
-            if (!(gmask >> g & 1)) gmax = fmaxf(gmax, gsc[g]);
-        if ((int)p.topk_groups < (int)p.ngroups) margin = fminf(margin, gmin - gmax);
+            if (!(gmask >> g & 1)) gmax = sel_max(gmax, gsc[g]);
+        if ((int)p.topk_groups < (int)p.ngroups) margin = sel_min(margin, gmin - gmax);
 #pragma unroll
         for (int i = 0; i < RMAX; ++i) {
             const int e = 32 * i + lane;
@@ -148,15 +280,15 @@ __global__ void k_route_select(const float *__restrict__ L, const float *__restr
     }
     // expert selection, best first
     int sel[16];
-    float selv[16];
+    T selv[16];
     const int k = (int)p.nsel;
     for (int r = 0; r < k; ++r) {
-        float bv = NEG;
+        T bv = NEG;
         int bi = 1 << 30;
 #pragma unroll
         for (int i = 0; i < RMAX; ++i)
             if (allowed[i] && sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
-        warp_argmax(bv, bi);
+        warp_argmax_t(bv, bi);
         sel[r] = bi;
         selv[r] = bv;
 #pragma unroll
@@ -164,26 +296,26 @@ __global__ void k_route_select(const float *__restrict__ L, const float *__restr
             if (32 * i + lane == bi) allowed[i] = false;
     }
     {
-        float bv = NEG;
+        T bv = NEG;
         int bi = 1 << 30;
 #pragma unroll
         for (int i = 0; i < RMAX; ++i)
             if (allowed[i] && sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
-        warp_argmax(bv, bi);
-        if (bv > NEG) margin = fminf(margin, selv[k - 1] - bv);
+        warp_argmax_t(bv, bi);
+        if (bv > NEG) margin = sel_min(margin, selv[k - 1] - bv);
         // the list order of the chosen experts is part of the answer: two chosen experts closer
         // than the margin could be listed in the other order by an exact fold
-        for (int r = 1; r < k; ++r) margin = fminf(margin, selv[r - 1] - selv[r]);
+        for (int r = 1; r < k; ++r) margin = sel_min(margin, selv[r - 1] - selv[r]);
     }
     // weights
-    float w[16];
+    T w[16];
     if (p.mode == 4) {
         // dsv4-topk lists the picks last-first; weights from the unbiased probs, sum floored at
         // 2^-14, times wscale / sum (dsv4-forward.fk:105-111)
-        float s0 = 0.0f;
+        T s0 = (T)0;
         for (int r = 0; r < k; ++r) {
             const int e = sel[k - 1 - r];
-            float pe = 0.0f;
+            T pe = (T)0;
 #pragma unroll
             for (int i = 0; i < RMAX; ++i)
                 if (32 * i + lane == e) pe = pr[i];
@@ -191,33 +323,38 @@ __global__ void k_route_select(const float *__restrict__ L, const float *__restr
             w[r] = pe;
             s0 += pe;
         }
-        const float s = s0 < 6.103515625e-05f ? 6.103515625e-05f : s0;
-        const float scl = p.wscale / s;
+        const T s = s0 < (T)6.103515625e-05f ? (T)6.103515625e-05f : s0;
+        const T scl = (T)p.wscale / s;
         for (int r = 0; r < k; ++r) w[r] *= scl;
         if (lane == 0)
             for (int r = 0; r < k; ++r) {
                 ids[(size_t)t * k + r] = sel[k - 1 - r];
-                wts[(size_t)t * k + r] = w[r];
+                wts[(size_t)t * k + r] = (float)w[r];
             }
     } else {
         // softmax over all experts (max-subtracted), the chosen probabilities, best first
-        float mx = NEG;
+        T mx = NEG;
 #pragma unroll
-        for (int i = 0; i < RMAX; ++i) mx = fmaxf(mx, sc[i]);
+        for (int i = 0; i < RMAX; ++i) mx = sel_max(mx, sc[i]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float s = 0.0f;
+        for (int o = 16; o > 0; o >>= 1) mx = sel_max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        T s = (T)0;
 #pragma unroll
         for (int i = 0; i < RMAX; ++i)
-            if (32 * i + lane < (int)p.ne) s += expf(sc[i] - mx);
-        s = warp_sum(s);
+            if (32 * i + lane < (int)p.ne) s += sel_exp(sc[i] - mx);
+        s = warp_sum_t(s);
         if (lane == 0)
             for (int r = 0; r < k; ++r) {
                 ids[(size_t)t * k + r] = sel[r];
-                wts[(size_t)t * k + r] = expf(selv[r] - mx) / s;
+                wts[(size_t)t * k + r] = (float)(sel_exp(selv[r] - mx) / s);
             }
     }
-    if (lane == 0 && !(margin >= p.tau)) {
+    // the threshold: tau, or 16 roundings of the largest logit (float form) / 16 x 2^-40 of the
+    // largest sum|w x| (double form) when that is larger
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    const T tau = sel_max((T)p.tau, (T)(sabs ? 16.0 * 9.094947017729282e-13 * lmax : 16.0 * 5.9604645e-8 * lmax));
+    if (lane == 0 && !(margin > tau)) {  // an exact tie (margin 0) always goes to the exact path
         const uint32_t slot = atomicAdd(flag_count, 1u);
         flag_list[slot] = t;
     }
@@ -373,7 +510,23 @@ int launch_route_select(const float *L, const float *bias, int32_t *ids, float *
         return CK_ERR_SHAPE;
     if (p.mode == 4 && !bias) return CK_ERR_ARG;
     cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
-    if (p.ntok) k_route_select<<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, bias, ids, wts, flag_list, flag_count, p);
+    if (p.ntok)
+        k_route_select<float><<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, nullptr, bias, ids, wts, flag_list,
+                                                                          flag_count, p);
+    return (int)cudaGetLastError();
+}
+int launch_route_select_d(const double *L, const float *sabs, const float *bias, int32_t *ids, float *wts,
+                          uint32_t *flag_list, uint32_t *flag_count, const RouteParams &p, cudaStream_t s) {
+    if (p.ne == 0 || p.ne > 32 * RMAX || p.nsel == 0 || p.nsel > 16 || p.nsel > p.ne) return CK_ERR_SHAPE;
+    if (p.mode == 4 && (p.ngroups == 0 || p.ngroups > 32 || p.ne % p.ngroups || p.topk_groups == 0 ||
+                        p.topk_groups > p.ngroups || p.nsel > p.topk_groups * (p.ne / p.ngroups)))
+        return CK_ERR_SHAPE;
+    if (p.mode == 4 && !bias) return CK_ERR_ARG;
+    if (!sabs) return CK_ERR_ARG;
+    cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
+    if (p.ntok)
+        k_route_select<double><<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, sabs, bias, ids, wts, flag_list,
+                                                                           flag_count, p);
     return (int)cudaGetLastError();
 }
 int launch_route_softmax_tokens(const float *L, uint32_t *ids, float *wts, uint32_t ne, uint32_t nsel, uint32_t ntok,

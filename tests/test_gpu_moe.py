@@ -134,3 +134,47 @@ def test_moe_exact_reroute_covers_ties():
     cfg = O.moe_cfg(256, 128, 16, 1, 4, 4, 4, 2, 2.5)
     rids, rwts, _ = O.moe_route(cfg, w["router"], w["bias"], w["x"])
     assert np.array_equal(ids, rids)
+
+
+def test_moe_dsv3_decode_sizes():
+    """At most 64 tokens (a decode-sized batch) the router logits run as a matvec with compensated
+    float-pair sums (accurate to the logits' fp32 rounding) and few flagged tokens take one exact
+    fold chain per lane: ids, counts and weights against the oracle's routing at 1, 3, 8 and 64
+    tokens, outputs against the oracle's layer up to 8."""
+    spec = workloads.MOE_DSV3
+    w = workloads.make_moe(spec, 64, seed=5)
+    lay = layer_for(spec, w, 64)
+    cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
+                    spec.topk_groups, spec.wscale)
+    for n in (1, 3, 8, 64):
+        x = np.ascontiguousarray(w["x"][:n])
+        out, ids, wts, counts = lay(torch.from_numpy(x.view(np.int16)).cuda())
+        lay.status(n)
+        logits = lay._ws_views(n)["logits"].cpu().numpy()
+        ref_logits = synth.bf16_bits_to_f32(x).astype(np.float64) @ w["router"].astype(np.float64).T
+        assert np.abs(logits - ref_logits).max() <= 2e-6
+        rids, rwts, _ = O.moe_route(cfg, w["router"], w["bias"], x)
+        ids, wts, counts = ids.cpu().numpy(), wts.cpu().numpy(), counts.cpu().numpy()
+        assert np.array_equal(ids, rids)
+        assert np.array_equal(counts, np.bincount(rids.reshape(-1), minlength=spec.n_experts))
+        assert np.allclose(wts, rwts, rtol=1e-5, atol=1e-7)
+        if n <= 8:
+            sids, _, sout = O.moe_layer(cfg, w, x, np.arange(n))
+            assert np.array_equal(sids, ids)
+            check_outputs(out.float().cpu().numpy(), sout)
+
+
+def test_moe_decode_tie_reroute():
+    # four tokens: the logits take the fp64 matvec, and token 0 (all-zero activations, zero bias)
+    # ties everywhere, so the exact re-route's few-token form must pick the reference's experts
+    spec = MoeSpec(256, 128, 16, 1, 4, 4, 4, 2, 2.5)
+    w = workloads.make_moe(spec, 4, seed=9)
+    w["x"][0, :] = 0
+    w["bias"][:] = 0
+    keep = {}
+    out, ids, wts, counts = run_layer(spec, w, w["x"], keep)
+    assert keep["flagged"] >= 1
+    cfg = O.moe_cfg(256, 128, 16, 1, 4, 4, 4, 2, 2.5)
+    rids, rwts, _ = O.moe_route(cfg, w["router"], w["bias"], w["x"])
+    assert np.array_equal(ids, rids)
+    assert np.allclose(wts, rwts, rtol=1e-5, atol=1e-7)
