@@ -494,11 +494,12 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(spec, {k: w[k] for k in w}) if len(experts) == spec.n_experts else None
-        # our kernels per step: route 6 (split, tiles, logits GEMM, select, exact logits, exact
-        # select), permute 3, GEMM 2, combine 1; expert parallel gathers the dispatch rows (1) in
-        # place of the source permute, regroups on the receiver (permute 3), restores the pair order
-        # (1), and runs the shared expert's token tiles + 2 GEMMs per shared expert on a side stream
-        launches_per_step = 12 if world == 1 else 14 + 1 + 2 * spec.n_shared
+        # our kernels per step: route 7 (split, tiles, logits GEMM, select, the two forms of the
+        # exact logits, exact select), permute 3, GEMM 2, combine 1; expert parallel plans the
+        # exchange (1) and gathers the dispatch rows (1) in place of the source permute, regroups on
+        # the receiver (permute 3), restores the pair order (1), and runs the shared expert's token
+        # tiles + 2 GEMMs per shared expert on a side stream
+        launches_per_step = 13 if world == 1 else 16 + 1 + 2 * spec.n_shared
         line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",

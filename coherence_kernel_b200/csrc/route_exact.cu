@@ -14,8 +14,8 @@
 //
 // Two kernels: k_exact_logits spreads (token, expert) right folds over the whole GPU (each fold is a
 // 7168-long dependent chain, so many chains must be in flight) -- tiled over 16 tokens x 64 experts
-// when more than 32 tokens are flagged, one chain per lane fed by a cp.async ring
-// (k_exact_logits_few) when at most 32 are; k_exact_select is one CTA per token.
+// when more than 128 tokens are flagged, one chain per lane fed by a cp.async ring
+// (k_exact_logits_few) when at most 128 are; k_exact_select is one CTA per token.
 #include "ck_common.cuh"
 #include "ck_launch.h"
 
@@ -58,7 +58,7 @@ constexpr int XL_TPT = 4;    // tokens (independent fold chains) per thread
 // router row's next columns eight at a time (two 16-byte cp.async) into a per-warp ring of
 // XF_NB stages in shared memory, lane 0 copies the token's eight activations beside them, and the
 // chain consumes stage i while stages i+1 .. i+XF_NB-1 are in flight.  Same fold, same bits.
-constexpr uint32_t XL_FEW = 32;
+constexpr uint32_t XL_FEW = 128;  // 8 items per token: one item per warp at two CTAs per SM
 constexpr int XF_NB = 24;       // ring stages per warp (8 columns each)
 constexpr int XF_WARPS = 4;     // warps per CTA in the few-token form
 struct XfRing {
@@ -381,8 +381,8 @@ int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int
         few_attr = true;
     }
     // both forms are launched; each returns at once unless the flagged count is its own
-    k_exact_logits_few<<<nsm, XF_WARPS * 32, XF_WARPS * sizeof(XfRing), s>>>(x, w, flag_list, flag_count, scratch,
-                                                                            p.ne, p.hidden);
+    k_exact_logits_few<<<2 * nsm, XF_WARPS * 32, XF_WARPS * sizeof(XfRing), s>>>(x, w, flag_list, flag_count,
+                                                                                scratch, p.ne, p.hidden);
     k_exact_logits<<<nsm * 2, 256, 0, s>>>(x, w, flag_list, flag_count, scratch, p.ne, p.hidden);
     k_exact_select<<<nsm * 2, 256, 0, s>>>(scratch, bias, ids, wts, flag_list, flag_count, p);
     return (int)cudaGetLastError();
