@@ -469,7 +469,7 @@ def main():
     # stream) and step i-1's download (another) run beside step i's layer, double-buffered on the
     # device; the timed region runs from before the first timed upload to after the last download
     e2e = None
-    if world == 1:
+    if True:
         xh = torch.from_numpy(np.ascontiguousarray(x_host.view(np.int16))).pin_memory()
         oh = [torch.empty((T, spec.hidden), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
         xd = [torch.empty_like(x) for _ in range(2)]
@@ -498,7 +498,10 @@ def main():
                     upload(i + 1)
                 stream.wait_event(in_ready[b])
                 stream.wait_event(out_free[b])
-                layer(xd[b], out=od[b], ids=ids, wts=wts, counts=counts)
+                if world == 1:
+                    layer(xd[b], out=od[b], ids=ids, wts=wts, counts=counts)
+                else:
+                    layer(xd[b], out=od[b])
                 in_free[b].record(stream)
                 out_ready[b].record(stream)
                 down.wait_event(out_ready[b])
@@ -508,6 +511,8 @@ def main():
             stream.wait_stream(down)
         run(args.warmup)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         run(args.steps, start=e0)
@@ -515,9 +520,14 @@ def main():
         e1.record(stream)
         torch.cuda.synchronize()
         e_ms = e0.elapsed_time(e1) / args.steps
-        e2e = {"value": T_all / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(xh.numel() * 2),
-               "d2h_bytes_per_step": int(oh[0].numel() * 2), "ms_per_step": round(e_ms, 4),
-               "copies": "pipelined: upload of step i+1 and download of step i-1 beside step i"}
+        if world > 1:
+            m = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(m, op=dist.ReduceOp.MAX)
+            e_ms = float(m.item())
+        e2e = {"value": T_all / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(xh.numel() * 2) * world,
+               "d2h_bytes_per_step": int(oh[0].numel() * 2) * world, "ms_per_step": round(e_ms, 4),
+               "copies": "pipelined: upload of step i+1 and download of step i-1 beside step i; bytes summed "
+                         "over the ranks, time the max over ranks"}
 
     subs = None
     if world == 1 and args.shard == 1 and not args.no_sub:
