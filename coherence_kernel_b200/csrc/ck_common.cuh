@@ -69,6 +69,16 @@ CK_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking probe of a phase: far cheaper than try_wait when the phase has already completed.
+CK_DEV bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 CK_DEV uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -77,7 +87,7 @@ CK_DEV uint64_t globaltimer_ns() {
 // Bounded wait: gives up after about one second, records `code` in the error word and returns
 // false, so a broken pipeline ends the kernel with a status the host reads instead of hanging.
 CK_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err, int code) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;

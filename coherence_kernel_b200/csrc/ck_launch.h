@@ -24,6 +24,9 @@ int launch_q80_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows
 bool gemv_stream_ok(const void *qb, const float *x, uint32_t cols);
 int launch_gemv_stream(int kind, const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols,
                        cudaStream_t s);
+// tensor-core Q4_K decode matvec (gemv_tc.cu): cols % 256 == 0, weights and x 16-byte aligned
+bool gemv_tc_ok(const void *qb, const float *x, uint32_t rows, uint32_t cols);
+int launch_gemv_tc(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
 int launch_f16_matvec(const uint16_t *w, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
 int launch_scale(const float *x, float *y, float a, uint32_t n, cudaStream_t s);
 int launch_axpy(const float *x, float *y, float a, uint32_t n, cudaStream_t s);

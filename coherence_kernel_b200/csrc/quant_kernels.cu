@@ -290,7 +290,14 @@ int launch_matvec_ordered(int kind, const uint8_t *qb, const float *x, float *y,
 int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
                       cudaStream_t s) {
     if (cols % 64 != 0) return CK_ERR_SHAPE;
-    if (ntok == 1 && gemv_stream_ok(qb, x, cols)) {
+    // one token: the tensor-core matvec from about 12 MB of weights up (and wherever the streaming
+    // kernel's x does not fit its shared memory), the streaming one below that, where its shorter
+    // fixed cost per launch wins
+    const bool stream_ok = gemv_stream_ok(qb, x, cols);
+    if (ntok == 1 && gemv_tc_ok(qb, x, rows, cols) &&
+        (!stream_ok || (uint64_t)rows * (cols / 256) * Q4K_BYTES >= (12ull << 20))) {
+        return launch_gemv_tc(qb, x, y, rows, cols, s);
+    } else if (ntok == 1 && stream_ok) {
         return launch_gemv_stream(12, qb, x, y, rows, cols, s);
     } else if (ntok == 1) {
         k_q4k_matvec_fast<1><<<dim3(nblk(rows, 8), 1), 256, 0, s>>>(qb, x, y, rows, cols, 1);

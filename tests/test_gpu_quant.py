@@ -81,6 +81,46 @@ def test_q4k_matvec_sizes(rows, cols):
         assert abs(y[r] - ref) <= 1e-3 * np.abs(w * x).sum(), r
 
 
+def q4k_rows_check(q, x, y, rows, cols, nsample=64, tol=1e-3):
+    sample = np.unique(np.linspace(0, rows - 1, nsample).astype(int))
+    x64 = x.astype(np.float64)
+    for r in sample:
+        w = O.q4k_dequant(q, r * cols, cols)
+        ref = O.lib().ckr_dot(w.ctypes.data, x64.ctypes.data, cols)
+        assert abs(y[r] - ref) <= tol * np.abs(w * x64).sum(), (r, y[r], ref)
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 11008), (19000, 4096), (1000, 8448), (777, 9216), (5, 8448),
+                                       (300, 16384), (129, 12288)])
+def test_q4k_matvec_tensor_core_shapes(rows, cols):
+    """One token through the tensor-core matvec (from about 12 MB of weights, or cols beyond the
+    streaming kernel's limit): ragged last tiles, K splits of 1, 2 and 4 CTAs, a 149-tile grid."""
+    rng = np.random.default_rng(rows * 3 + cols)
+    q = synth.make_q4k(rng, rows * cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = ops.q4k_matvec(dev(q), dev(x), rows, cols).cpu().numpy()
+    assert np.all(np.isfinite(y))
+    q4k_rows_check(q, x, y, rows, cols, nsample=48)
+
+
+def test_q4k_matvec_tensor_core_dynamic_range():
+    """x scaled per 32-value sub-block over 1e-40 .. 1e25, with all-zero sub-blocks: the matvec holds
+    each sub-block of x as a fixed-point integer relative to its own power-of-two bound."""
+    rows, cols = 777, 9216
+    rng = np.random.default_rng(11)
+    q = synth.make_q4k(rng, rows * cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    x[0:256] = 0
+    x[256:512] *= np.float32(1e-30)
+    x[512:768] *= np.float32(1e25)
+    x[768:800] = 0
+    x[1024:1056] = np.float32(1e-40)
+    x[2048:2080] *= np.float32(3e-12)
+    y = ops.q4k_matvec(dev(q), dev(x), rows, cols).cpu().numpy()
+    assert np.all(np.isfinite(y))
+    q4k_rows_check(q, x, y, rows, cols, nsample=32)
+
+
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (64, 96), (1000, 2048), (999, 256), (513, 7168), (64, 8192),
                                        (3, 1280)])
 def test_q8_0_matvec_sizes(rows, cols):
