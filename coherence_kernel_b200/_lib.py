@@ -58,6 +58,8 @@ SIGNATURES = {
     "ck_moe_permute": (_i32, [_p, _p, _p, _u32, _u32, _u32, _u32, _u32, _i32, _p, _p, _p, _p, _p, _p, _p, _p]),
     "ck_moe_expert_gemm": (_i32, [_i32, _p, _p, _p, _p, _u64, _u32, _u32, _p, _u32, _p, _u32, _p, _p, _p, _u32, _u32,
                                   _u32, _i32, _p, _p]),
+    "ck_moe_expert_gemm_bounded": (_i32, [_i32, _p, _p, _p, _p, _u64, _u32, _u32, _p, _u32, _p, _u32, _p, _p, _p,
+                                          _u32, _u32, _u32, _i32, _u32, _p, _p]),
     "ck_moe_combine": (_i32, [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _i32, _p, _p, _p]),
     "ck_token_tiles": (_i32, [_p, _p, _u32, _p]),
     "ck_gather_rows": (_i32, [_p, _p, _p, _u32, _u32, _p]),

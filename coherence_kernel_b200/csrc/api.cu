@@ -67,6 +67,15 @@ struct MoeWs {
     size_t total;
 };
 
+// Token tiles of the permute's table: decode-sized batches (at most CK_MOE_DECODE_TOKENS tokens) cut
+// them to CK_MOE_FEW_TOKENS tokens, so that every tile fits the few-token grouped matvec; larger
+// batches use the grouped GEMM's tiles of up to GEMM_TILE_TOKENS.  (Cutting batches of 16 and 64
+// tokens into 8-token tiles for the matvec measured slower than the GEMM on the gate/up matrices:
+// its per-step epilogue work grows with the tokens per tile.)
+uint32_t moe_tile_tokens(uint32_t ntok) {
+    return ntok <= CK_MOE_DECODE_TOKENS ? (uint32_t)CK_MOE_FEW_TOKENS : ck::GEMM_TILE_TOKENS;
+}
+
 ck::PermuteParams perm_params(const ck_moe_config *c, uint32_t ntok) {
     ck::PermuteParams p;
     p.ntok = ntok;
@@ -74,7 +83,7 @@ ck::PermuteParams perm_params(const ck_moe_config *c, uint32_t ntok) {
     p.n_experts = c->n_experts;
     p.n_shared = c->n_shared;
     p.hidden = c->hidden;
-    p.bn = ck::GEMM_TILE_TOKENS;
+    p.bn = moe_tile_tokens(ntok);
     p.weight_in_mid = c->mode == 4 ? 1 : 0;
     return p;
 }
@@ -225,8 +234,15 @@ int ck_swiglu_f32(const float *g, const float *u, float *o, uint32_t n, float w,
 
 // ------------------------------------------------------------------------------ MoE layer
 uint32_t ck_moe_max_tiles(uint32_t ntok, uint32_t nsel, uint32_t n_experts, uint32_t n_shared) {
-    const uint64_t A = (uint64_t)ntok * nsel;
-    return (uint32_t)(n_experts + A / 128 + 1 + (uint64_t)n_shared * (ntok / 128 + 2));
+    // A segment of c rows makes ceil(c / bn) tiles (permute's seg_tiles), at most c / bn + 1.  The
+    // bound is monotone in ntok, so a table sized for ntok also holds the tiles of any smaller batch,
+    // whose tiles may be the shorter decode-sized ones (a caller sizes once for its largest batch).
+    const auto bound = [&](uint64_t t, uint64_t bn) {
+        return n_experts + t * nsel / bn + 1 + (uint64_t)n_shared * (t / bn + 2);
+    };
+    const uint64_t few = bound(ntok < CK_MOE_DECODE_TOKENS ? ntok : CK_MOE_DECODE_TOKENS, CK_MOE_FEW_TOKENS);
+    const uint64_t big = ntok > CK_MOE_DECODE_TOKENS ? bound(ntok, 128) : 0;
+    return (uint32_t)(few > big ? few : big);
 }
 size_t ck_moe_permute_workspace_bytes(uint32_t ntok, uint32_t nsel, uint32_t n_experts) {
     ck::PermuteParams p = {};
@@ -309,7 +325,8 @@ int ck_moe_route_flagged(const ck_moe_config *c, uint32_t ntok, const void *ws, 
 int ck_moe_permute(const int32_t *ids, const float *wts, const void *x, uint32_t ntok, uint32_t nsel,
                    uint32_t n_experts, uint32_t n_shared, uint32_t hidden, int weight_in_mid, void *xp, float *row_w,
                    int32_t *pair_pos, int32_t *counts, void *tiles, int32_t *ntiles, void *ws, void *s) {
-    ck::PermuteParams p = {ntok, nsel, n_experts, n_shared, hidden, ck::GEMM_TILE_TOKENS, (uint32_t)(weight_in_mid ? 1 : 0)};
+    ck::PermuteParams p = {ntok, nsel, n_experts, n_shared, hidden, moe_tile_tokens(ntok),
+                           (uint32_t)(weight_in_mid ? 1 : 0)};
     return fail(ck::launch_permute(ids, wts, (const uint16_t *)x, (uint16_t *)xp, row_w, pair_pos, counts,
                                    (int4 *)tiles, ntiles, ws, p, S(s)),
                 "ck_moe_permute");
@@ -319,7 +336,17 @@ int ck_moe_expert_gemm(int dual, const void *w0, const void *w1, const void *s0,
                        uint32_t n_routed, uint32_t n_shared, const void *x, uint32_t x_rows, void *out,
                        uint32_t out_rows, const float *row_w, const void *tiles, const int32_t *ntiles,
                        uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow, int *err, void *s) {
+    return ck_moe_expert_gemm_bounded(dual, w0, w1, s0, s1, w_stride, n_routed, n_shared, x, x_rows, out, out_rows,
+                                      row_w, tiles, ntiles, max_tiles, n, k, xrow_is_orow, 0, err, s);
+}
+
+int ck_moe_expert_gemm_bounded(int dual, const void *w0, const void *w1, const void *s0, const void *s1,
+                               uint64_t w_stride, uint32_t n_routed, uint32_t n_shared, const void *x, uint32_t x_rows,
+                               void *out, uint32_t out_rows, const float *row_w, const void *tiles,
+                               const int32_t *ntiles, uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow,
+                               uint32_t max_tile_tokens, int *err, void *s) {
     ck::GemmParams p = {};
+    p.max_tile_tok = max_tile_tokens;
     p.w0 = (const uint8_t *)w0;
     p.w1 = (const uint8_t *)w1;
     p.s0 = (const uint8_t *)s0;
@@ -389,11 +416,15 @@ int ck_moe_layer_bf16(const ck_moe_config *c, const void *x, uint32_t ntok, cons
     if (rc) return rc;
     const uint32_t mt = ck_moe_max_tiles(ntok, c->nsel, c->n_experts, c->n_shared);
     const uint64_t stride = (uint64_t)c->inter * c->hidden / 256 * 144;
-    rc = ck_moe_expert_gemm(1, wg, wu, sg, su, stride, c->n_experts, c->n_shared, w.xp, A + ntok, w.h, R, w.row_w,
-                            w.tiles, w.ntiles, mt, c->inter, c->hidden, 0, w.err, s);
+    // every tile holds at most ntok tokens (a token picks an expert once; the shared tiles take the
+    // ntok tokens), and at most CK_MOE_FEW_TOKENS in a decode-sized batch: there the expert weights
+    // stream through the grouped matvec
+    const uint32_t bound = ntok <= CK_MOE_DECODE_TOKENS ? (ntok < CK_MOE_FEW_TOKENS ? ntok : CK_MOE_FEW_TOKENS) : 0;
+    rc = ck_moe_expert_gemm_bounded(1, wg, wu, sg, su, stride, c->n_experts, c->n_shared, w.xp, A + ntok, w.h, R,
+                                    w.row_w, w.tiles, w.ntiles, mt, c->inter, c->hidden, 0, bound, w.err, s);
     if (rc) return rc;
-    rc = ck_moe_expert_gemm(0, wd, nullptr, sd, nullptr, stride, c->n_experts, c->n_shared, w.h, R, w.y, R, nullptr,
-                            w.tiles, w.ntiles, mt, c->hidden, c->inter, 1, w.err, s);
+    rc = ck_moe_expert_gemm_bounded(0, wd, nullptr, sd, nullptr, stride, c->n_experts, c->n_shared, w.h, R, w.y, R,
+                                    nullptr, w.tiles, w.ntiles, mt, c->hidden, c->inter, 1, bound, w.err, s);
     if (rc) return rc;
     return ck_moe_combine(w.y, ids, wts, w.pair_pos, ntok, c->nsel, c->n_shared, c->hidden, c->mode == 3, out, nullptr,
                           s);

@@ -109,8 +109,13 @@ struct GemmParams {
     const void *a_dense;
     uint32_t kx;
     float *out_f32;
+    // a bound on the tokens of every tile (0: none known); 1..8 runs the few-token grouped matvec
+    // (moe_gemv.cu) where its shape rules hold
+    uint32_t max_tile_tok;
 };
 int launch_gemm_q4k(const GemmParams &p, cudaStream_t s);
+bool gemv_moe_ok(const GemmParams &p);
+int launch_gemv_moe(const GemmParams &p, cudaStream_t s);
 int launch_gemm_dense(const GemmParams &p, cudaStream_t s);
 // fp32 [rows, k] -> bf16 [rows, 3k]: w = w1 + w2 + w3 with each term the bf16 rounding of the
 // remainder (exact to about 2^-24 relative)

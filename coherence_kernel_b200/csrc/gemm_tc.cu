@@ -638,6 +638,8 @@ int launch_gemm_q4k(const GemmParams &p, cudaStream_t s) {
     if (p.K % gemm::BK != 0 || p.N == 0 || p.K == 0 || ((uint64_t)p.N * p.K) % 256 != 0) return CK_ERR_SHAPE;
     if (p.dual && !p.w1) return CK_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.w0) & 15)) return CK_ERR_ARG;
+    // tiles of at most eight tokens (a decode-sized batch): the weight-streaming grouped matvec
+    if (p.max_tile_tok && gemv_moe_ok(p)) return launch_gemv_moe(p, s);
     // TMA-staged packed weights when every row starts on a superblock and the tile is full height
     const bool pt = p.K % 256 == 0 && p.N >= (uint32_t)gemm::BM && !(reinterpret_cast<uintptr_t>(p.w0) & 15) &&
                     !(p.w1 && (reinterpret_cast<uintptr_t>(p.w1) & 15)) &&

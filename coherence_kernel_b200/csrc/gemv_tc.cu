@@ -31,12 +31,14 @@
 // wait is bounded (about one second); a CTA whose wait gives up writes NaN to its rows.
 #include "ck_common.cuh"
 #include "ck_launch.h"
+#include "tc_i8.cuh"
 
 #include <initializer_list>
 #include <mutex>
 
 namespace ck {
 namespace gtc {
+using namespace tci8;
 
 constexpr int NTHR = 640;
 constexpr int ROWS = 128;  // MMA M: rows per tile
@@ -61,40 +63,16 @@ constexpr uint32_t BAR_OFF = INBOX_OFF + (MAX_CLUSTER - 1) * (ROWS + 1) * 4 + 4;
 constexpr uint32_t SMEM = BAR_OFF + 512 + 1024;       // + barriers, + alignment slack
 constexpr uint32_t A_COLS = 64, D_OFF = NA * A_COLS, TMEM_COLS = 512;
 // kind::i8 instruction descriptor: D s32, A u8, B s8, both K-major, M x N
-constexpr uint32_t IDESC = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(NCOL >> 3) << 17) | ((uint32_t)(ROWS >> 4) << 24);
+constexpr uint32_t IDESC = idesc_u8s8(ROWS, NCOL);
 static_assert(D_OFF + ND * NCOL <= TMEM_COLS, "tensor memory");
 static_assert(SMEM <= 227 * 1024, "shared memory");
 
-CK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-CK_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-CK_DEV void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %3, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %4, p;\n}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(accumulate), "r"(IDESC)
-        : "memory");
-}
-// one lane of a converged warp
-CK_DEV bool elect_one() {
-    uint32_t pred = 0;
-    asm volatile("{\n .reg .b32 %%rx;\n .reg .pred %%px;\n elect.sync %%rx|%%px, %1;\n selp.u32 %0, 1, 0, %%px;\n}"
-                 : "=r"(pred)
-                 : "r"(0xffffffffu));
-    return pred != 0;
-}
 CK_DEV void tma_load_2d_u8(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
             smem_u32(dst)),
         "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
-}
-CK_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
 }
 CK_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 CK_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
@@ -116,15 +94,6 @@ CK_DEV void st_peer_u32(const void *local, uint32_t rank, uint32_t v) {
 CK_DEV void mbar_arrive_peer(uint64_t *local, uint32_t rank) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(peer_addr(local, rank))
                  : "memory");
-}
-// bytes 0 of a, b, c, d packed low to high
-CK_DEV uint32_t pack_b0(int a, int b, int c, int d) {
-    return __byte_perm(__byte_perm((uint32_t)a, (uint32_t)b, 0x0040), __byte_perm((uint32_t)c, (uint32_t)d, 0x0040),
-                       0x5410);
-}
-// byte offset of (row n, K kk) in a [32 x 128] s8 tile with the 128-byte swizzle
-CK_DEV uint32_t b_off(int n, int kk) {
-    return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((kk >> 4) ^ (n & 7))) << 4) + (kk & 15));
 }
 
 struct Params {
@@ -224,7 +193,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
                 const uint32_t dt = tmem + D_OFF + NCOL * ds, at = tmem + A_COLS * a;
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    umma_i8_ts(dt, at + 8 * k, (k < 4 ? bd0 : bd1) + (uint64_t)(2 * (k & 3)), k > 0 ? 1u : 0u);
+                    umma_i8_ts(dt, at + 8 * k, (k < 4 ? bd0 : bd1) + (uint64_t)(2 * (k & 3)), IDESC, k > 0 ? 1u : 0u);
                 umma_commit(&mma_done[ds]);
             }
             __syncwarp();
@@ -268,23 +237,10 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             sum += __shfl_xor_sync(0xffffffffu, sum, 1);
             sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            // |x| < 2^e: e = biased exponent of mx - 126, kept in [-100, 129] (zero -> 2^0)
-            int e = (int)((__float_as_uint(mx) >> 23) & 255u) - 126;
-            e = mx == 0.0f ? 0 : max(-100, e);
-            const float up = __uint_as_float((uint32_t)(127 + 22 - e) << 23);  // 2^(22-e)
-            int d0[8], d1[8], d2[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int X = __float2int_rn(xv[i] * up);  // |X| <= 2^22
-                const int X1 = (X + 128) >> 8, X0 = (X1 + 128) >> 8;
-                d2[i] = X;  // low bytes: the balanced digits
-                d1[i] = X1;
-                d0[i] = X0;
-            }
+            const int e = subblock_exponent(mx);
+            uint2 w0, w1, w2;
+            digits8(xv, e, w0, w1, w2);
             uint8_t *st = smem + B_OFF + bs * B_STAGE + toff;
-            const uint2 w0 = make_uint2(pack_b0(d0[0], d0[1], d0[2], d0[3]), pack_b0(d0[4], d0[5], d0[6], d0[7]));
-            const uint2 w1 = make_uint2(pack_b0(d1[0], d1[1], d1[2], d1[3]), pack_b0(d1[4], d1[5], d1[6], d1[7]));
-            const uint2 w2 = make_uint2(pack_b0(d2[0], d2[1], d2[2], d2[3]), pack_b0(d2[4], d2[5], d2[6], d2[7]));
             *reinterpret_cast<uint2 *>(st + b_off(4 * s + 0, kk0)) = w0;
             *reinterpret_cast<uint2 *>(st + b_off(4 * s + 1, kk0)) = w1;
             *reinterpret_cast<uint2 *>(st + b_off(4 * s + 2, kk0)) = w2;
@@ -292,7 +248,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
                 float *slot = xs + (j % XSL) * 16;
                 slot[s] = sum;
                 // 2^(e-22), and 2^(e-26) for the high nibbles (A holds 16 q there)
-                slot[8 + s] = __uint_as_float((uint32_t)(127 - 22 - 4 * (s & 1) + e) << 23);
+                slot[8 + s] = digit_scale(e, 4 * (s & 1));
             }
             fence_proxy_async_smem();  // generic writes of B, read by the tensor cores
             __syncwarp();
@@ -357,10 +313,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
                 const int i = s;
                 int scv, mv;
                 q4k_scale_min(hdr.y, hdr.z, hdr.w, s, scv, mv);
-                // each digit sum is exact in int32 and in fp32; their weighted sum is not in int32
-                const float sq = fmaf((float)(int)dv[4 * i], 65536.0f,
-                                      fmaf((float)(int)dv[4 * i + 1], 256.0f, (float)(int)dv[4 * i + 2]));
-                const float qx = sq * slot[8 + s];  // sum q x over the sub-block
+                const float qx = digit_sum(dv[4 * i], dv[4 * i + 1], dv[4 * i + 2]) * slot[8 + s];  // sum q x
                 acc = fmaf(d * (float)scv, qx, fmaf(-(dmin * (float)mv), slot[s], acc));
             }
             tc_fence_before();
@@ -400,22 +353,6 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
     }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-static EncodeTiledFn get_encode() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *f = nullptr;
-        cudaDriverEntryPointQueryResult qr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
-            qr == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(f);
-    });
-    return fn;
-}
-
 // Tile height and K split.  Within one wave of CTAs the time follows the superblocks each CTA
 // streams (its pipeline's cadence), not the bytes: so full 128-row tiles, and the largest split in
 // {1, 2, 4} that keeps every CTA resident and gives each at least two superblocks.  (Clusters of 8
@@ -430,6 +367,19 @@ static void plan(uint32_t rows, uint32_t nsb, uint32_t nsm, uint32_t &trows, uin
 
 }  // namespace gtc
 
+EncodeTiledFn tensor_map_encoder() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
 bool gemv_tc_ok(const void *qb, const float *x, uint32_t rows, uint32_t cols) {
     return cols % 256 == 0 && cols >= 256 && rows >= 1 && (reinterpret_cast<uintptr_t>(qb) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(x) & 15) == 0;
@@ -439,7 +389,7 @@ namespace gtc {
 static int launch(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t trows,
                   uint32_t csize, cudaStream_t s) {
     if (trows == 0 || trows > ROWS || csize == 0 || csize > MAX_CLUSTER) return CK_ERR_ARG;
-    gtc::EncodeTiledFn enc = gtc::get_encode();
+    EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return CK_ERR_NODEV;
     const uint32_t nsb = cols / 256, row_bytes = nsb * Q4K_BYTES;
     CUtensorMap map;

@@ -187,7 +187,7 @@ int launch_permute(const int32_t *ids, const float *wts, const uint16_t *x, uint
                    int32_t *pair_pos, int32_t *counts, int4 *tiles, int32_t *ntiles, void *workspace,
                    const PermuteParams &p, cudaStream_t s) {
     if (p.n_experts == 0 || p.n_experts > MAX_EXPERTS || p.nsel == 0 || p.hidden % 8 != 0 || p.bn == 0 ||
-        p.bn % 16 != 0)
+        p.bn % 8 != 0 || p.bn > GEMM_TILE_TOKENS)
         return CK_ERR_SHAPE;
     if (!ids || !x || !xp || !row_w || !pair_pos || !counts || !tiles || !ntiles || !workspace) return CK_ERR_ARG;
     PermWs w = carve(workspace, p);

@@ -21,6 +21,12 @@ import torch
 from . import _lib
 from .ops import _dev, _ptr, _stream, q4k_nbytes
 
+# CK_MOE_FEW_TOKENS / CK_MOE_DECODE_TOKENS of ck_b200.h: batches up to DECODE_TOKENS tokens are
+# permuted into tiles of at most FEW_TOKENS tokens and run the expert projections as the few-token
+# grouped matvec
+FEW_TOKENS = 8
+DECODE_TOKENS = 8
+
 
 @dataclass
 class MoeSpec:
@@ -114,14 +120,15 @@ class MoELayer:
                                     _ptr(w["ntiles"]), _ptr(w["perm_ws"]), st), "permute")
         mark("permute")
         mb = sp.matrix_bytes
-        _lib.check(L.ck_moe_expert_gemm(1, _ptr(self.w[0]), _ptr(self.w[1]), _ptr(self.s[0]), _ptr(self.s[1]), mb, E,
-                                         sp.n_shared, _ptr(w["xp"]), A + T, _ptr(w["h"]), R, _ptr(w["row_w"]), _ptr(w["tiles"]),
-                                         _ptr(w["ntiles"]), w["mt"], I, H, 0, _ptr(w["err"]), st), "gate/up")
+        bound = min(T, FEW_TOKENS) if T <= DECODE_TOKENS else 0  # the most tokens any tile holds
+        _lib.check(L.ck_moe_expert_gemm_bounded(1, _ptr(self.w[0]), _ptr(self.w[1]), _ptr(self.s[0]), _ptr(self.s[1]),
+                                                 mb, E, sp.n_shared, _ptr(w["xp"]), A + T, _ptr(w["h"]), R,
+                                                 _ptr(w["row_w"]), _ptr(w["tiles"]), _ptr(w["ntiles"]), w["mt"], I, H, 0,
+                                                 bound, _ptr(w["err"]), st), "gate/up")
         mark("gate_up")
-        _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, _ptr(self.s[2]), None, mb, E, sp.n_shared,
-                                         _ptr(w["h"]), R,
-                                         _ptr(w["y"]), R, None, _ptr(w["tiles"]), _ptr(w["ntiles"]), w["mt"], H, I, 1,
-                                         _ptr(w["err"]), st), "down")
+        _lib.check(L.ck_moe_expert_gemm_bounded(0, _ptr(self.w[2]), None, _ptr(self.s[2]), None, mb, E, sp.n_shared,
+                                                 _ptr(w["h"]), R, _ptr(w["y"]), R, None, _ptr(w["tiles"]),
+                                                 _ptr(w["ntiles"]), w["mt"], H, I, 1, bound, _ptr(w["err"]), st), "down")
         mark("down")
         _lib.check(L.ck_moe_combine(_ptr(w["y"]), _ptr(ids), _ptr(wts), _ptr(w["pair_pos"]), T, K, sp.n_shared, H,
                                     int(sp.mode == 3), _ptr(out), None, st), "combine")
