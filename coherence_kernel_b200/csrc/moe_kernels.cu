@@ -375,71 +375,100 @@ int launch_ep_plan(const int32_t *ids, const float *wts, uint32_t ntok, uint32_t
     return (int)cudaGetLastError();
 }
 
-// Combine: one block per token.  order_by_expert = 1 is moe-mix (moe-gate.fk:32-37): the chosen
-// experts in ascending index, acc + g*y.  order_by_expert = 0 is dsv4-moe-acc
-// (dsv4-forward.fk:100-103): the slots in list order, acc + y (the weight was applied inside the
-// expert).  Shared experts are added after, in index order.  fp32 accumulation, bf16 out.
-__global__ void __launch_bounds__(256) k_combine(const uint16_t *__restrict__ y, const int32_t *__restrict__ ids,
-                                                 const float *__restrict__ wts, const int32_t *__restrict__ pair_pos,
-                                                 uint16_t *__restrict__ out, float *__restrict__ out_f32,
-                                                 PermuteParams p, int order_by_expert) {
+// Combine: a token's row is split over gridDim.y blocks of CMB_THREADS threads, one 8-column vector
+// per thread.  order_by_expert = 1 is moe-mix (moe-gate.fk:32-37): the chosen experts in ascending
+// index, acc + g*y.  order_by_expert = 0 is dsv4-moe-acc (dsv4-forward.fk:100-103): the slots in
+// list order, acc + y (the weight was applied inside the expert).  Shared experts are added after,
+// in index order.  fp32 accumulation, bf16 out.  The token's slots (row position and weight, in
+// summation order) are set up once per block in shared memory, and a thread issues all its rows'
+// loads before it adds them in that order: per-slot dependent loads made a decode-sized combine a
+// chain of memory round trips.
+constexpr int CMB_THREADS = 128;
+__global__ void __launch_bounds__(CMB_THREADS) k_combine(const uint16_t *__restrict__ y, const int32_t *__restrict__ ids,
+                                                         const float *__restrict__ wts, const int32_t *__restrict__ pair_pos,
+                                                         uint16_t *__restrict__ out, float *__restrict__ out_f32,
+                                                         PermuteParams p, int order_by_expert) {
     const uint32_t t = blockIdx.x;
     const uint32_t A = p.ntok * p.nsel;
-    int order[16];
     const int ns = (int)min(p.nsel, 16u);
-    for (int k = 0; k < ns; ++k) order[k] = k;
-    if (order_by_expert) {
-        for (int i = 1; i < ns; ++i) {
-            int v = order[i], j = i - 1;
-            while (j >= 0 && ids[t * p.nsel + order[j]] > ids[t * p.nsel + v]) { order[j + 1] = order[j]; --j; }
-            order[j + 1] = v;
+    __shared__ int s_id[16], s_pos[16], s_ord[16];
+    __shared__ float s_g[16];
+    if ((int)threadIdx.x < ns) {
+        const int k = (int)threadIdx.x;
+        s_id[k] = ids[t * p.nsel + k];
+        s_pos[k] = pair_pos[t * p.nsel + k];
+        s_g[k] = order_by_expert ? wts[t * p.nsel + k] : 1.0f;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // the summation order: ascending expert, stable (insertion sort), or the list order
+        for (int k = 0; k < ns; ++k) s_ord[k] = k;
+        if (order_by_expert)
+            for (int i = 1; i < ns; ++i) {
+                const int v = s_ord[i];
+                int j = i - 1;
+                while (j >= 0 && s_id[s_ord[j]] > s_id[v]) {
+                    s_ord[j + 1] = s_ord[j];
+                    --j;
+                }
+                s_ord[j + 1] = v;
+            }
+    }
+    __syncthreads();
+    const uint32_t v = blockIdx.y * CMB_THREADS + threadIdx.x;
+    if (v >= p.hidden / 8) return;
+    uint4 q[16];
+    int pos[16];
+    float g[16];
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+        pos[kk] = -1;
+        if (kk < ns) {
+            pos[kk] = s_pos[s_ord[kk]];
+            g[kk] = s_g[s_ord[kk]];
+            if (pos[kk] >= 0) q[kk] = __ldg(reinterpret_cast<const uint4 *>(y + (size_t)pos[kk] * p.hidden) + v);
         }
     }
-    for (uint32_t v = threadIdx.x; v < p.hidden / 8; v += blockDim.x) {
-        float acc[8];
+    float acc[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-        for (int kk = 0; kk < ns; ++kk) {
-            const int k = order[kk];
-            const int pos = pair_pos[t * p.nsel + k];
-            if (pos < 0) continue;
-            const float g = order_by_expert ? wts[t * p.nsel + k] : 1.0f;
-            const uint4 q = __ldg(reinterpret_cast<const uint4 *>(y + (size_t)pos * p.hidden) + v);
-            const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float lo = __uint_as_float(qq[i] << 16), hi = __uint_as_float(qq[i] & 0xFFFF0000u);
-                if (order_by_expert) {
-                    acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(g, lo));
-                    acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(g, hi));
-                } else {
-                    acc[2 * i] = __fadd_rn(acc[2 * i], lo);
-                    acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], hi);
-                }
+    for (int kk = 0; kk < 16; ++kk) {
+        if (pos[kk] < 0) continue;  // a slot this layer did not compute (another rank's expert)
+        const uint32_t qq[4] = {q[kk].x, q[kk].y, q[kk].z, q[kk].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float lo = __uint_as_float(qq[i] << 16), hi = __uint_as_float(qq[i] & 0xFFFF0000u);
+            if (order_by_expert) {
+                acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(g[kk], lo));
+                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(g[kk], hi));
+            } else {
+                acc[2 * i] = __fadd_rn(acc[2 * i], lo);
+                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], hi);
             }
         }
-        for (uint32_t s = 0; s < p.n_shared; ++s) {
-            const uint4 q = __ldg(reinterpret_cast<const uint4 *>(y + ((size_t)A + (size_t)s * p.ntok + t) * p.hidden) + v);
-            const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+    }
+    for (uint32_t sh = 0; sh < p.n_shared; ++sh) {
+        const uint4 qs = __ldg(reinterpret_cast<const uint4 *>(y + ((size_t)A + (size_t)sh * p.ntok + t) * p.hidden) + v);
+        const uint32_t qq[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(qq[i] << 16));
-                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(qq[i] & 0xFFFF0000u));
-            }
+        for (int i = 0; i < 4; ++i) {
+            acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(qq[i] << 16));
+            acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(qq[i] & 0xFFFF0000u));
         }
-        if (out) {
-            uint4 o;
-            o.x = pack_bf16x2(acc[0], acc[1]);
-            o.y = pack_bf16x2(acc[2], acc[3]);
-            o.z = pack_bf16x2(acc[4], acc[5]);
-            o.w = pack_bf16x2(acc[6], acc[7]);
-            reinterpret_cast<uint4 *>(out + (size_t)t * p.hidden)[v] = o;
-        }
-        if (out_f32) {
-            float4 *o4 = reinterpret_cast<float4 *>(out_f32 + (size_t)t * p.hidden + v * 8);
-            o4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            o4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-        }
+    }
+    if (out) {
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        reinterpret_cast<uint4 *>(out + (size_t)t * p.hidden)[v] = o;
+    }
+    if (out_f32) {
+        float4 *o4 = reinterpret_cast<float4 *>(out_f32 + (size_t)t * p.hidden + v * 8);
+        o4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
 }
 
@@ -447,7 +476,9 @@ int launch_combine(const uint16_t *y, const int32_t *ids, const float *wts, cons
                    float *out_f32, const PermuteParams &p, int order_by_expert, cudaStream_t s) {
     if (p.hidden % 8 != 0 || p.nsel > 16) return CK_ERR_SHAPE;
     if (!y || !ids || !pair_pos || (!out && !out_f32) || (order_by_expert && !wts)) return CK_ERR_ARG;
-    if (p.ntok) k_combine<<<p.ntok, 256, 0, s>>>(y, ids, wts, pair_pos, out, out_f32, p, order_by_expert);
+    if (p.ntok)
+        k_combine<<<dim3(p.ntok, (p.hidden / 8 + CMB_THREADS - 1) / CMB_THREADS), CMB_THREADS, 0, s>>>(
+            y, ids, wts, pair_pos, out, out_f32, p, order_by_expert);
     return (int)cudaGetLastError();
 }
 

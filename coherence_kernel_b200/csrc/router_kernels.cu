@@ -232,10 +232,13 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
     bool allowed[RMAX];
 #pragma unroll
     for (int i = 0; i < RMAX; ++i) allowed[i] = true;
+    // Per-group, per-pick and per-weight values live one per lane (group g or pick r in lane g or
+    // r), not in arrays indexed at run time, which would sit in local memory on the selection's
+    // chain of dependent steps.
     if (p.mode == 4 && p.ngroups > 1) {
         // group score = sum of the group's two best scores (ties: lower index first, like dsv4-topk)
         const int gs = (int)(p.ne / p.ngroups);
-        T gsc[32];
+        T my_gsc = NEG;  // lane g: group g's score
         for (int g = 0; g < (int)p.ngroups; ++g) {
             T b1 = NEG, b2 = NEG;
             int i1 = 1 << 30;
@@ -255,22 +258,22 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
             }
             int dummy = 0;
             warp_argmax_t(b2, dummy);
-            gsc[g] = b2 + best;  // tn-sum over (second, best): (0 + second) + best
+            if (lane == g) my_gsc = b2 + best;  // tn-sum over (second, best): (0 + second) + best
         }
-        // top groups by repeated argmax; the margin is min(chosen) - max(rejected)
+        // top groups by repeated argmax (ties: the lower group); the margin is min(chosen) -
+        // max(rejected)
         unsigned gmask = 0;
         T gmin = (T)3.0e38f;
         for (int r = 0; r < (int)p.topk_groups; ++r) {
-            T bv = NEG;
-            int bi = 0;
-            for (int g = 0; g < (int)p.ngroups; ++g)
-                if (!(gmask >> g & 1) && gsc[g] > bv) { bv = gsc[g]; bi = g; }
+            T bv = lane < (int)p.ngroups && !(gmask >> lane & 1) ? my_gsc : NEG;
+            int bi = lane;
+            warp_argmax_t(bv, bi);
             gmask |= 1u << bi;
             gmin = sel_min(gmin, bv);
         }
-        T gmax = NEG;
-        for (int g = 0; g < (int)p.ngroups; ++g)
-            if (!(gmask >> g & 1)) gmax = sel_max(gmax, gsc[g]);
+        T gmax = lane < (int)p.ngroups && !(gmask >> lane & 1) ? my_gsc : NEG;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) gmax = sel_max(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
         if ((int)p.topk_groups < (int)p.ngroups) margin = sel_min(margin, gmin - gmax);
 #pragma unroll
         for (int i = 0; i < RMAX; ++i) {
@@ -278,10 +281,10 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
             allowed[i] = e < (int)p.ne && (gmask >> (e / gs) & 1);
         }
     }
-    // expert selection, best first
-    int sel[16];
-    T selv[16];
+    // expert selection, best first: lane r keeps the r-th pick
     const int k = (int)p.nsel;
+    int my_sel = 0;
+    T my_selv = NEG, last = NEG;
     for (int r = 0; r < k; ++r) {
         T bv = NEG;
         int bi = 1 << 30;
@@ -289,8 +292,11 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
         for (int i = 0; i < RMAX; ++i)
             if (allowed[i] && sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
         warp_argmax_t(bv, bi);
-        sel[r] = bi;
-        selv[r] = bv;
+        if (lane == r) {
+            my_sel = bi;
+            my_selv = bv;
+        }
+        last = bv;
 #pragma unroll
         for (int i = 0; i < RMAX; ++i)
             if (32 * i + lane == bi) allowed[i] = false;
@@ -302,35 +308,38 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
         for (int i = 0; i < RMAX; ++i)
             if (allowed[i] && sc[i] > bv) { bv = sc[i]; bi = 32 * i + lane; }
         warp_argmax_t(bv, bi);
-        if (bv > NEG) margin = sel_min(margin, selv[k - 1] - bv);
+        if (bv > NEG) margin = sel_min(margin, last - bv);
         // the list order of the chosen experts is part of the answer: two chosen experts closer
         // than the margin could be listed in the other order by an exact fold
-        for (int r = 1; r < k; ++r) margin = sel_min(margin, selv[r - 1] - selv[r]);
+        const T prev = __shfl_up_sync(0xffffffffu, my_selv, 1);
+        T dm = lane >= 1 && lane < k ? prev - my_selv : (T)3.0e38f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dm = sel_min(dm, __shfl_xor_sync(0xffffffffu, dm, o));
+        margin = sel_min(margin, dm);
     }
     // weights
-    T w[16];
     if (p.mode == 4) {
         // dsv4-topk lists the picks last-first; weights from the unbiased probs, sum floored at
-        // 2^-14, times wscale / sum (dsv4-forward.fk:105-111)
-        T s0 = (T)0;
+        // 2^-14, times wscale / sum (dsv4-forward.fk:105-111); lane r holds list position r
+        T s0 = (T)0, my_w = (T)0;
         for (int r = 0; r < k; ++r) {
-            const int e = sel[k - 1 - r];
+            const int e = __shfl_sync(0xffffffffu, my_sel, k - 1 - r);
             T pe = (T)0;
 #pragma unroll
             for (int i = 0; i < RMAX; ++i)
                 if (32 * i + lane == e) pe = pr[i];
             pe = __shfl_sync(0xffffffffu, pe, e & 31);
-            w[r] = pe;
+            if (lane == r) my_w = pe;
             s0 += pe;
         }
         const T s = s0 < (T)6.103515625e-05f ? (T)6.103515625e-05f : s0;
         const T scl = (T)p.wscale / s;
-        for (int r = 0; r < k; ++r) w[r] *= scl;
-        if (lane == 0)
-            for (int r = 0; r < k; ++r) {
-                ids[(size_t)t * k + r] = sel[k - 1 - r];
-                wts[(size_t)t * k + r] = (float)w[r];
-            }
+        my_w *= scl;
+        const int my_id = __shfl_sync(0xffffffffu, my_sel, (k - 1 - lane) & 31);
+        if (lane < k) {
+            ids[(size_t)t * k + lane] = my_id;
+            wts[(size_t)t * k + lane] = (float)my_w;
+        }
     } else {
         // softmax over all experts (max-subtracted), the chosen probabilities, best first
         T mx = NEG;
@@ -343,11 +352,10 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
         for (int i = 0; i < RMAX; ++i)
             if (32 * i + lane < (int)p.ne) s += sel_exp(sc[i] - mx);
         s = warp_sum_t(s);
-        if (lane == 0)
-            for (int r = 0; r < k; ++r) {
-                ids[(size_t)t * k + r] = sel[r];
-                wts[(size_t)t * k + r] = (float)(sel_exp(selv[r] - mx) / s);
-            }
+        if (lane < k) {
+            ids[(size_t)t * k + lane] = my_sel;
+            wts[(size_t)t * k + lane] = (float)(sel_exp(my_selv - mx) / s);
+        }
     }
     // the threshold: tau, or 16 roundings of the largest logit (float form) / 16 x 2^-40 of the
     // largest sum|w x| (double form) when that is larger
