@@ -207,25 +207,76 @@ template <typename T>
 __global__ void k_route_select(const T *__restrict__ L, const float *__restrict__ sabs,
                                const float *__restrict__ bias, int32_t *__restrict__ ids, float *__restrict__ wts,
                                uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p) {
+    constexpr bool CTA = sizeof(T) == 8;  // the fp64 form: a CTA of 256 threads per token
     const int lane = threadIdx.x & 31;
-    const uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t t = CTA ? blockIdx.x : (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (t >= p.ntok) return;
     const T NEG = (T)-3.0e38f;
     T sc[RMAX], pr[RMAX];
     const int nreg = (int)((p.ne + 31) / 32);
     float lmax = 0.0f;  // max |logit| (float form) or max sum|w x| (double form) of the token
-#pragma unroll
-    for (int i = 0; i < RMAX; ++i) {
-        const int e = 32 * i + lane;
-        const bool v = i < nreg && e < (int)p.ne;
+    T pre_gsc = NEG;       // lane g: group g's score, when the CTA form computed it (one warp per group)
+    bool have_gsc = false;
+    if constexpr (CTA) {
+        // one expert per thread: the 256 fp64 sigmoids (an exp and a division each, long dependent
+        // chains on this GPU's fp64 pipe) in parallel instead of eight in a row per lane; warp 0
+        // then selects from shared memory
+        __shared__ T s_sc[256], s_pr[256];
+        __shared__ float s_lmax[8];
+        const int e = threadIdx.x;
+        const bool v = e < (int)p.ne;
         const T l = v ? L[(size_t)t * p.ne + e] : NEG;
-        if (v) lmax = fmaxf(lmax, sabs ? sabs[(size_t)t * p.ne + e] : fabsf((float)l));
-        if (p.mode == 4) {
-            pr[i] = v ? (T)1 / ((T)1 + sel_exp(-l)) : (T)0;
-            sc[i] = v ? pr[i] + (T)bias[e] : NEG;
-        } else {
-            pr[i] = l;
-            sc[i] = l;
+        float lm = v ? sabs[(size_t)t * p.ne + e] : 0.0f;
+        T prv = (T)0, scv = NEG;
+        if (v) {
+            prv = p.mode == 4 ? (T)1 / ((T)1 + sel_exp(-l)) : l;
+            scv = p.mode == 4 ? prv + (T)bias[e] : l;
+        }
+        s_sc[e] = scv;
+        s_pr[e] = prv;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, o));
+        if (lane == 0) s_lmax[threadIdx.x >> 5] = lm;
+        __syncthreads();
+        // groups of 32 experts (at most 8): warp g takes group g's two best scores, with the ties
+        // and the sum of the warp form below
+        __shared__ T s_gsc[8];
+        have_gsc = p.mode == 4 && p.ngroups > 1 && p.ngroups <= 8 && p.ne == 32 * p.ngroups;
+        if (have_gsc) {
+            const int g = threadIdx.x >> 5;
+            if (g < (int)p.ngroups) {
+                T v = s_sc[threadIdx.x];
+                int vi = (int)threadIdx.x;
+                warp_argmax_t(v, vi);
+                T b2 = (int)threadIdx.x != vi ? s_sc[threadIdx.x] : NEG;
+                int dummy = 0;
+                warp_argmax_t(b2, dummy);
+                if (lane == 0) s_gsc[g] = b2 + v;  // tn-sum over (second, best): (0 + second) + best
+            }
+            __syncthreads();
+            if (threadIdx.x < 32 && lane < (int)p.ngroups) pre_gsc = s_gsc[lane];
+        }
+        if (threadIdx.x >= 32) return;
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i) {
+            sc[i] = s_sc[32 * i + lane];
+            pr[i] = s_pr[32 * i + lane];
+            lmax = fmaxf(lmax, s_lmax[i]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < RMAX; ++i) {
+            const int e = 32 * i + lane;
+            const bool v = i < nreg && e < (int)p.ne;
+            const T l = v ? L[(size_t)t * p.ne + e] : NEG;
+            if (v) lmax = fmaxf(lmax, sabs ? sabs[(size_t)t * p.ne + e] : fabsf((float)l));
+            if (p.mode == 4) {
+                pr[i] = v ? (T)1 / ((T)1 + sel_exp(-l)) : (T)0;
+                sc[i] = v ? pr[i] + (T)bias[e] : NEG;
+            } else {
+                pr[i] = l;
+                sc[i] = l;
+            }
         }
     }
     T margin = (T)3.0e38f;
@@ -238,8 +289,8 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
     if (p.mode == 4 && p.ngroups > 1) {
         // group score = sum of the group's two best scores (ties: lower index first, like dsv4-topk)
         const int gs = (int)(p.ne / p.ngroups);
-        T my_gsc = NEG;  // lane g: group g's score
-        for (int g = 0; g < (int)p.ngroups; ++g) {
+        T my_gsc = pre_gsc;  // lane g: group g's score
+        for (int g = 0; g < (have_gsc ? 0 : (int)p.ngroups); ++g) {
             T b1 = NEG, b2 = NEG;
             int i1 = 1 << 30;
 #pragma unroll
@@ -533,8 +584,7 @@ int launch_route_select_d(const double *L, const float *sabs, const float *bias,
     if (!sabs) return CK_ERR_ARG;
     cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
     if (p.ntok)
-        k_route_select<double><<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, sabs, bias, ids, wts, flag_list,
-                                                                           flag_count, p);
+        k_route_select<double><<<p.ntok, 256, 0, s>>>(L, sabs, bias, ids, wts, flag_list, flag_count, p);
     return (int)cudaGetLastError();
 }
 int launch_route_softmax_tokens(const float *L, uint32_t *ids, float *wts, uint32_t ne, uint32_t nsel, uint32_t ntok,
