@@ -275,7 +275,7 @@ int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const flo
     // practice only exact ties take the fp64 re-route.  Otherwise the logits run on the tensor cores,
     // x . [W1 | W2 | W3]^T with the fp32 router split into bf16 terms, and are selected in fp32
     // with the margin tau.
-    rc = ntok <= 64 ? ck::launch_router_logits_few((const uint16_t *)x, rw, logits, w.exact, w.sabs, ntok,
+    rc = ntok <= 64 ? ck::launch_router_logits_few((const uint16_t *)x, rw, logits, w.exact, w.sabs, w.flags, ntok,
                                                    c->n_experts, c->hidden, S(s))
                     : CK_ERR_SHAPE;
     if (rc == 0) {

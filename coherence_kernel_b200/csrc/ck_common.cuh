@@ -113,6 +113,29 @@ CK_DEV void prefetch_tmap(const CUtensorMap *map) {
 }
 CK_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ----------------------------------------------------------------------------- dependent launch
+// Kernels launched with programmatic stream serialization (launch_pdl) may start while the kernel
+// before them finishes: each calls grid_dep_trigger (let the next one be scheduled) and then
+// grid_dep_wait (the previous kernel has completed and its writes are visible) before its first
+// global-memory access.  Both are no-ops for a kernel launched without the attribute.
+CK_DEV void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+CK_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ----------------------------------------------------------------------------- tcgen05
 CK_DEV void tmem_alloc(uint32_t *smem_slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),

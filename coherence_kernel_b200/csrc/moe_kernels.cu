@@ -46,6 +46,8 @@ static PermWs carve(void *ws, const PermuteParams &p) {
 // a pair among its expert's pairs in this chunk follows the (token, slot) order exactly.
 __global__ void k_perm_hist(const int32_t *__restrict__ ids, uint32_t npairs, uint32_t E, int32_t *__restrict__ chunk_hist,
                             int32_t *__restrict__ local_rank) {
+    grid_dep_trigger();
+    grid_dep_wait();
     __shared__ int32_t cnt[MAX_EXPERTS];
     const int lane = threadIdx.x;
     for (uint32_t e = lane; e < E; e += 32) cnt[e] = 0;
@@ -112,6 +114,8 @@ __device__ __forceinline__ int seg_tiles(int c, int bn, int &base) {
 __global__ void __launch_bounds__(1024) k_perm_scan(int32_t *__restrict__ chunk_hist, uint32_t nchunks, PermuteParams p,
                                                     int32_t *__restrict__ expert_off, int32_t *__restrict__ counts,
                                                     int4 *__restrict__ tiles, int32_t *__restrict__ ntiles) {
+    grid_dep_trigger();
+    grid_dep_wait();
     const int e = threadIdx.x;
     int c = 0;
     if (e < (int)p.n_experts) {
@@ -154,6 +158,8 @@ __global__ void k_perm_scatter(const int32_t *__restrict__ ids, const float *__r
                                int32_t *__restrict__ pair_pos, const int32_t *__restrict__ chunk_off,
                                const int32_t *__restrict__ local_rank, const int32_t *__restrict__ expert_off,
                                PermuteParams p) {
+    grid_dep_trigger();
+    grid_dep_wait();
     const uint32_t A = p.ntok * p.nsel;
     const uint32_t wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -192,12 +198,15 @@ int launch_permute(const int32_t *ids, const float *wts, const uint16_t *x, uint
     if (!ids || !x || !xp || !row_w || !pair_pos || !counts || !tiles || !ntiles || !workspace) return CK_ERR_ARG;
     PermWs w = carve(workspace, p);
     const uint32_t npairs = n_pairs(p), nch = n_chunks(p);
-    if (nch) k_perm_hist<<<nch, 32, 0, s>>>(ids, npairs, p.n_experts, w.chunk_hist, w.local_rank);
-    k_perm_scan<<<1, 1024, 0, s>>>(w.chunk_hist, nch, p, w.expert_off, counts, tiles, ntiles);
+    cudaError_t e = cudaSuccess;
+    if (nch) e = launch_pdl(k_perm_hist, dim3(nch), dim3(32), 0, s, ids, npairs, p.n_experts, w.chunk_hist, w.local_rank);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_perm_scan, dim3(1), dim3(1024), 0, s, w.chunk_hist, nch, p, w.expert_off, counts, tiles, ntiles);
     const uint64_t warps = (uint64_t)npairs + (p.n_shared ? p.ntok : 0u);
-    if (warps) k_perm_scatter<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(
-        ids, wts, x, xp, row_w, pair_pos, w.chunk_hist, w.local_rank, w.expert_off, p);
-    return (int)cudaGetLastError();
+    if (e == cudaSuccess && warps)
+        e = launch_pdl(k_perm_scatter, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, s, ids, wts, x, xp,
+                       row_w, pair_pos, w.chunk_hist, w.local_rank, w.expert_off, p);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 // The token tiles of a single matrix over ntok rows (a prefill GEMM): group 0, rows in order.
@@ -388,6 +397,8 @@ __global__ void __launch_bounds__(CMB_THREADS) k_combine(const uint16_t *__restr
                                                          const float *__restrict__ wts, const int32_t *__restrict__ pair_pos,
                                                          uint16_t *__restrict__ out, float *__restrict__ out_f32,
                                                          PermuteParams p, int order_by_expert) {
+    grid_dep_trigger();
+    grid_dep_wait();
     const uint32_t t = blockIdx.x;
     const uint32_t A = p.ntok * p.nsel;
     const int ns = (int)min(p.nsel, 16u);
@@ -476,9 +487,11 @@ int launch_combine(const uint16_t *y, const int32_t *ids, const float *wts, cons
                    float *out_f32, const PermuteParams &p, int order_by_expert, cudaStream_t s) {
     if (p.hidden % 8 != 0 || p.nsel > 16) return CK_ERR_SHAPE;
     if (!y || !ids || !pair_pos || (!out && !out_f32) || (order_by_expert && !wts)) return CK_ERR_ARG;
-    if (p.ntok)
-        k_combine<<<dim3(p.ntok, (p.hidden / 8 + CMB_THREADS - 1) / CMB_THREADS), CMB_THREADS, 0, s>>>(
-            y, ids, wts, pair_pos, out, out_f32, p, order_by_expert);
+    if (p.ntok) {
+        const cudaError_t e = launch_pdl(k_combine, dim3(p.ntok, (p.hidden / 8 + CMB_THREADS - 1) / CMB_THREADS),
+                                         dim3(CMB_THREADS), 0, s, y, ids, wts, pair_pos, out, out_f32, p, order_by_expert);
+        if (e != cudaSuccess) return (int)e;
+    }
     return (int)cudaGetLastError();
 }
 

@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(XF_WARPS * 32) k_exact_logits_few(const uint16
                                                                     const uint32_t *__restrict__ flag_count,
                                                                     double *__restrict__ out, uint32_t ne,
                                                                     uint32_t hidden) {
+    grid_dep_trigger();
+    grid_dep_wait();
     extern __shared__ __align__(16) uint8_t xf_smem[];
     const uint32_t nflag = *flag_count;
     if (nflag > XL_FEW) return;  // the tiled kernel takes them
@@ -134,6 +136,8 @@ __global__ void __launch_bounds__(256) k_exact_logits(const uint16_t *__restrict
                                                       const uint32_t *__restrict__ flag_list,
                                                       const uint32_t *__restrict__ flag_count, double *__restrict__ out,
                                                       uint32_t ne, uint32_t hidden) {
+    grid_dep_trigger();
+    grid_dep_wait();
     __shared__ double wt[2][XL_EXP][XL_J + 1];
     __shared__ __align__(16) double xt[2][XL_TOK][XL_J];
     const uint32_t nflag = *flag_count;
@@ -341,6 +345,8 @@ __global__ void __launch_bounds__(256) k_exact_select(const double *__restrict__
                                                       int32_t *__restrict__ ids, float *__restrict__ wts,
                                                       const uint32_t *__restrict__ flag_list,
                                                       const uint32_t *__restrict__ flag_count, RouteParams p) {
+    grid_dep_trigger();
+    grid_dep_wait();
     __shared__ double sbuf[256], sprob[256];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const uint32_t nflag = *flag_count;
@@ -381,11 +387,15 @@ int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int
         few_attr = true;
     }
     // both forms are launched; each returns at once unless the flagged count is its own
-    k_exact_logits_few<<<2 * nsm, XF_WARPS * 32, XF_WARPS * sizeof(XfRing), s>>>(x, w, flag_list, flag_count,
-                                                                                scratch, p.ne, p.hidden);
-    k_exact_logits<<<nsm * 2, 256, 0, s>>>(x, w, flag_list, flag_count, scratch, p.ne, p.hidden);
-    k_exact_select<<<nsm * 2, 256, 0, s>>>(scratch, bias, ids, wts, flag_list, flag_count, p);
-    return (int)cudaGetLastError();
+    cudaError_t e = launch_pdl(k_exact_logits_few, dim3(2 * nsm), dim3(XF_WARPS * 32), XF_WARPS * sizeof(XfRing), s, x,
+                               w, flag_list, flag_count, scratch, p.ne, p.hidden);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_exact_logits, dim3(nsm * 2), dim3(256), 0, s, x, w, flag_list, flag_count, scratch, p.ne,
+                       p.hidden);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_exact_select, dim3(nsm * 2), dim3(256), 0, s, scratch, bias, ids, wts, flag_list, flag_count,
+                       p);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 }  // namespace ck

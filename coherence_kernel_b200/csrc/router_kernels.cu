@@ -97,7 +97,13 @@ CK_DEV void dot_pair(float &s, float &c, float w, float x) {
 __global__ void __launch_bounds__(256, 2) k_router_logits_few(const uint16_t *__restrict__ x,
                                                               const float *__restrict__ w, float *__restrict__ L,
                                                               double *__restrict__ Ld, float *__restrict__ sabs,
-                                                              uint32_t T, uint32_t E, uint32_t H) {
+                                                              uint32_t *__restrict__ flag_count, uint32_t T, uint32_t E,
+                                                              uint32_t H) {
+    grid_dep_trigger();
+    grid_dep_wait();
+    // the selection's flagged-token counter starts at zero (cleared here: a memset would end the
+    // chain of dependent launches)
+    if (flag_count && blockIdx.x == 0 && threadIdx.x == 0) *flag_count = 0;
     __shared__ double part[8][RS_TMAX];
     __shared__ float apart[8][RS_TMAX];
     const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
@@ -163,14 +169,14 @@ __global__ void __launch_bounds__(256, 2) k_router_logits_few(const uint16_t *__
         sabs[(size_t)t * E + e] = av;
     }
 }
-int launch_router_logits_few(const uint16_t *x, const float *w, float *L, double *Ld, float *sabs, uint32_t T,
-                             uint32_t E, uint32_t H, cudaStream_t s) {
+int launch_router_logits_few(const uint16_t *x, const float *w, float *L, double *Ld, float *sabs,
+                             uint32_t *flag_count, uint32_t T, uint32_t E, uint32_t H, cudaStream_t s) {
     if (T > RS_TMAX || H % 32 || H > 32 * 32 * RS_IT || (reinterpret_cast<uintptr_t>(x) & 7) ||
         (reinterpret_cast<uintptr_t>(w) & 15))
         return CK_ERR_SHAPE;
     if (!T || !E) return 0;
-    k_router_logits_few<<<E, 256, 0, s>>>(x, w, L, Ld, sabs, T, E, H);
-    return (int)cudaGetLastError();
+    const cudaError_t e = launch_pdl(k_router_logits_few, dim3(E), dim3(256), 0, s, x, w, L, Ld, sabs, flag_count, T, E, H);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ 2. fast selection
@@ -207,6 +213,8 @@ template <typename T>
 __global__ void k_route_select(const T *__restrict__ L, const float *__restrict__ sabs,
                                const float *__restrict__ bias, int32_t *__restrict__ ids, float *__restrict__ wts,
                                uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p) {
+    grid_dep_trigger();
+    grid_dep_wait();
     constexpr bool CTA = sizeof(T) == 8;  // the fp64 form: a CTA of 256 threads per token
     const int lane = threadIdx.x & 31;
     const uint32_t t = CTA ? blockIdx.x : (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -582,9 +590,12 @@ int launch_route_select_d(const double *L, const float *sabs, const float *bias,
         return CK_ERR_SHAPE;
     if (p.mode == 4 && !bias) return CK_ERR_ARG;
     if (!sabs) return CK_ERR_ARG;
-    cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
-    if (p.ntok)
-        k_route_select<double><<<p.ntok, 256, 0, s>>>(L, sabs, bias, ids, wts, flag_list, flag_count, p);
+    // flag_count was cleared by launch_router_logits_few, the kernel before this one
+    if (p.ntok) {
+        const cudaError_t e = launch_pdl(k_route_select<double>, dim3(p.ntok), dim3(256), 0, s, L, sabs, bias, ids, wts,
+                                         flag_list, flag_count, p);
+        if (e != cudaSuccess) return (int)e;
+    }
     return (int)cudaGetLastError();
 }
 int launch_route_softmax_tokens(const float *L, uint32_t *ids, float *wts, uint32_t ne, uint32_t nsel, uint32_t ntok,
