@@ -19,9 +19,9 @@
 // Roles (640 threads): warp 0 TMA-loads superblock columns of 128 weight rows (3D maps over the
 // stacked expert matrices); warp 1 owns tensor memory and issues the MMAs from an elected lane;
 // warps 2-3 write the B tiles of alternate steps; warps 4-11, two sets of four on alternate steps,
-// build A and pass the rows' headers on; warps 12-19 apply the scales, K steps 0-3 (low-nibble
-// sub-blocks) and 4-7 (high-nibble ones), and meet once per item to finish it.  Every wait is
-// bounded (about one second) and a wait that gives up records its code in the error word.
+// build A and pass the rows' headers on; warps 12-19, again two sets on alternate steps, apply the
+// scales and meet once per item to finish it.  Every wait is bounded (about one second) and a wait
+// that gives up records its code in the error word.
 #include "ck_common.cuh"
 #include "ck_launch.h"
 #include "tc_i8.cuh"
@@ -94,12 +94,14 @@ CK_DEV Step step_at(const Params &p, int j, int S) {
     step_fields(st, p);
     return st;
 }
-// by <= S; the caller stops before the sequence ends (the tile entry past the end is not read)
+// Moves `by` steps on (an item may have fewer steps than that); the caller passes more = false when
+// the new position is past its sequence, so the tile entry there is not read.
 CK_DEV void step_advance(Step &st, const Params &p, int by, int S, bool more) {
     st.js += by;
     if (st.js >= S) {
-        st.js -= S;
-        ++st.kit;
+        const int w = st.js / S;
+        st.js -= w * S;
+        st.kit += w;
         if (more) step_item(st, p);
     }
     step_fields(st, p);
@@ -110,14 +112,18 @@ CK_DEV bool warp_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, err, code));
 }
 
-// The epilogue of half G (warps 12-15 for G = 0, 16-19 for G = 1): per step, the four K steps'
-// accumulators of every row and token to sums of q x, weighted by the rows' scales; at an item's
-// end half 1 hands its sums to half 0, which applies silu * up * route weight (dual) and stores.
+// The epilogue of set H (warps 12-15 for H = 0, 16-19 for H = 1), which takes the steps j with
+// j % 2 == H: per step, the eight K steps' accumulators of every row and token to sums of q x,
+// weighted by the rows' scales.  An item's last step belongs to one set (the finisher); the other
+// set hands its partial sums over after its own last step of the item (at step S - 2), and the
+// finisher applies silu * up * route weight (dual) and stores.  In the dual form each set moves its
+// gate sums aside at its first up step of the item.
 template <int NN>
 CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mma_done, uint64_t *d_empty,
-                     uint64_t *red_full, uint64_t *red_empty, int *err, uint32_t tmem, int G, int sub, int lane) {
+                     uint64_t *red_full, uint64_t *red_empty, int *err, uint32_t tmem, int H, int sub, int lane) {
     constexpr int DS = 8 * NN;
     constexpr int ND = (int)(TMEM_COLS - D_OFF) / DS;
+    constexpr int KB = NN == 8 ? 8 : 32 / NN;  // K steps per accumulator load (64 or 32 registers)
     const int r = 32 * sub + lane;
     const uint32_t trow = tmem + ((uint32_t)(32 * sub) << 16);
     float *xs = reinterpret_cast<float *>(smem + XS_OFF);
@@ -126,20 +132,31 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
 #pragma unroll
     for (int t = 0; t < MAXT; ++t) acc[t] = accg[t] = 0.0f;
     Step st = {};
-    if (nj > 0) st = step_at(p, 0, S);
-    for (int j = 0; j < nj; step_advance(st, p, 1, S, ++j < nj)) {
+    if (H < nj) st = step_at(p, H, S);
+    int cur_kit = -1;
+    bool up = false;  // this set has reached the item's up rows
+    for (int j = H; j < nj; j += 2, step_advance(st, p, 2, S, j < nj)) {
         if (!warp_wait(&mma_done[j % NSLOT], (j / NSLOT) & 1, err, 9)) break;
         tc_fence_after();
+        if (st.kit != cur_kit) {
+            cur_kit = st.kit;
+            up = false;
+        }
+        if (p.dual && !up && st.js >= (int)p.nsb) {  // the gate rows are done; the up rows follow
+            up = true;
+#pragma unroll
+            for (int t = 0; t < MAXT; ++t) {
+                accg[t] = acc[t];
+                acc[t] = 0.0f;
+            }
+        }
         const int n = min(st.tl.w, MAXT);
         const uint4 hdr = reinterpret_cast<const uint4 *>(smem + H_OFF + (j % NSLOT) * H_STAGE)[r];
         const float *slot = xs + (j % NSLOT) * (XS_SLOT / 4);
         const float d = f16_bits_to_float(hdr.x & 0xFFFF), dmin = f16_bits_to_float(hdr.x >> 16);
-        // this half's four K steps are 4 NN consecutive columns: loaded in one or four batches,
-        // each before a single wait
-        const uint32_t dbase = trow + D_OFF + (uint32_t)((j % ND) * DS) + (uint32_t)(4 * G * NN);
-        constexpr int KB = NN == 32 ? 1 : 4;  // K steps per batch (at most 64 registers)
+        const uint32_t dbase = trow + D_OFF + (uint32_t)((j % ND) * DS);
 #pragma unroll
-        for (int kb = 0; kb < 4; kb += KB) {
+        for (int kb = 0; kb < 8; kb += KB) {
             uint32_t dv[KB][NN];
 #pragma unroll
             for (int i = 0; i < KB; ++i) {
@@ -150,7 +167,7 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < KB; ++i) {
-                const int s = 2 * (kb + i) + G;
+                const int k = kb + i, s = k < 4 ? 2 * k : 2 * (k - 4) + 1;  // K step k is sub-block s
                 int scv, mv;
                 q4k_scale_min(hdr.y, hdr.z, hdr.w, s, scv, mv);
                 const float dsc = d * (float)scv, ndm = -(dmin * (float)mv);
@@ -166,19 +183,20 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&d_empty[j % NSLOT]);
-        if (p.dual && st.js == (int)p.nsb - 1) {  // the gate rows are done; the up rows follow
+        const bool last = st.js == S - 1, donor = S >= 2 && st.js == S - 2;
+        if (last || donor) {
+            if (p.dual && !up) {  // this set saw only gate rows of the item (one superblock per row)
 #pragma unroll
-            for (int t = 0; t < MAXT; ++t) {
-                accg[t] = acc[t];
-                acc[t] = 0.0f;
+                for (int t = 0; t < MAXT; ++t) {
+                    accg[t] = acc[t];
+                    acc[t] = 0.0f;
+                }
             }
-        }
-        if (st.js == S - 1) {
-            // the item's last step: half 1 hands its sums to half 0, which writes the outputs
-            const int buf = st.kit & 1;
+            // buffer kit % 2, used for the (kit / 2)-th time: written by the donor, read by the finisher
+            const int buf = st.kit & 1, use = st.kit >> 1;
             float *rg = red + (size_t)buf * 2 * MAXT * ROWS, *ru = rg + MAXT * ROWS;
-            if (G == 1) {
-                if (st.kit >= 2 && !warp_wait(&red_empty[buf], ((st.kit >> 1) & 1) ^ 1, err, 10)) break;
+            if (donor) {
+                if (use >= 1 && !warp_wait(&red_empty[buf], (use - 1) & 1, err, 10)) break;
 #pragma unroll
                 for (int t = 0; t < MAXT; ++t)
                     if (t < n) {
@@ -188,14 +206,15 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&red_full[buf]);
             } else {
-                if (!warp_wait(&red_full[buf], (st.kit >> 1) & 1, err, 11)) break;
+                const bool other = S >= 2;  // the other set holds partial sums of this item
+                if (other && !warp_wait(&red_full[buf], use & 1, err, 11)) break;
                 const int col = st.rt * ROWS + r;
 #pragma unroll
                 for (int t = 0; t < MAXT; ++t) {
                     if (t >= n) break;
-                    float v = acc[t] + ru[t * ROWS + r];
+                    float v = acc[t] + (other ? ru[t * ROWS + r] : 0.0f);
                     if (p.dual) {
-                        const float gv = accg[t] + rg[t * ROWS + r];
+                        const float gv = accg[t] + (other ? rg[t * ROWS + r] : 0.0f);
                         const float rw = p.row_w ? p.row_w[st.tl.z + t] : 1.0f;
                         // silu(g) = g / (1 + e^-g), as the grouped GEMM computes it
                         v = __fdividef(gv, 1.0f + __expf(-gv)) * v * rw;
@@ -203,7 +222,7 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
                     p.out[(size_t)(st.tl.z + t) * p.N + col] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&red_empty[buf]);
+                if (other && lane == 0) mbar_arrive(&red_empty[buf]);
             }
 #pragma unroll
             for (int t = 0; t < MAXT; ++t) acc[t] = accg[t] = 0.0f;
@@ -243,7 +262,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         for (int i = 0; i < NA; ++i) mbar_init(&ops_full[i], 5);
         for (int i = 0; i < NSLOT; ++i) {
             mbar_init(&mma_done[i], 1);
-            mbar_init(&d_empty[i], 8);
+            mbar_init(&d_empty[i], 4);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&red_full[i], 4);
@@ -427,9 +446,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        // half g: K steps 4g .. 4g+3, i.e. sub-blocks 2 kk + g for kk = 0..3.  One copy of the code
-        // for both halves: a second copy measured slower (the roles already share each scheduler's
-        // instruction cache)
+        // two sets of four warps on alternate steps (one copy of the code for both: a second copy
+        // measured slower, the roles already share each scheduler's instruction cache)
         epilogue<NN>(p, S, nj, smem, mma_done, d_empty, red_full, red_empty, err, tmem, (warp - 12) >> 2, warp & 3,
                      lane);
     }
@@ -478,9 +496,11 @@ int launch_gemv_moe(const GemmParams &p, cudaStream_t s) {
     EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return CK_ERR_NODEV;
     const uint32_t nsb = p.K / 256, row_bytes = nsb * Q4K_BYTES;
+    // a single matrix (one group, w_stride 0) still needs a valid stride for the map's third axis
+    const uint64_t wstr = p.w_stride ? p.w_stride : (uint64_t)row_bytes * p.N;
     auto encode = [&](CUtensorMap &m, const uint8_t *base, uint32_t count) {
         cuuint64_t dims[3] = {row_bytes, p.N, count};
-        cuuint64_t strides[2] = {row_bytes, p.w_stride};
+        cuuint64_t strides[2] = {row_bytes, wstr};
         cuuint32_t box[3] = {Q4K_BYTES, (cuuint32_t)gmv::ROWS, 1};
         cuuint32_t estr[3] = {1, 1, 1};
         return enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(base), dims, strides, box, estr,

@@ -31,8 +31,11 @@ def run(rows, cols, ntok, seed, sample_rows=None):
 
 
 @pytest.mark.parametrize("rows,cols,ntok", [(128, 64, 16), (256, 512, 1), (256, 512, 17), (384, 1408, 300),
-                                            (128, 256, 256), (512, 2048, 520)])
+                                            (128, 256, 256), (512, 2048, 520), (256, 768, 4), (384, 1024, 8),
+                                            (640, 2048, 3), (200, 512, 3), (256, 256, 2)])
 def test_gemm_small(rows, cols, ntok):
+    # up to 4 tokens, rows a multiple of 128 and cols of 256 take the few-token tensor-core matvec;
+    # the rest (and 200 rows) the dequantizing GEMM
     run(rows, cols, ntok, seed=rows * 31 + ntok)
 
 
