@@ -123,14 +123,17 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
                      uint64_t *red_full, uint64_t *red_empty, int *err, uint32_t tmem, int H, int sub, int lane) {
     constexpr int DS = 8 * NN;
     constexpr int ND = (int)(TMEM_COLS - D_OFF) / DS;
-    constexpr int KB = NN == 8 ? 8 : 32 / NN;  // K steps per accumulator load (64 or 32 registers)
+    constexpr int KB = 32 / NN;  // K steps per accumulator load (32 registers)
+    // the tokens this variant's N holds (3 digit rows each): the token loops are unrolled only that
+    // far, which keeps the code small (the roles share each scheduler's instruction cache)
+    constexpr int MT = NN / 3 < MAXT ? NN / 3 : MAXT;
     const int r = 32 * sub + lane;
     const uint32_t trow = tmem + ((uint32_t)(32 * sub) << 16);
     float *xs = reinterpret_cast<float *>(smem + XS_OFF);
     float *red = reinterpret_cast<float *>(smem + RED_OFF);
-    float acc[MAXT], accg[MAXT];
+    float acc[MT], accg[MT];
 #pragma unroll
-    for (int t = 0; t < MAXT; ++t) acc[t] = accg[t] = 0.0f;
+    for (int t = 0; t < MT; ++t) acc[t] = accg[t] = 0.0f;
     Step st = {};
     if (H < nj) st = step_at(p, H, S);
     int cur_kit = -1;
@@ -145,38 +148,45 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
         if (p.dual && !up && st.js >= (int)p.nsb) {  // the gate rows are done; the up rows follow
             up = true;
 #pragma unroll
-            for (int t = 0; t < MAXT; ++t) {
+            for (int t = 0; t < MT; ++t) {
                 accg[t] = acc[t];
                 acc[t] = 0.0f;
             }
         }
-        const int n = min(st.tl.w, MAXT);
+        const int n = min(st.tl.w, MT);
         const uint4 hdr = reinterpret_cast<const uint4 *>(smem + H_OFF + (j % NSLOT) * H_STAGE)[r];
         const float *slot = xs + (j % NSLOT) * (XS_SLOT / 4);
         const float d = f16_bits_to_float(hdr.x & 0xFFFF), dmin = f16_bits_to_float(hdr.x >> 16);
         const uint32_t dbase = trow + D_OFF + (uint32_t)((j % ND) * DS);
 #pragma unroll
         for (int kb = 0; kb < 8; kb += KB) {
+            // a batch's KB K steps are KB NN consecutive columns, read 32 at a time (a 32-column
+            // load costs about what an 8-column one does)
             uint32_t dv[KB][NN];
 #pragma unroll
-            for (int i = 0; i < KB; ++i) {
-                if constexpr (NN == 8) tmem_ld8(dbase + (kb + i) * NN, dv[i]);
-                else if constexpr (NN == 16) tmem_ld16(dbase + (kb + i) * NN, dv[i]);
-                else tmem_ld32(dbase + (kb + i) * NN, dv[i]);
-            }
+            for (int c = 0; c < KB * NN; c += 32)
+                tmem_ld32(dbase + kb * NN + c, *reinterpret_cast<uint32_t(*)[32]>(&dv[c / NN][c % NN]));
             tmem_ld_wait();
+            // the batch's scales first, then token by token over its K steps: one branch per token,
+            // so a token's loads and conversions for all K steps can overlap (a branch per K step
+            // serialised them)
+            float dsc[KB], ndm[KB];
 #pragma unroll
             for (int i = 0; i < KB; ++i) {
                 const int k = kb + i, s = k < 4 ? 2 * k : 2 * (k - 4) + 1;  // K step k is sub-block s
                 int scv, mv;
                 q4k_scale_min(hdr.y, hdr.z, hdr.w, s, scv, mv);
-                const float dsc = d * (float)scv, ndm = -(dmin * (float)mv);
+                dsc[i] = d * (float)scv;
+                ndm[i] = -(dmin * (float)mv);
+            }
 #pragma unroll
-                for (int t = 0; t < MAXT; ++t) {
-                    if (3 * t + 2 < NN && t < n) {
-                        const float qx = digit_sum(dv[i][3 * t], dv[i][3 * t + 1], dv[i][3 * t + 2]) * slot[t * 16 + 8 + s];
-                        acc[t] = fmaf(dsc, qx, fmaf(ndm, slot[t * 16 + s], acc[t]));
-                    }
+            for (int t = 0; t < MT; ++t) {
+                if (t >= n) break;
+#pragma unroll
+                for (int i = 0; i < KB; ++i) {
+                    const int k = kb + i, s = k < 4 ? 2 * k : 2 * (k - 4) + 1;
+                    const float qx = digit_sum(dv[i][3 * t], dv[i][3 * t + 1], dv[i][3 * t + 2]) * slot[t * 16 + 8 + s];
+                    acc[t] = fmaf(dsc[i], qx, fmaf(ndm[i], slot[t * 16 + s], acc[t]));
                 }
             }
         }
@@ -187,7 +197,7 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
         if (last || donor) {
             if (p.dual && !up) {  // this set saw only gate rows of the item (one superblock per row)
 #pragma unroll
-                for (int t = 0; t < MAXT; ++t) {
+                for (int t = 0; t < MT; ++t) {
                     accg[t] = acc[t];
                     acc[t] = 0.0f;
                 }
@@ -198,7 +208,7 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
             if (donor) {
                 if (use >= 1 && !warp_wait(&red_empty[buf], (use - 1) & 1, err, 10)) break;
 #pragma unroll
-                for (int t = 0; t < MAXT; ++t)
+                for (int t = 0; t < MT; ++t)
                     if (t < n) {
                         ru[t * ROWS + r] = acc[t];
                         rg[t * ROWS + r] = accg[t];
@@ -210,7 +220,7 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
                 if (other && !warp_wait(&red_full[buf], use & 1, err, 11)) break;
                 const int col = st.rt * ROWS + r;
 #pragma unroll
-                for (int t = 0; t < MAXT; ++t) {
+                for (int t = 0; t < MT; ++t) {
                     if (t >= n) break;
                     float v = acc[t] + (other ? ru[t * ROWS + r] : 0.0f);
                     if (p.dual) {
@@ -225,7 +235,7 @@ CK_DEV void epilogue(const Params &p, int S, int nj, uint8_t *smem, uint64_t *mm
                 if (other && lane == 0) mbar_arrive(&red_empty[buf]);
             }
 #pragma unroll
-            for (int t = 0; t < MAXT; ++t) acc[t] = accg[t] = 0.0f;
+            for (int t = 0; t < MT; ++t) acc[t] = accg[t] = 0.0f;
         }
     }
 }
