@@ -69,9 +69,9 @@ struct MoeWs {
 
 // Token tiles of the permute's table: decode-sized batches (at most CK_MOE_DECODE_TOKENS tokens) cut
 // them to CK_MOE_FEW_TOKENS tokens, so that every tile fits the few-token grouped matvec; larger
-// batches use the grouped GEMM's tiles of up to GEMM_TILE_TOKENS.  (Cutting batches of 16 and 64
-// tokens into 8-token tiles for the matvec measured slower than the GEMM on the gate/up matrices:
-// its per-step epilogue work grows with the tokens per tile.)
+// batches use the grouped GEMM's tiles of up to GEMM_TILE_TOKENS.  (Measured on the DSv3 decode
+// step: the matvec path is ahead up to 16 tokens, behind at 64, where hot experts' weights would be
+// read once per 8 of their tokens.)
 uint32_t moe_tile_tokens(uint32_t ntok) {
     return ntok <= CK_MOE_DECODE_TOKENS ? (uint32_t)CK_MOE_FEW_TOKENS : ck::GEMM_TILE_TOKENS;
 }

@@ -119,6 +119,12 @@ CK_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::c
 // grid_dep_wait (the previous kernel has completed and its writes are visible) before its first
 // global-memory access.  Both are no-ops for a kernel launched without the attribute.
 CK_DEV void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// An early trigger only from a grid that fits on the GPU at once (one CTA per SM of a B200 at
+// most): the next kernel's CTAs then wait on otherwise idle SMs.  From a larger grid they would take
+// SM room from the CTAs still running, so such a grid triggers implicitly as its CTAs exit.
+CK_DEV void grid_dep_trigger_small() {
+    if (gridDim.x * gridDim.y * gridDim.z <= 148u) grid_dep_trigger();
+}
 CK_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,

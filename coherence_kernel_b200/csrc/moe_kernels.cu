@@ -46,7 +46,7 @@ static PermWs carve(void *ws, const PermuteParams &p) {
 // a pair among its expert's pairs in this chunk follows the (token, slot) order exactly.
 __global__ void k_perm_hist(const int32_t *__restrict__ ids, uint32_t npairs, uint32_t E, int32_t *__restrict__ chunk_hist,
                             int32_t *__restrict__ local_rank) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     __shared__ int32_t cnt[MAX_EXPERTS];
     const int lane = threadIdx.x;
@@ -114,7 +114,7 @@ __device__ __forceinline__ int seg_tiles(int c, int bn, int &base) {
 __global__ void __launch_bounds__(1024) k_perm_scan(int32_t *__restrict__ chunk_hist, uint32_t nchunks, PermuteParams p,
                                                     int32_t *__restrict__ expert_off, int32_t *__restrict__ counts,
                                                     int4 *__restrict__ tiles, int32_t *__restrict__ ntiles) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     const int e = threadIdx.x;
     int c = 0;
@@ -158,7 +158,7 @@ __global__ void k_perm_scatter(const int32_t *__restrict__ ids, const float *__r
                                int32_t *__restrict__ pair_pos, const int32_t *__restrict__ chunk_off,
                                const int32_t *__restrict__ local_rank, const int32_t *__restrict__ expert_off,
                                PermuteParams p) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     const uint32_t A = p.ntok * p.nsel;
     const uint32_t wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -384,20 +384,21 @@ int launch_ep_plan(const int32_t *ids, const float *wts, uint32_t ntok, uint32_t
     return (int)cudaGetLastError();
 }
 
-// Combine: a token's row is split over gridDim.y blocks of CMB_THREADS threads, one 8-column vector
-// per thread.  order_by_expert = 1 is moe-mix (moe-gate.fk:32-37): the chosen experts in ascending
+// Combine: a token's row is split over gridDim.y blocks of CMB_THREADS threads, 8-column vectors
+// strided over them (small batches: one vector per thread; large ones: one block per token, which
+// sets the token's slots up once).  order_by_expert = 1 is moe-mix (moe-gate.fk:32-37): the chosen experts in ascending
 // index, acc + g*y.  order_by_expert = 0 is dsv4-moe-acc (dsv4-forward.fk:100-103): the slots in
 // list order, acc + y (the weight was applied inside the expert).  Shared experts are added after,
 // in index order.  fp32 accumulation, bf16 out.  The token's slots (row position and weight, in
 // summation order) are set up once per block in shared memory, and a thread issues all its rows'
 // loads before it adds them in that order: per-slot dependent loads made a decode-sized combine a
 // chain of memory round trips.
-constexpr int CMB_THREADS = 128;
+constexpr int CMB_THREADS = 256;
 __global__ void __launch_bounds__(CMB_THREADS) k_combine(const uint16_t *__restrict__ y, const int32_t *__restrict__ ids,
                                                          const float *__restrict__ wts, const int32_t *__restrict__ pair_pos,
                                                          uint16_t *__restrict__ out, float *__restrict__ out_f32,
                                                          PermuteParams p, int order_by_expert) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     const uint32_t t = blockIdx.x;
     const uint32_t A = p.ntok * p.nsel;
@@ -411,75 +412,75 @@ __global__ void __launch_bounds__(CMB_THREADS) k_combine(const uint16_t *__restr
         s_g[k] = order_by_expert ? wts[t * p.nsel + k] : 1.0f;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        // the summation order: ascending expert, stable (insertion sort), or the list order
-        for (int k = 0; k < ns; ++k) s_ord[k] = k;
-        if (order_by_expert)
-            for (int i = 1; i < ns; ++i) {
-                const int v = s_ord[i];
-                int j = i - 1;
-                while (j >= 0 && s_id[s_ord[j]] > s_id[v]) {
-                    s_ord[j + 1] = s_ord[j];
-                    --j;
-                }
-                s_ord[j + 1] = v;
-            }
+    if ((int)threadIdx.x < ns) {
+        // the summation order: ascending expert, ties in list order (a stable sort), or the list
+        // order; slot k's place is the number of slots that come before it
+        const int k = (int)threadIdx.x;
+        int rank = k;
+        if (order_by_expert) {
+            rank = 0;
+            for (int i = 0; i < ns; ++i) rank += s_id[i] < s_id[k] || (s_id[i] == s_id[k] && i < k);
+        }
+        s_ord[rank] = k;
     }
     __syncthreads();
-    const uint32_t v = blockIdx.y * CMB_THREADS + threadIdx.x;
-    if (v >= p.hidden / 8) return;
-    uint4 q[16];
-    int pos[16];
-    float g[16];
+    for (uint32_t v = blockIdx.y * CMB_THREADS + threadIdx.x; v < p.hidden / 8; v += gridDim.y * CMB_THREADS) {
+        float acc[8];
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-        pos[kk] = -1;
-        if (kk < ns) {
-            pos[kk] = s_pos[s_ord[kk]];
-            g[kk] = s_g[s_ord[kk]];
-            if (pos[kk] >= 0) q[kk] = __ldg(reinterpret_cast<const uint4 *>(y + (size_t)pos[kk] * p.hidden) + v);
-        }
-    }
-    float acc[8];
+        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+        // eight slots' loads at a time, then their adds in order
+        for (int k0 = 0; k0 < ns; k0 += 8) {
+            uint4 q[8];
+            int pos[8];
+            float g[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+            for (int kk = 0; kk < 8; ++kk) {
+                pos[kk] = -1;
+                if (k0 + kk < ns) {
+                    pos[kk] = s_pos[s_ord[k0 + kk]];
+                    g[kk] = s_g[s_ord[k0 + kk]];
+                    if (pos[kk] >= 0) q[kk] = __ldg(reinterpret_cast<const uint4 *>(y + (size_t)pos[kk] * p.hidden) + v);
+                }
+            }
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-        if (pos[kk] < 0) continue;  // a slot this layer did not compute (another rank's expert)
-        const uint32_t qq[4] = {q[kk].x, q[kk].y, q[kk].z, q[kk].w};
+            for (int kk = 0; kk < 8; ++kk) {
+                if (pos[kk] < 0) continue;  // a slot this layer did not compute (another rank's expert)
+                const uint32_t qq[4] = {q[kk].x, q[kk].y, q[kk].z, q[kk].w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float lo = __uint_as_float(qq[i] << 16), hi = __uint_as_float(qq[i] & 0xFFFF0000u);
-            if (order_by_expert) {
-                acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(g[kk], lo));
-                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(g[kk], hi));
-            } else {
-                acc[2 * i] = __fadd_rn(acc[2 * i], lo);
-                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], hi);
+                for (int i = 0; i < 4; ++i) {
+                    const float lo = __uint_as_float(qq[i] << 16), hi = __uint_as_float(qq[i] & 0xFFFF0000u);
+                    if (order_by_expert) {
+                        acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(g[kk], lo));
+                        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(g[kk], hi));
+                    } else {
+                        acc[2 * i] = __fadd_rn(acc[2 * i], lo);
+                        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], hi);
+                    }
+                }
             }
         }
-    }
-    for (uint32_t sh = 0; sh < p.n_shared; ++sh) {
-        const uint4 qs = __ldg(reinterpret_cast<const uint4 *>(y + ((size_t)A + (size_t)sh * p.ntok + t) * p.hidden) + v);
-        const uint32_t qq[4] = {qs.x, qs.y, qs.z, qs.w};
+        for (uint32_t sh = 0; sh < p.n_shared; ++sh) {
+            const uint4 qs = __ldg(reinterpret_cast<const uint4 *>(y + ((size_t)A + (size_t)sh * p.ntok + t) * p.hidden) + v);
+            const uint32_t qq[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(qq[i] << 16));
-            acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(qq[i] & 0xFFFF0000u));
+            for (int i = 0; i < 4; ++i) {
+                acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(qq[i] << 16));
+                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(qq[i] & 0xFFFF0000u));
+            }
         }
-    }
-    if (out) {
-        uint4 o;
-        o.x = pack_bf16x2(acc[0], acc[1]);
-        o.y = pack_bf16x2(acc[2], acc[3]);
-        o.z = pack_bf16x2(acc[4], acc[5]);
-        o.w = pack_bf16x2(acc[6], acc[7]);
-        reinterpret_cast<uint4 *>(out + (size_t)t * p.hidden)[v] = o;
-    }
-    if (out_f32) {
-        float4 *o4 = reinterpret_cast<float4 *>(out_f32 + (size_t)t * p.hidden + v * 8);
-        o4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        o4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        if (out) {
+            uint4 o;
+            o.x = pack_bf16x2(acc[0], acc[1]);
+            o.y = pack_bf16x2(acc[2], acc[3]);
+            o.z = pack_bf16x2(acc[4], acc[5]);
+            o.w = pack_bf16x2(acc[6], acc[7]);
+            reinterpret_cast<uint4 *>(out + (size_t)t * p.hidden)[v] = o;
+        }
+        if (out_f32) {
+            float4 *o4 = reinterpret_cast<float4 *>(out_f32 + (size_t)t * p.hidden + v * 8);
+            o4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            o4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        }
     }
 }
 
@@ -488,7 +489,8 @@ int launch_combine(const uint16_t *y, const int32_t *ids, const float *wts, cons
     if (p.hidden % 8 != 0 || p.nsel > 16) return CK_ERR_SHAPE;
     if (!y || !ids || !pair_pos || (!out && !out_f32) || (order_by_expert && !wts)) return CK_ERR_ARG;
     if (p.ntok) {
-        const cudaError_t e = launch_pdl(k_combine, dim3(p.ntok, (p.hidden / 8 + CMB_THREADS - 1) / CMB_THREADS),
+        const uint32_t split = p.ntok <= 256 ? (p.hidden / 8 + CMB_THREADS - 1) / CMB_THREADS : 1;
+        const cudaError_t e = launch_pdl(k_combine, dim3(p.ntok, split),
                                          dim3(CMB_THREADS), 0, s, y, ids, wts, pair_pos, out, out_f32, p, order_by_expert);
         if (e != cudaSuccess) return (int)e;
     }

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(XF_WARPS * 32) k_exact_logits_few(const uint16
                                                                     const uint32_t *__restrict__ flag_count,
                                                                     double *__restrict__ out, uint32_t ne,
                                                                     uint32_t hidden) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     extern __shared__ __align__(16) uint8_t xf_smem[];
     const uint32_t nflag = *flag_count;
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(256) k_exact_logits(const uint16_t *__restrict
                                                       const uint32_t *__restrict__ flag_list,
                                                       const uint32_t *__restrict__ flag_count, double *__restrict__ out,
                                                       uint32_t ne, uint32_t hidden) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     __shared__ double wt[2][XL_EXP][XL_J + 1];
     __shared__ __align__(16) double xt[2][XL_TOK][XL_J];
@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(256) k_exact_select(const double *__restrict__
                                                       int32_t *__restrict__ ids, float *__restrict__ wts,
                                                       const uint32_t *__restrict__ flag_list,
                                                       const uint32_t *__restrict__ flag_count, RouteParams p) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     __shared__ double sbuf[256], sprob[256];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;

@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(256, 2) k_router_logits_few(const uint16_t *__
                                                               double *__restrict__ Ld, float *__restrict__ sabs,
                                                               uint32_t *__restrict__ flag_count, uint32_t T, uint32_t E,
                                                               uint32_t H) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     // the selection's flagged-token counter starts at zero (cleared here: a memset would end the
     // chain of dependent launches)
@@ -213,7 +213,7 @@ template <typename T>
 __global__ void k_route_select(const T *__restrict__ L, const float *__restrict__ sabs,
                                const float *__restrict__ bias, int32_t *__restrict__ ids, float *__restrict__ wts,
                                uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p) {
-    grid_dep_trigger();
+    grid_dep_trigger_small();
     grid_dep_wait();
     constexpr bool CTA = sizeof(T) == 8;  // the fp64 form: a CTA of 256 threads per token
     const int lane = threadIdx.x & 31;

@@ -25,7 +25,7 @@ from .ops import _dev, _ptr, _stream, q4k_nbytes
 # permuted into tiles of at most FEW_TOKENS tokens and run the expert projections as the few-token
 # grouped matvec
 FEW_TOKENS = 8
-DECODE_TOKENS = 8
+DECODE_TOKENS = 16
 
 
 @dataclass

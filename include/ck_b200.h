@@ -143,7 +143,7 @@ int ck_moe_expert_gemm(int dual, const void *w0_dev, const void *w1_dev, const v
 #define CK_MOE_FEW_TOKENS 8
 /* batches of at most this many tokens are permuted into tiles of at most CK_MOE_FEW_TOKENS tokens
  * (ck_moe_permute, ck_moe_max_tiles) and their expert projections run the few-token matvec */
-#define CK_MOE_DECODE_TOKENS 8
+#define CK_MOE_DECODE_TOKENS 16
 int ck_moe_expert_gemm_bounded(int dual, const void *w0_dev, const void *w1_dev, const void *s0_dev,
                                const void *s1_dev, uint64_t w_stride, uint32_t n_routed, uint32_t n_shared,
                                const void *x_bf16_dev, uint32_t x_rows, void *out_bf16_dev, uint32_t out_rows,
