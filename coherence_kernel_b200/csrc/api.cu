@@ -69,9 +69,9 @@ struct MoeWs {
 
 // Token tiles of the permute's table: decode-sized batches (at most CK_MOE_DECODE_TOKENS tokens) cut
 // them to CK_MOE_FEW_TOKENS tokens, so that every tile fits the few-token grouped matvec; larger
-// batches use the grouped GEMM's tiles of up to GEMM_TILE_TOKENS.  (Measured on the DSv3 decode
-// step: the matvec path is ahead up to 16 tokens, behind at 64, where hot experts' weights would be
-// read once per 8 of their tokens.)
+// batches use the grouped GEMM's tiles of up to GEMM_TILE_TOKENS.  Five tokens (15 accumulator
+// columns per K step, 16 with the padding) is the most whose accumulators fit twice in the
+// matvec's tensor memory beside its weight stages.
 uint32_t moe_tile_tokens(uint32_t ntok) {
     return ntok <= CK_MOE_DECODE_TOKENS ? (uint32_t)CK_MOE_FEW_TOKENS : ck::GEMM_TILE_TOKENS;
 }
@@ -274,12 +274,12 @@ int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const flo
     if (ntok == 0) return 0;
     RouteWs w = route_ws(c, ntok, ws);
     ck::RouteParams p = {ntok, c->n_experts, c->nsel, c->hidden, c->mode, c->ngroups, c->topk_groups, c->wscale, c->tau};
-    // A decode-sized batch (at most 64 tokens): the router as a matvec over all SMs with compensated
+    // A decode-sized batch (at most CK_MOE_DECODE_TOKENS tokens): the router as a matvec over all SMs with compensated
     // sums, selected in fp64 with a margin sized by the dot's own rounding (about 1e-9 here), so in
     // practice only exact ties take the fp64 re-route.  Otherwise the logits run on the tensor cores,
     // x . [W1 | W2 | W3]^T with the fp32 router split into bf16 terms, and are selected in fp32
     // with the margin tau.
-    rc = ntok <= 64 ? ck::launch_router_logits_few((const uint16_t *)x, rw, logits, w.exact, w.sabs, w.flags, ntok,
+    rc = ntok <= CK_MOE_DECODE_TOKENS ? ck::launch_router_logits_few((const uint16_t *)x, rw, logits, w.exact, w.sabs, w.flags, ntok,
                                                    c->n_experts, c->hidden, S(s))
                     : CK_ERR_SHAPE;
     if (rc == 0) {

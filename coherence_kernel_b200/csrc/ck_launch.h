@@ -46,8 +46,8 @@ struct RouteParams {
     float wscale;          // mode 4 weight scale
     float tau;             // decision margin below which a token is re-routed exactly in fp64
 };
-// router logits for at most 64 tokens (compensated sums over the fp32 router) in fp32 and fp64, with
-// sum |w x| per logit; ntok > 64 returns CK_ERR_SHAPE
+// router logits for at most 128 tokens (compensated sums over the fp32 router) in fp32 and fp64, with
+// sum |w x| per logit; ntok > 128 returns CK_ERR_SHAPE
 int launch_router_logits_few(const uint16_t *x, const float *w, float *L, double *Ld, float *sabs, uint32_t *flag_count, uint32_t T,
                              uint32_t E, uint32_t H, cudaStream_t s);
 // the fast selection over fp64 logits (the decode-batch form); its margin scales with sabs

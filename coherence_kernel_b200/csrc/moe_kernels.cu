@@ -192,8 +192,9 @@ __global__ void k_perm_scatter(const int32_t *__restrict__ ids, const float *__r
 int launch_permute(const int32_t *ids, const float *wts, const uint16_t *x, uint16_t *xp, float *row_w,
                    int32_t *pair_pos, int32_t *counts, int4 *tiles, int32_t *ntiles, void *workspace,
                    const PermuteParams &p, cudaStream_t s) {
+    // tiles of up to 8 tokens (the few-token matvec's), or a multiple of 8 up to the GEMM's tile
     if (p.n_experts == 0 || p.n_experts > MAX_EXPERTS || p.nsel == 0 || p.hidden % 8 != 0 || p.bn == 0 ||
-        p.bn % 8 != 0 || p.bn > GEMM_TILE_TOKENS)
+        (p.bn > 8 && p.bn % 8 != 0) || p.bn > GEMM_TILE_TOKENS)
         return CK_ERR_SHAPE;
     if (!ids || !x || !xp || !row_w || !pair_pos || !counts || !tiles || !ntiles || !workspace) return CK_ERR_ARG;
     PermWs w = carve(workspace, p);

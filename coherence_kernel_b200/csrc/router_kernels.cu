@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const uint16_t *__restric
 // (the loop is bound by load latency).  The lanes' pairs are merged by two-sums in a fixed shuffle
 // tree and the eighths in order; the logit is written in fp64 (for the fp64 selection) and fp32,
 // with sum |w x| beside it (the scale of every rounding error in the dot).
-constexpr uint32_t RS_TMAX = 64;  // tokens
+constexpr uint32_t RS_TMAX = 128;  // tokens
 constexpr uint32_t RS_IT = 8;     // float4 per lane of a warp's eighth of the row: hidden <= 8192
 // (explicit round-to-nearest intrinsics: a contracted multiply-add would break the two-sum)
 CK_DEV void two_sum_into(float &s, float &c, float p) {

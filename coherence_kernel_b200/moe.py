@@ -24,8 +24,8 @@ from .ops import _dev, _ptr, _stream, q4k_nbytes
 # CK_MOE_FEW_TOKENS / CK_MOE_DECODE_TOKENS of ck_b200.h: batches up to DECODE_TOKENS tokens are
 # permuted into tiles of at most FEW_TOKENS tokens and run the expert projections as the few-token
 # grouped matvec
-FEW_TOKENS = 8
-DECODE_TOKENS = 16
+FEW_TOKENS = 5
+DECODE_TOKENS = 128
 
 
 @dataclass

@@ -136,14 +136,16 @@ int ck_moe_expert_gemm(int dual, const void *w0_dev, const void *w1_dev, const v
                        const int32_t *ntiles_dev, uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow,
                        int *err_dev, void *stream);
 /* ck_moe_expert_gemm with a bound on the tokens of every tile of the table (0: none known).  A bound
- * of 1..CK_MOE_FEW_TOKENS streams the expert weights through the few-token grouped matvec on the
- * integer tensor cores (where n % 128 == 0, k % 256 == 0 and the pointers are 16-byte aligned);
- * the results agree with the grouped GEMM's to its bf16 output rounding.  ck_moe_layer_bf16 passes
- * min(ntok, CK_MOE_FEW_TOKENS) when ntok <= CK_MOE_DECODE_TOKENS. */
-#define CK_MOE_FEW_TOKENS 8
+ * of 1..8 streams the expert weights through the few-token grouped matvec on the integer tensor
+ * cores (where n % 128 == 0, k % 256 == 0 and the pointers are 16-byte aligned); the results agree
+ * with the grouped GEMM's to its bf16 output rounding.  ck_moe_layer_bf16 passes
+ * min(ntok, CK_MOE_FEW_TOKENS) when ntok <= CK_MOE_DECODE_TOKENS.  Up to 5 tokens a tile's
+ * accumulators fit twice in tensor memory, so the matvec of one step overlaps the epilogue of the
+ * step before; 6 to 8 tokens fit once. */
+#define CK_MOE_FEW_TOKENS 5
 /* batches of at most this many tokens are permuted into tiles of at most CK_MOE_FEW_TOKENS tokens
  * (ck_moe_permute, ck_moe_max_tiles) and their expert projections run the few-token matvec */
-#define CK_MOE_DECODE_TOKENS 16
+#define CK_MOE_DECODE_TOKENS 128
 int ck_moe_expert_gemm_bounded(int dual, const void *w0_dev, const void *w1_dev, const void *s0_dev,
                                const void *s1_dev, uint64_t w_stride, uint32_t n_routed, uint32_t n_shared,
                                const void *x_bf16_dev, uint32_t x_rows, void *out_bf16_dev, uint32_t out_rows,

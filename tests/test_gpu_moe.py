@@ -137,17 +137,17 @@ def test_moe_exact_reroute_covers_ties():
 
 
 def test_moe_dsv3_decode_sizes():
-    """At most 64 tokens (a decode-sized batch) the router logits run as a matvec with compensated
+    """At most 128 tokens (a decode-sized batch) the router logits run as a matvec with compensated
     float-pair sums (accurate to the logits' fp32 rounding), few flagged tokens take one exact fold
-    chain per lane, and up to 16 tokens the expert projections run the few-token grouped matvec on
-    tiles of at most 8 tokens: ids, counts and weights against the oracle's routing at 1, 3, 8, 16
-    and 64 tokens, outputs against the oracle's layer (all tokens up to 8, a sample beyond)."""
+    chain per lane, and up to 128 tokens the expert projections run the few-token grouped matvec on
+    tiles of at most 5 tokens: ids, counts and weights against the oracle's routing at 1, 3, 8, 16,
+    64 and 128 tokens, outputs against the oracle's layer (all tokens up to 8, a sample beyond)."""
     spec = workloads.MOE_DSV3
-    w = workloads.make_moe(spec, 64, seed=5)
-    lay = layer_for(spec, w, 64)
+    w = workloads.make_moe(spec, 128, seed=5)
+    lay = layer_for(spec, w, 128)
     cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
                     spec.topk_groups, spec.wscale)
-    for n in (1, 3, 8, 16, 64):
+    for n in (1, 3, 8, 16, 64, 128):
         x = np.ascontiguousarray(w["x"][:n])
         out, ids, wts, counts = lay(torch.from_numpy(x.view(np.int16)).cuda())
         lay.status(n)
@@ -159,7 +159,8 @@ def test_moe_dsv3_decode_sizes():
         assert np.array_equal(ids, rids)
         assert np.array_equal(counts, np.bincount(rids.reshape(-1), minlength=spec.n_experts))
         assert np.allclose(wts, rwts, rtol=1e-5, atol=1e-7)
-        toks = np.arange(n) if n <= 8 else np.array([0, 9, 15]) if n == 16 else np.array([0, 9, 23, 40, 63])
+        toks = (np.arange(n) if n <= 8 else np.array([0, 9, 15]) if n == 16 else np.array([0, 9, 23, 40, 63]) if n == 64
+                else np.array([0, 41, 64, 99, 127]))
         sids, _, sout = O.moe_layer(cfg, w, x, toks)
         assert np.array_equal(sids, ids[toks])
         check_outputs(out.float().cpu().numpy()[toks], sout)
