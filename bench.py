@@ -133,8 +133,8 @@ def zipf_bias(rng, spec, slope=1.1, c=1.0):
 def sub_benchmarks(torch, dev, hbm, tc_burst):
     """The other configurations on one GPU: Q8_0 decode matvec 4096^2, Q4_K prefill 11008x4096 at
     each M, the small MoE layer, and the decode-shaped sweep (dense stand-in + the DSv3 layer at
-    batch 1, 4, 16, 64 with Zipf(1.1) expert load).  Small kernels are timed as CUDA-graph replays
-    over rotating weight copies (more bytes than L2)."""
+    batch 1, 4, 16, 64, 128 with Zipf(1.1) expert load).  Small kernels and the decode steps are
+    timed as CUDA-graph replays over rotating weight copies (more bytes than L2)."""
     from coherence_kernel_b200 import ops, synth, workloads
     from coherence_kernel_b200.moe import MoELayer
     out = {}
@@ -239,7 +239,7 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
     zipf_slope = slope_for(zipf_c)
     del xcal
     sweep = {}
-    for bsz in (1, 4, 16, 64):
+    for bsz in (1, 4, 16, 64, 128):
         xx = t(w["x"][:bsz].view(np.int16))
         o = torch.empty((bsz, sp.hidden), dtype=torch.bfloat16, device=dev)
 
@@ -250,19 +250,16 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
         for k in range(3):
             step(k)
         torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for k in range(20):
-            step(k)
-        b.record()
-        torch.cuda.synchronize()
-        us = a.elapsed_time(b) * 1e3 / 20
+        # a decode engine replays its step as a CUDA graph: four steps (all 16 dense weight copies)
+        # captured once and replayed, so the host's launch gaps are not in the step time
+        us = _graph_us(torch, step, 4, 4)
         _, ids, _, _ = step(0)
         U = len(set(ids.cpu().numpy().reshape(-1).tolist()))
         nb = 4 * (7168 * 7168 // 256 * 144) + (U + 1) * 3 * sp.matrix_bytes
         sweep[f"b{bsz}"] = {"us_per_step": round(us, 1), "experts_touched": U, "bytes_per_token": nb // bsz,
                             "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
     out["decode_sweep"] = {"steps": sweep, "dense_matvec_us": round(dense_us, 2),
+                           "timing": "CUDA graph of 4 decode steps, replayed 5 times after 3 warm replays",
                            "zipf": {"bias": "c*log(rank^-1.1), seeded ranking", "c": round(zipf_c, 3),
                                     "measured_slope": round(zipf_slope, 3), "tokens": ncal,
                                     "fit": "log load vs log rank over experts with >= 8 tokens"}}
