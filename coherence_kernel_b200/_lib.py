@@ -39,7 +39,9 @@ SIGNATURES = {
     "ck_q4k_matmul_batch_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
     "ck_q4k_gemm_workspace_bytes": (_sz, [_u32]),
     "ck_q4k_gemm_bf16": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p, _sz, _p]),
+    "ck_q4k_gemm_status": (_i32, [_u32, _p, _p]),
     "ck_q4k_gemm_bf16_noalloc": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
+    "ck_q4k_gemm_bf16_noalloc_status": (_i32, [_p]),
     "ck_f16_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_route_softmax_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _i32, _p]),
     "ck_route_dsv4_f32": (_i32, [_p, _p, _p, _p, _u32, _u32, _f, _u32, _p]),
@@ -64,6 +66,7 @@ SIGNATURES = {
     "ck_token_tiles": (_i32, [_p, _p, _u32, _p]),
     "ck_gather_rows": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_ep_dispatch_plan": (_i32, [_p, _p, _u32, _u32, _u32, _u32, _p, _p, _p, _p, _p, _p]),
+    "ck_wait_selftest": (_i32, [_u64, _p, _p, _p]),
     # the handle door
     "fk_metal_pipeline_external": (_ll, [ctypes.c_char_p, _ll, ctypes.c_char_p, _ll]),
     "fk_metal_buf_alloc_external": (_ll, [_ll]),

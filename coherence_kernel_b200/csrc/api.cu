@@ -209,6 +209,21 @@ int ck_q4k_gemm_bf16(const void *qb, const void *x, void *y, uint32_t rows, uint
     return fail(ck::launch_gemm_q4k(p, S(s)), "ck_q4k_gemm_bf16");
 }
 
+// Reads the error word ck_q4k_gemm_bf16 left in its workspace (synchronizes the stream).
+int ck_q4k_gemm_status(uint32_t ntok, const void *ws, void *s) {
+    if (!ws) return fail(CK_EARG, "ck_q4k_gemm_status");
+    const size_t tb = al(((size_t)ntok / 16 + 2) * 16);
+    int e = 0;
+    cudaError_t r = cudaMemcpyAsync(&e, (const uint8_t *)ws + tb + 256, 4, cudaMemcpyDeviceToHost, S(s));
+    if (r == cudaSuccess) r = cudaStreamSynchronize(S(s));
+    if (r != cudaSuccess) return fail((int)r, "ck_q4k_gemm_status");
+    if (e) {
+        snprintf(g_err, sizeof(g_err), "ck_q4k_gemm_bf16: device wait timed out (role code %d)", e);
+        return CK_ETIMEOUT;
+    }
+    return 0;
+}
+
 int ck_f16_matvec_f32(const void *w, const float *x, float *y, uint32_t rows, uint32_t cols, void *s) {
     if (!w || !x || !y) return fail(CK_EARG, "ck_f16_matvec_f32");
     return fail(ck::launch_f16_matvec((const uint16_t *)w, x, y, rows, cols, S(s)), "ck_f16_matvec_f32");
@@ -495,17 +510,19 @@ int noalloc_scratch(void **out) {
 
 extern "C" int ck_q4k_gemm_bf16_noalloc(const void *qb, const void *x, void *y, uint32_t rows, uint32_t cols,
                                         uint32_t ntok, void *s) {
-    if (!qb || !x || !y) return fail(CK_EARG, "ck_q4k_gemm_bf16_noalloc");
     if (ntok > CK_Q4K_GEMM_NOALLOC_MAX_TOKENS) {
         static thread_local char what[160];
         snprintf(what, sizeof(what), "ck_q4k_gemm_bf16_noalloc: %u tokens, the fixed scratch holds at most %u",
                  ntok, (unsigned)CK_Q4K_GEMM_NOALLOC_MAX_TOKENS);
         return fail(CK_ESHAPE, what);
     }
+    // the set-up comes before the pointer check, so that a warm-up call with ntok == 0 (null
+    // pointers allowed) looks the array up outside any stream capture
     void *base = nullptr;
     int rc = noalloc_scratch(&base);
     if (rc) return fail(rc, "ck_q4k_gemm_bf16_noalloc scratch address");
     if (ntok == 0) return 0;
+    if (!qb || !x || !y) return fail(CK_EARG, "ck_q4k_gemm_bf16_noalloc");
     uint8_t *b = (uint8_t *)base;
     int4 *tiles = (int4 *)b;
     int32_t *ntiles = (int32_t *)(b + kNoallocTileRegion);
@@ -532,4 +549,22 @@ extern "C" int ck_q4k_gemm_bf16_noalloc(const void *qb, const void *x, void *y, 
     p.K = cols;
     p.err = err;
     return fail(ck::launch_gemm_q4k(p, S(s)), "ck_q4k_gemm_bf16_noalloc");
+}
+
+// Reads the error word the last ck_q4k_gemm_bf16_noalloc call on the current device left in the
+// fixed scratch (synchronizes `stream`).  It shares the scratch's rule: a call still in flight on
+// another stream may rewrite the word.
+extern "C" int ck_q4k_gemm_bf16_noalloc_status(void *s) {
+    void *base = nullptr;
+    int rc = noalloc_scratch(&base);
+    if (rc) return fail(rc, "ck_q4k_gemm_bf16_noalloc_status scratch address");
+    int e = 0;
+    cudaError_t r = cudaMemcpyAsync(&e, (uint8_t *)base + kNoallocTileRegion + 256, 4, cudaMemcpyDeviceToHost, S(s));
+    if (r == cudaSuccess) r = cudaStreamSynchronize(S(s));
+    if (r != cudaSuccess) return fail((int)r, "ck_q4k_gemm_bf16_noalloc_status");
+    if (e) {
+        snprintf(g_err, sizeof(g_err), "ck_q4k_gemm_bf16_noalloc: device wait timed out (role code %d)", e);
+        return CK_ETIMEOUT;
+    }
+    return 0;
 }

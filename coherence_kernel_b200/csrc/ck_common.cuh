@@ -84,20 +84,24 @@ CK_DEV uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-// Bounded wait: gives up after about one second, records `code` in the error word and returns
-// false, so a broken pipeline ends the kernel with a status the host reads instead of hanging.
-CK_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err, int code) {
+// Bounded wait: gives up after `limit_ns` (about one second in every pipeline), records `code` in
+// the error word and returns false, so a broken pipeline ends the kernel with a status the host
+// reads instead of hanging.
+CK_DEV bool mbar_wait_bounded_ns(uint64_t *bar, uint32_t parity, int *err, int code, uint64_t limit_ns) {
     if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 1023u) == 0) {
             if (err && *(volatile int *)err) return false;  // another role already gave up
-            if (globaltimer_ns() - t0 > 1000000000ull) break;
+            if (globaltimer_ns() - t0 > limit_ns) break;
         }
     }
     if (err) atomicCAS(err, 0, code);
     return false;
+}
+CK_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err, int code) {
+    return mbar_wait_bounded_ns(bar, parity, err, code, 1000000000ull);
 }
 
 // ----------------------------------------------------------------------------- TMA

@@ -116,6 +116,10 @@ class Q4KGemm:
                                                 _ptr(self.ws), self.ws_bytes, _stream()), "ck_q4k_gemm_bf16")
         return y
 
+    def status(self, ntok):
+        """Synchronize and raise if a device-side wait of the last call (over ntok tokens) gave up."""
+        _lib.check(_lib.load().ck_q4k_gemm_status(ntok, _ptr(self.ws), _stream()), "ck_q4k_gemm_status")
+
 
 def route_softmax(logits, nsel, renorm=True):
     ntok, ne = logits.shape

@@ -59,18 +59,27 @@ int ck_q4k_matmul_batch_f32(const void *qb_dev, const float *x_dev, float *y_dev
 size_t ck_q4k_gemm_workspace_bytes(uint32_t ntok);
 int ck_q4k_gemm_bf16(const void *qb_dev, const void *x_bf16_dev, void *y_bf16_dev, uint32_t rows, uint32_t cols,
                      uint32_t ntok, void *workspace_dev, size_t workspace_bytes, void *stream);
+/* After a ck_q4k_gemm_bf16 call with this workspace and ntok: synchronizes `stream` and returns
+ * CK_ETIMEOUT when a device-side wait of the GEMM gave up (y is then not valid), else 0. */
+int ck_q4k_gemm_status(uint32_t ntok, const void *workspace_dev, void *stream);
 
 /* The same GEMM for callers that cannot allocate or hand over a workspace (a host runtime with its
  * own arenas and no CUDA-aware allocator, a serving loop that must not allocate per request).  No
  * counterpart in the reference, whose matmul kernels take no scratch.  The scratch lives in one
  * fixed array in device memory (about 65 KB), so ntok <= CK_Q4K_GEMM_NOALLOC_MAX_TOKENS; larger
  * ntok fails with CK_ESHAPE.  The first call on a device looks the array up (it may load the
- * module): make it, with any ntok including 0, before stream capture.  Every call on a device
- * shares the array and leaves its contents behind; calls that overlap in time on one device race
- * on it and must be serialized by the caller. */
+ * module): make it before stream capture -- a call with ntok 0 does only that, and accepts null
+ * pointers.  The address is cached per device for the life of the process, so cudaDeviceReset is
+ * not supported between calls.  Every call on a device shares the array and leaves its contents
+ * behind; calls that overlap in time on one device race on it and must be serialized by the
+ * caller. */
 #define CK_Q4K_GEMM_NOALLOC_MAX_TOKENS 65536u
 int ck_q4k_gemm_bf16_noalloc(const void *qb_dev, const void *x_bf16_dev, void *y_bf16_dev, uint32_t rows,
                              uint32_t cols, uint32_t ntok, void *stream);
+/* Synchronizes `stream` and returns CK_ETIMEOUT when a device-side wait of the last
+ * ck_q4k_gemm_bf16_noalloc call on the current device gave up (its y is then not valid), else 0.
+ * The error word lives in the same shared array, so the serialization rule above applies. */
+int ck_q4k_gemm_bf16_noalloc_status(void *stream);
 
 /* ---- small kernels of the reference's MoE decode (moe-msl.fk:114-140, dsv4-moe-msl.fk:87-88,
  *      dsv4-router-msl.fk:103-106, moe-route-wide-msl.fk) -- one routing per token, ntok tokens */
@@ -172,6 +181,13 @@ int ck_gather_rows(const void *src_dev, const int32_t *idx_dev, void *dst_dev, u
 int ck_ep_dispatch_plan(const int32_t *ids_dev, const float *wts_dev, uint32_t ntok, uint32_t nsel,
                         uint32_t n_experts, uint32_t world, int32_t *counts_dev, int64_t *sizes_dev,
                         int32_t *send_tok_dev, int32_t *meta_dev, int32_t *ret_pos_dev, void *stream);
+
+/* Failure-path self-test (no counterpart in the reference).  Runs the library's bounded device wait
+ * on an mbarrier that nothing ever arrives on, with a time limit of limit_ns (1 ns .. 2 s): the wait
+ * gives up, writes code 77 to *err_dev (which the caller zeroes first) and the time it waited to
+ * *waited_ns_dev, and the kernel returns.  Every pipeline here ends a stuck wait the same way,
+ * with its own code in its own error word. */
+int ck_wait_selftest(uint64_t limit_ns, int *err_dev, unsigned long long *waited_ns_dev, void *stream);
 
 #ifdef __cplusplus
 }

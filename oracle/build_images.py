@@ -6,7 +6,7 @@ linked with the CUDA carrier (oracle/_ref/fkwu-cuda) into oracle/_ref/fk-cuda/. 
 without the reference tree, so they travel with the repository to a machine that has none.  Test
 infrastructure only.
 
-    python oracle/build_images.py [--ref /root/reference]
+    python oracle/build_images.py --ref <the reference tree>   (or CK_REFERENCE=<tree>)
 """
 from __future__ import annotations
 
@@ -67,5 +67,8 @@ def build(ref: str) -> list:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
-    print("images:", build(ap.parse_args().ref))
+    ap.add_argument("--ref", default=os.environ.get("CK_REFERENCE"))
+    a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref <the reference tree> (or CK_REFERENCE) is required")
+    print("images:", build(a.ref))

@@ -6,10 +6,10 @@ oracle/fk/, and writes inputs + fp64 outputs as small .npz fixtures beside this 
 copies the reference's two real-weight fixtures (q4k-two-superblocks.bin, q8-0-three-blocks.bin)
 and records every weight the reference decodes from them.
 
-Needs the reference tree (default /root/reference) and runs only where it is present; the
+Needs the reference tree, named by --ref or CK_REFERENCE, and runs only where it is present; the
 fixtures it writes are committed and are all that the tests read.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <the reference tree> [--only quant,fixtures,route,moe]
 """
 from __future__ import annotations
 
@@ -108,9 +108,11 @@ def golden_ref_fixtures(fr: FormRunner, ref: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("CK_REFERENCE"))
     ap.add_argument("--only", default="")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref <the reference tree> (or CK_REFERENCE) is required")
     if not os.path.exists(FKWU):
         subprocess.run(["make", "-s", "-C", os.path.join(REPO, "oracle"), "ref", f"REF={a.ref}"], check=True)
     fr = FormRunner(a.ref)

@@ -3,6 +3,8 @@
 Expert ids and per-expert counts bit-exact (ids in the reference's list order: mm-topk best-first
 for the softmax layer, dsv4-topk last-first for the DeepSeek-style layer); routing weights within
 1e-5 relative (fp32); outputs normwise max|gpu - ref| / max|ref| <= 2e-2 per token (bf16 MMA).
+At full size every token's routing is compared, and the outputs of at least 256 tokens that
+together touch every expert.
 """
 import os
 
@@ -107,19 +109,49 @@ def full_size(spec, ntok, sample):
     assert np.array_equal(ids, rids), np.argwhere((ids != rids).any(axis=1))[:10]
     assert np.array_equal(counts, np.bincount(rids.reshape(-1), minlength=spec.n_experts))
     assert np.allclose(wts, rwts, rtol=1e-5, atol=1e-7)
-    toks = np.unique(np.concatenate([np.linspace(0, ntok - 1, sample).astype(int), np.argsort(margin)[:2]]))
+    toks = sample_tokens(ids, margin, spec.n_experts, sample)
     sids, swts, sout = O.moe_layer(cfg, w, w["x"], toks)
     assert np.array_equal(sids, ids[toks])
     check_outputs(out[toks], sout)
+    err = max(np.abs(out[t] - sout[i]).max() / np.abs(sout[i]).max() for i, t in enumerate(toks))
+    print(f"{len(toks)} tokens compared, every expert covered; worst per-token normwise error {err:.3e}")
     return margin
 
 
+def sample_tokens(ids, margin, n_experts, sample):
+    """Tokens whose outputs are compared with the oracle: a greedy cover of every routed expert (so
+    every expert's token tiles and the shared-expert tiles they sit beside are exercised), the two
+    lowest-margin tokens, the first and last token, then evenly spaced tokens up to `sample`."""
+    ntok = ids.shape[0]
+    order = np.random.default_rng(0).permutation(ntok)
+    covered = np.zeros(n_experts, dtype=bool)
+    pick = [0, ntok - 1] + list(np.argsort(margin)[:2])
+    for t in pick:
+        covered[ids[t]] = True
+    for t in order:
+        if covered.all():
+            break
+        if not covered[ids[t]].all():
+            covered[ids[t]] = True
+            pick.append(int(t))
+    rest = sample - len(set(pick))
+    if rest > 0:
+        pick += list(np.linspace(0, ntok - 1, rest + 2).astype(int)[1:-1])
+    have = set(int(t) for t in pick)
+    for t in order:
+        if len(have) >= sample:
+            break
+        have.add(int(t))
+    assert covered[np.unique(ids)].all()
+    return np.array(sorted(have), dtype=np.int64)
+
+
 def test_moe_small_full_size():
-    full_size(workloads.MOE_SMALL, workloads.MOE_SMALL_TOKENS, sample=12)
+    full_size(workloads.MOE_SMALL, workloads.MOE_SMALL_TOKENS, sample=256)
 
 
 def test_moe_dsv3_full_size():
-    margin = full_size(workloads.MOE_DSV3, workloads.MOE_DSV3_TOKENS, sample=4)
+    margin = full_size(workloads.MOE_DSV3, workloads.MOE_DSV3_TOKENS, sample=256)
     assert margin.min() >= 0.0
 
 
