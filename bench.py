@@ -268,6 +268,176 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
     return out
 
 
+def full_weights(spec, ntok, have, experts_have):
+    """The weights of every expert on the host: this rank's own experts are reused, the rest are
+    regenerated from their seeded streams (workloads.make_moe draws each expert from its own)."""
+    from coherence_kernel_b200 import workloads
+    missing = [e for e in range(spec.n_experts) if e not in set(experts_have)]
+    if not missing:
+        return have
+    more = workloads.make_moe(spec, ntok, seed=0, experts=missing)
+    mb = spec.matrix_bytes
+    full = dict(have)
+    pos = {e: ("have", i) for i, e in enumerate(experts_have)}
+    pos.update({e: ("more", i) for i, e in enumerate(missing)})
+    for k in ("gate", "up", "down"):
+        arr = np.empty(spec.n_experts * mb, dtype=np.uint8)
+        for e in range(spec.n_experts):
+            src, i = pos[e]
+            arr[e * mb:(e + 1) * mb] = (have if src == "have" else more)[k][i * mb:(i + 1) * mb]
+        full[k] = arr
+    return full
+
+
+def ep_parity(torch, dist, spec, w, experts, ids, wts, out, rank, world, dev, tag="prefill", sample=64,
+              wfull=None):
+    """Parity of an expert-parallel forward with the oracle, outside the timed region: rank 0 gathers
+    every rank's ids / weights / outputs, compares the ids of ALL tokens bit for bit and the weights
+    to 1e-5 with the oracle's routing, and the outputs of `sample` tokens (each rank's two
+    lowest-margin tokens among them) with the oracle's layer at 2e-2 normwise per token.  Every
+    rank learns the verdict.  Returns (summary dict on rank 0 else None, full weights on rank 0)."""
+    from oracle import oracle as O
+    T = ids.shape[0]
+    g_ids = [torch.empty_like(ids) for _ in range(world)]
+    g_wts = [torch.empty_like(wts) for _ in range(world)]
+    g_out = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(g_ids, ids)
+    dist.all_gather(g_wts, wts)
+    dist.all_gather(g_out, out)
+    torch.cuda.synchronize()
+    res = None
+    ok = torch.ones(1, dtype=torch.int32, device=dev)
+    if rank == 0:
+        t0 = time.perf_counter()
+        x = np.ascontiguousarray(w["x"][:T * world])
+        cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
+                        spec.topk_groups, spec.wscale)
+        gi = torch.cat(g_ids).cpu().numpy()
+        gw = torch.cat(g_wts).cpu().numpy()
+        go = torch.cat(g_out).float().cpu().numpy()
+        rids, rwts, margin = O.moe_route(cfg, w["router"], w["bias"], x)
+        ids_exact = bool(np.array_equal(gi, rids))
+        counts_exact = bool(np.array_equal(np.bincount(gi.reshape(-1), minlength=spec.n_experts),
+                                           np.bincount(rids.reshape(-1), minlength=spec.n_experts)))
+        wts_ok = bool(np.allclose(gw, rwts, rtol=1e-5, atol=1e-7))
+        toks = set()
+        for r in range(world):  # each rank's two lowest-margin tokens
+            toks.update((r * T + np.argsort(margin[r * T:(r + 1) * T])[:2]).tolist())
+        toks.update(np.linspace(0, T * world - 1, max(0, sample - len(toks)) + 2).astype(int)[1:-1].tolist())
+        toks = np.array(sorted(toks), dtype=np.int64)
+        if wfull is None:
+            wfull = full_weights(spec, T * world, w, experts)
+        sids, _, sout = O.moe_layer(cfg, wfull, x, toks)
+        errs = np.abs(go[toks] - sout).max(axis=1) / np.abs(sout).max(axis=1)
+        out_ok = bool(np.array_equal(sids, gi[toks])) and bool((errs <= 2e-2).all())
+        res = {"tokens": int(T * world), "ids_exact": ids_exact, "counts_exact": counts_exact,
+               "weights_rtol_1e-5": wts_ok, "outputs_sampled": int(len(toks)),
+               "output_max_err": float(errs.max()), "output_tol": 2e-2, "ok": ids_exact and counts_exact and wts_ok
+               and out_ok, "oracle_s": round(time.perf_counter() - t0, 1), "case": tag}
+        ok.fill_(1 if res["ok"] else 0)
+    dist.broadcast(ok, 0)
+    return res, wfull, bool(ok.item())
+
+
+def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, hbm, wfull=None, steps=20):
+    """Config 5 at N GPUs: data-parallel attention and expert-parallel MoE, the layout a multi-GPU
+    decode server runs.  Every rank holds its own decode batch of b tokens (b = 1, 4, 16, 64) and
+    runs the four dense 7168^2 Q4_K matvecs of the attention stand-in on it, then the DSv3 MoE layer
+    with its experts sharded 256/N per GPU.  The expert load follows Zipf(1.1) through the same
+    seeded selection bias as the single-GPU sweep, calibrated on 4096 tokens routed through this
+    layer.  Step time is the max over ranks of CUDA-event time over `steps` steps; bytes per token
+    are every rank's weight bytes (its dense matrices, the local experts its receive touched and the
+    shared expert) over the N*b tokens of the step."""
+    from coherence_kernel_b200 import ops, synth
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    el = spec.n_experts // world
+    base = w["bias"].copy()
+    ncal = 4096 // world
+    lay = layer_cls(spec, t(w["gate"]), t(w["up"]), t(w["down"]), t(w["s_gate"]), t(w["s_up"]), t(w["s_down"]),
+                    t(w["router"]), t(base), max_tokens=max(ncal, 64))
+    xall = w["x"]
+
+    def slope_for(c):
+        lay.bias.copy_(t(base + zipf_bias(np.random.default_rng(7), spec, c=c)))
+        xr = t(xall[rank * ncal:(rank + 1) * ncal].view(np.int16))
+        lay(xr)
+        cnt = lay.counts.clone()
+        dist.all_reduce(cnt)
+        cnt = np.sort(cnt.cpu().numpy())[::-1].astype(np.float64)
+        r = np.arange(1, cnt.size + 1, dtype=np.float64)[cnt >= 8]
+        cnt = cnt[cnt >= 8]
+        return float(np.polyfit(np.log(r), np.log(cnt), 1)[0])
+    lo, hi = 0.0, None
+    for c in np.arange(0.125, 6.01, 0.125):
+        if slope_for(float(c)) <= -1.1:
+            hi = float(c)
+            break
+        lo = float(c)
+    hi = lo if hi is None else hi
+    for _ in range(8):
+        mid = 0.5 * (lo + hi)
+        if slope_for(mid) > -1.1:
+            lo = mid
+        else:
+            hi = mid
+    zipf_c = 0.5 * (lo + hi)
+    zipf_slope = slope_for(zipf_c)
+    R = C = 7168
+    q4 = [t(synth.make_q4k(np.random.default_rng([2, i]), R * C)) for i in range(16)]
+    xv = t(np.random.default_rng(3).standard_normal(C).astype(np.float32))
+    yv = torch.empty(R, device=dev)
+    dense_b = R * C // 256 * 144
+    sweep = {}
+    parity = None
+    for bsz in (1, 4, 16, 64):
+        # rank r's batch: tokens [r*b, (r+1)*b) of the seeded stream
+        xb = t(xall[rank * bsz:(rank + 1) * bsz].view(np.int16))
+        o = torch.empty((bsz, spec.hidden), dtype=torch.bfloat16, device=dev)
+
+        def step(k):
+            for j in range(4):
+                ops.q4k_matvec(q4[(4 * k + j) % 16], xv, R, C, out=yv)
+            return lay(xb, out=o)
+        for k in range(3):
+            step(k)
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for k in range(steps):
+            step(k)
+        b.record()
+        torch.cuda.synchronize()
+        us = torch.tensor([a.elapsed_time(b) * 1e3 / steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        out_b, ids_b, wts_b, _ = step(0)
+        used = torch.tensor([float(int((lay.counts2 > 0).sum().item()) if lay.last_recv_pairs else 0)],
+                            dtype=torch.float64, device=dev)
+        mine = float(4 * dense_b + (used.item() + spec.n_shared) * 3 * spec.matrix_bytes)
+        tot = torch.tensor([mine], dtype=torch.float64, device=dev)
+        dist.all_reduce(tot)
+        dist.all_reduce(used)
+        us = float(us)
+        sweep[f"b{bsz}"] = {"tokens_per_rank": bsz, "tokens_per_step": bsz * world, "us_per_step": round(us, 1),
+                            "experts_touched": int(used.item()), "bytes_per_token": int(tot.item() / (bsz * world)),
+                            "roofline": _roof("hbm", tot.item() / world / us / 1e3, hbm, "GB/s"),
+                            "timing": "eager steps, CUDA events, max over ranks"}
+        if bsz == 16:
+            # parity of the skewed decode batch (every token's routing, a sample of outputs)
+            wb = dict(w)
+            wb["bias"] = base + zipf_bias(np.random.default_rng(7), spec, c=zipf_c)
+            parity, wfull, okp = ep_parity(torch, dist, spec, wb, experts, ids_b, wts_b, out_b, rank, world, dev,
+                                           tag=f"decode b{bsz} per rank, Zipf-skewed", sample=32,
+                                           wfull=None if wfull is None else dict(wfull, bias=wb["bias"]))
+            if not okp:
+                raise SystemExit("decode sweep parity failed")
+    del lay, q4
+    torch.cuda.synchronize()
+    return {"steps": sweep, "layout": "data-parallel attention stand-in, expert-parallel MoE",
+            "zipf": {"c": round(zipf_c, 3), "measured_slope": round(zipf_slope, 3), "tokens": ncal * world},
+            "parity": parity}
+
+
 def cpu_baseline(spec, w, target_s=12.0):
     """The oracle (fp64 C restatement of the reference's Form recipes) on a bounded sample of whole
     tokens of the layer, one token per host thread at a time: one token per thread first to size
@@ -403,13 +573,13 @@ def main():
         return rec, mark
 
     def step(record):
+        rec, mark = marks_factory()
         if world == 1:
-            rec, mark = marks_factory()
             layer.forward_steps(x, out, ids, wts, counts, marks=mark if record else None)
-            if record:
-                evs.append(rec)
         else:
-            layer.forward(x, out=out)
+            layer.forward(x, out=out, marks=mark if record else None)
+        if record:
+            evs.append(rec)
 
     for _ in range(args.warmup):
         step(False)
@@ -447,19 +617,47 @@ def main():
     weight_bytes = (spec.n_experts + spec.n_shared) * 3 * spec.matrix_bytes
     A = T * spec.nsel
     roof = None
+    phases = None
+    # the timed region is well under a second, so the burst bf16 peak is the denominator
     if world == 1 and evs:
         gu = [r["permute"].elapsed_time(r["gate_up"]) for r in evs]
         dn = [r["gate_up"].elapsed_time(r["down"]) for r in evs]
         gu_ms = sum(gu) / len(gu)
         flops_gu = 2.0 * (A + spec.n_shared * T) * 2 * spec.inter * spec.hidden
         ach = flops_gu / (gu_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_sust, "unit": "TFLOP/s",
-                "frac": round(ach / tc_sust, 4), "traffic": int(GATEUP_DRAM_BYTES_PER_ROW * (A + spec.n_shared * T)),
-                "kernel": "k_gemm_q4k<1> (grouped gate/up GEMM + SwiGLU)", "peak_source": f"{peak_src} sustained",
+        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_burst, "unit": "TFLOP/s",
+                "frac": round(ach / tc_burst, 4), "traffic": int(GATEUP_DRAM_BYTES_PER_ROW * (A + spec.n_shared * T)),
+                "kernel": "k_gemm_q4k<1> (grouped gate/up GEMM + SwiGLU)", "peak_source": f"{peak_src} burst",
+                "frac_of_sustained": round(ach / tc_sust, 4),
                 "kernel_ms": round(gu_ms, 4), "down_ms": round(sum(dn) / len(dn), 4),
                 "step_split_ms": {k: round(sum(r[b].elapsed_time(r[k]) for r in evs) / len(evs), 4)
                                   for b, k in (("start", "route"), ("route", "permute"), ("permute", "gate_up"),
                                                ("gate_up", "down"), ("down", "combine"))}}
+    elif world > 1 and evs:
+        # per-phase device time on the layer's stream, averaged over the timed steps, max over ranks
+        # (the shared expert runs beside them on a side stream)
+        names = [("start", "route"), ("route", "permute"), ("permute", "shared"), ("shared", "dispatch"),
+                 ("dispatch", "regroup"), ("regroup", "gate_up"), ("gate_up", "down"), ("down", "experts"),
+                 ("experts", "return"), ("return", "combine")]
+        vec = torch.tensor([sum(r[b].elapsed_time(r[k]) for r in evs) / len(evs) for b, k in names],
+                           dtype=torch.float64, device=dev)
+        mine = vec.clone()
+        dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+        label = {"permute": "plan", "shared": "shared_launch", "experts": "pair_order"}
+        phases = {label.get(k, k): round(float(v), 4) for (b, k), v in zip(names, vec.tolist())}
+        # the dominant kernel: the receiver's grouped gate/up GEMM over the (row, slot) pairs it received
+        pairs = torch.tensor([float(layer.last_recv_pairs)], dtype=torch.float64, device=dev)
+        gu_ms = float(mine[5])
+        ach_local = 2.0 * float(pairs) * 2 * spec.inter * spec.hidden / (gu_ms / 1e3) / 1e12
+        fr = torch.tensor([ach_local / tc_burst], dtype=torch.float64, device=dev)
+        frmin = fr.clone()
+        dist.all_reduce(frmin, op=dist.ReduceOp.MIN)
+        roof = {"bound": "tensor", "achieved": round(ach_local, 1), "peak": tc_burst, "unit": "TFLOP/s",
+                "frac": round(ach_local / tc_burst, 4), "frac_min_over_ranks": round(float(frmin), 4),
+                "traffic": int(GATEUP_DRAM_BYTES_PER_ROW * float(pairs)),
+                "kernel": "k_gemm_q4k<1> (receiver's grouped gate/up GEMM + SwiGLU), rank 0",
+                "peak_source": f"{peak_src} burst", "kernel_ms": round(gu_ms, 4),
+                "recv_pairs": int(float(pairs))}
 
     # end to end through the public call: every step's tokens copied in from pinned host memory and
     # its output copied back, pipelined as a server would run it -- step i+1's upload (one copy
@@ -527,10 +725,22 @@ def main():
                          "over the ranks, time the max over ranks"}
 
     subs = None
+    parity = None
+    parity_ok = True
     if world == 1 and args.shard == 1 and not args.no_sub:
         del layer, wg, wu, wd
         torch.cuda.empty_cache()
         subs = sub_benchmarks(torch, dev, hbm, tc_burst)
+    elif world > 1 and args.shard == 1:
+        # parity of the expert-parallel layer with the oracle, outside the timed region
+        o_p, i_p, w_p, _ = layer(x)
+        layer.check()
+        parity, wfull, parity_ok = ep_parity(torch, dist, spec, w, experts, i_p, w_p, o_p, rank, world, dev)
+        if parity_ok and not args.no_sub:
+            del layer, wg, wu, wd, o_p
+            torch.cuda.empty_cache()
+            subs = {"decode_sweep_ep": decode_sweep_ep(torch, dist, ExpertParallelMoE, spec, w, experts, rank,
+                                                       world, dev, hbm, wfull)}
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -552,12 +762,15 @@ def main():
                 "algorithmic_tflops": round(T_all * spec.flops_per_token() / (ms_step / 1e3) / 1e12, 1),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "router_exact_tokens": flagged,
+                "phase_ms": phases, "parity": parity,
                 "sub_benchmarks": subs,
                 "gpu_launches": launches_per_step * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if not parity_ok:
+        raise SystemExit("expert-parallel output differs from the oracle (see the parity object)")
 
 
 if __name__ == "__main__":

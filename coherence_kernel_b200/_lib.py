@@ -64,6 +64,7 @@ SIGNATURES = {
                                           _u32, _u32, _u32, _i32, _u32, _p, _p]),
     "ck_moe_combine": (_i32, [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _i32, _p, _p, _p]),
     "ck_token_tiles": (_i32, [_p, _p, _u32, _p]),
+    "ck_token_tiles_n": (_i32, [_p, _p, _u32, _u32, _p]),
     "ck_gather_rows": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_ep_dispatch_plan": (_i32, [_p, _p, _u32, _u32, _u32, _u32, _p, _p, _p, _p, _p, _p]),
     "ck_wait_selftest": (_i32, [_u64, _p, _p, _p]),

@@ -401,6 +401,9 @@ int ck_moe_combine(const void *y, const int32_t *ids, const float *wts, const in
 int ck_token_tiles(void *tiles, int32_t *ntiles, uint32_t ntok, void *s) {
     return fail(ck::launch_single_tiles((int4 *)tiles, ntiles, ntok, ck::GEMM_TILE_TOKENS, S(s)), "ck_token_tiles");
 }
+int ck_token_tiles_n(void *tiles, int32_t *ntiles, uint32_t ntok, uint32_t tile_tokens, void *s) {
+    return fail(ck::launch_single_tiles((int4 *)tiles, ntiles, ntok, tile_tokens, S(s)), "ck_token_tiles_n");
+}
 
 int ck_ep_dispatch_plan(const int32_t *ids, const float *wts, uint32_t ntok, uint32_t nsel, uint32_t n_experts,
                         uint32_t world, int32_t *counts, int64_t *sizes, int32_t *send_tok, int32_t *meta,

@@ -219,7 +219,7 @@ __global__ void k_single_tiles(int4 *__restrict__ tiles, int32_t *__restrict__ n
     if (threadIdx.x == 0) *ntiles = nt;
 }
 int launch_single_tiles(int4 *tiles, int32_t *ntiles, uint32_t ntok, uint32_t bn, cudaStream_t s) {
-    if (!tiles || !ntiles || bn == 0 || bn % 16) return CK_ERR_ARG;
+    if (!tiles || !ntiles || bn == 0 || (bn > 8 && bn % 16) || bn > GEMM_TILE_TOKENS) return CK_ERR_ARG;
     k_single_tiles<<<1, 256, 0, s>>>(tiles, ntiles, ntok, bn);
     return (int)cudaGetLastError();
 }

@@ -268,7 +268,7 @@ class ExpertParallelMoE:
         self.ret_pos = torch.empty(A, dtype=torch.int32, device=dev)
         self.y = torch.empty((A + sp.n_shared * T, H), dtype=torch.bfloat16, device=dev)
         self.h_sh = torch.empty((max(1, sp.n_shared) * T, I), dtype=torch.bfloat16, device=dev)
-        self.sh_tiles = torch.empty((T // 16 + 2, 4), dtype=torch.int32, device=dev)
+        self.sh_tiles = torch.empty((T // FEW_TOKENS + 2, 4), dtype=torch.int32, device=dev)
         self.sh_ntiles = torch.empty(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.counts = torch.empty(E, dtype=torch.int32, device=dev)
@@ -327,19 +327,24 @@ class ExpertParallelMoE:
             self.side.wait_stream(main)
             sst = ctypes.c_void_p(self.side.cuda_stream)
             mb = sp.matrix_bytes
-            _lib.check(L.ck_token_tiles(_ptr(self.sh_tiles), _ptr(self.sh_ntiles), T, sst), "ck_token_tiles")
+            # a decode-sized batch cuts the shared expert's tokens into tiles of at most FEW_TOKENS,
+            # which stream the weights through the few-token grouped matvec
+            sh_bound = min(T, FEW_TOKENS) if T <= DECODE_TOKENS else 0
+            _lib.check(L.ck_token_tiles_n(_ptr(self.sh_tiles), _ptr(self.sh_ntiles), T,
+                                          FEW_TOKENS if sh_bound else 192, sst), "ck_token_tiles_n")
             for s in range(sp.n_shared):
                 hs = self.h_sh[s * T:(s + 1) * T]
                 ys = self.y[A + s * T:A + (s + 1) * T]
-                _lib.check(L.ck_moe_expert_gemm(1, ctypes.c_void_p(self.s[0].data_ptr() + s * mb),
-                                                 ctypes.c_void_p(self.s[1].data_ptr() + s * mb), None, None, 0, 1, 0,
-                                                 _ptr(x), T, _ptr(hs), T, None, _ptr(self.sh_tiles),
-                                                 _ptr(self.sh_ntiles), self.sh_tiles.shape[0], I, H, 0, _ptr(self.err),
-                                                 sst), "shared gate/up")
-                _lib.check(L.ck_moe_expert_gemm(0, ctypes.c_void_p(self.s[2].data_ptr() + s * mb), None, None, None, 0,
-                                                 1, 0, _ptr(hs), T, _ptr(ys), T, None, _ptr(self.sh_tiles),
-                                                 _ptr(self.sh_ntiles), self.sh_tiles.shape[0], H, I, 0, _ptr(self.err),
-                                                 sst), "shared down")
+                _lib.check(L.ck_moe_expert_gemm_bounded(1, ctypes.c_void_p(self.s[0].data_ptr() + s * mb),
+                                                         ctypes.c_void_p(self.s[1].data_ptr() + s * mb), None, None, 0,
+                                                         1, 0, _ptr(x), T, _ptr(hs), T, None, _ptr(self.sh_tiles),
+                                                         _ptr(self.sh_ntiles), self.sh_tiles.shape[0], I, H, 0,
+                                                         sh_bound, _ptr(self.err), sst), "shared gate/up")
+                _lib.check(L.ck_moe_expert_gemm_bounded(0, ctypes.c_void_p(self.s[2].data_ptr() + s * mb), None, None,
+                                                         None, 0, 1, 0, _ptr(hs), T, _ptr(ys), T, None,
+                                                         _ptr(self.sh_tiles), _ptr(self.sh_ntiles),
+                                                         self.sh_tiles.shape[0], H, I, 0, sh_bound, _ptr(self.err),
+                                                         sst), "shared down")
             side_done = torch.cuda.Event()
             side_done.record(self.side)
         mark("shared")
@@ -358,24 +363,35 @@ class ExpertParallelMoE:
                                input_split_sizes=srow_l, group=self.group)
         mark("dispatch")
         # regroup the received (row, slot) pairs by local expert (a stable counting sort that skips
-        # the -1 slots), grouped GEMMs, then every pair's row back in (row, slot) order
+        # the -1 slots), grouped GEMMs, then every pair's row back in (row, slot) order.  A
+        # decode-sized receive (at most DECODE_TOKENS rows) is cut into tiles of at most FEW_TOKENS
+        # by the permute, and the expert weights stream through the few-token grouped matvec.
         if P:
+            bound = min(R, FEW_TOKENS) if R <= DECODE_TOKENS else 0
             rme = self.recv_meta[:R, :K].contiguous()
             rmw = self.recv_meta[:R, K:].contiguous().view(torch.float32)
             _lib.check(L.ck_moe_permute(_ptr(rme), _ptr(rmw), _ptr(self.recv_x), R, K, self.el, 0, H,
                                         int(sp.mode == 4), _ptr(self.xp2), _ptr(self.row_w2), _ptr(self.pair_pos2),
                                         _ptr(self.counts2), _ptr(self.tiles2), _ptr(self.ntiles2),
                                         _ptr(self.perm_ws2), st), "regroup")
-            _lib.check(L.ck_moe_expert_gemm(1, _ptr(self.w[0]), _ptr(self.w[1]), None, None, sp.matrix_bytes, self.el,
-                                             0, _ptr(self.xp2), P, _ptr(self.h2), P, _ptr(self.row_w2),
-                                             _ptr(self.tiles2), _ptr(self.ntiles2), self.mt2, I, H, 0, _ptr(self.err),
-                                             st), "expert gate/up")
-            _lib.check(L.ck_moe_expert_gemm(0, _ptr(self.w[2]), None, None, None, sp.matrix_bytes, self.el,
-                                             0, _ptr(self.h2), P, _ptr(self.y2), P, None, _ptr(self.tiles2),
-                                             _ptr(self.ntiles2), self.mt2, H, I, 1, _ptr(self.err), st), "expert down")
+            mark("regroup")
+            _lib.check(L.ck_moe_expert_gemm_bounded(1, _ptr(self.w[0]), _ptr(self.w[1]), None, None, sp.matrix_bytes,
+                                                     self.el, 0, _ptr(self.xp2), P, _ptr(self.h2), P,
+                                                     _ptr(self.row_w2), _ptr(self.tiles2), _ptr(self.ntiles2),
+                                                     self.mt2, I, H, 0, bound, _ptr(self.err), st), "expert gate/up")
+            mark("gate_up")
+            _lib.check(L.ck_moe_expert_gemm_bounded(0, _ptr(self.w[2]), None, None, None, sp.matrix_bytes, self.el,
+                                                     0, _ptr(self.h2), P, _ptr(self.y2), P, None, _ptr(self.tiles2),
+                                                     _ptr(self.ntiles2), self.mt2, H, I, 1, bound, _ptr(self.err), st),
+                       "expert down")
+            mark("down")
             pp = self.pair_pos2[:R * K]
             vidx = pp[torch.nonzero_static(pp >= 0, size=P).squeeze(1)]
             _lib.check(L.ck_gather_rows(_ptr(self.y2), _ptr(vidx), _ptr(self.y_recv), P, H * 2, st), "pair order")
+        else:
+            mark("regroup")
+            mark("gate_up")
+            mark("down")
         mark("experts")
         dist.all_to_all_single(self.y[:A], self.y_recv[:P], output_split_sizes=spair_l, input_split_sizes=rpair_l,
                                group=self.group)

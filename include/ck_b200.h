@@ -167,6 +167,10 @@ int ck_moe_combine(const void *y_bf16_dev, const int32_t *ids_dev, const float *
 /* the token-tile table of one matrix over ntok rows (group 0, rows in order), at most
  * ntok/16 + 2 entries of 4 int32 */
 int ck_token_tiles(void *tiles_dev, int32_t *ntiles_dev, uint32_t ntok, void *stream);
+/* the same table with tiles of at most tile_tokens tokens (1..8, or a multiple of 16 up to 192):
+ * ceil(ntok / tile_tokens) entries.  Tiles of at most CK_MOE_FEW_TOKENS feed the few-token grouped
+ * matvec (ck_moe_expert_gemm_bounded with that bound). */
+int ck_token_tiles_n(void *tiles_dev, int32_t *ntiles_dev, uint32_t ntok, uint32_t tile_tokens, void *stream);
 int ck_gather_rows(const void *src_dev, const int32_t *idx_dev, void *dst_dev, uint32_t nrows, uint32_t row_bytes,
                    void *stream);
 /* Expert-parallel dispatch plan (no counterpart in the reference, whose MoE runs on one device).

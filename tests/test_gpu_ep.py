@@ -1,8 +1,9 @@
-"""Expert parallelism over NCCL on two GPUs: the expert-parallel layer's output, ids and weights
-equal the single-GPU layer's bit for bit (each token row is computed by the same kernels in the
-same K order whichever tile it lands in, and the combine keeps the reference's order).
+"""Expert parallelism over NCCL on two and four GPUs: the expert-parallel layer's output, ids and
+weights equal the single-GPU layer's bit for bit (each token row is computed by the same kernels in
+the same K order whichever tile it lands in, and the combine keeps the reference's order).  The
+decode-sized cases (64 tokens in all) take the few-token grouped matvec on both sides.
 
-Runs as two spawned ranks when the box has at least two GPUs; skipped otherwise.
+Runs as spawned ranks when the box has enough GPUs; skipped otherwise.
 """
 import os
 import socket
@@ -18,7 +19,6 @@ SPECS = {
                  wscale=2.5),
     "softmax": dict(hidden=1024, inter=768, n_experts=8, n_shared=2, nsel=3, mode=3),
 }
-NTOK = 512
 
 
 def _free_port():
@@ -29,7 +29,7 @@ def _free_port():
     return port
 
 
-def _rank(rank, world, port, name, q):
+def _rank(rank, world, port, name, NTOK, q):
     import datetime
 
     import torch.distributed as dist
@@ -77,14 +77,16 @@ def _rank(rank, world, port, name, q):
         raise
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("name", sorted(SPECS))
-def test_expert_parallel_matches_single_gpu(name):
+@pytest.mark.parametrize("name,world,ntok", [("dsv4", 2, 512), ("softmax", 2, 512), ("dsv4", 4, 512),
+                                             ("softmax", 4, 768), ("dsv4", 2, 64), ("dsv4", 4, 64)])
+def test_expert_parallel_matches_single_gpu(name, world, ntok):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, name, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, name, ntok, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
