@@ -93,6 +93,30 @@ def make_q4k(rng: np.random.Generator, n_weights: int, chunk_blocks: int = 1 << 
     return out.reshape(-1)
 
 
+Q6K_BLOCK_BYTES = 210
+
+
+def q6k_bytes(n_weights: int) -> int:
+    assert n_weights % Q4K_BLOCK_WEIGHTS == 0, "a Q6_K tensor is a whole number of 256-weight superblocks"
+    return n_weights // Q4K_BLOCK_WEIGHTS * Q6K_BLOCK_BYTES
+
+
+def make_q6k(rng: np.random.Generator, n_weights: int, chunk_blocks: int = 1 << 20) -> np.ndarray:
+    """``n_weights`` Q6_K weights (flat) as a uint8 array of 210-byte superblocks: ql[128] and
+    qh[64] uniform (6-bit codes uniform over 0..63), 16 signed 8-bit scales uniform over -128..127,
+    fp16 d = |N(0,1)| * 0.0005."""
+    nb = n_weights // Q4K_BLOCK_WEIGHTS
+    assert nb * Q4K_BLOCK_WEIGHTS == n_weights
+    out = np.empty((nb, Q6K_BLOCK_BYTES), dtype=np.uint8)
+    for b0 in range(0, nb, chunk_blocks):
+        b1 = min(nb, b0 + chunk_blocks)
+        n = b1 - b0
+        out[b0:b1, 0:208] = rng.integers(0, 256, size=(n, 208), dtype=np.uint8)
+        d = (np.abs(rng.standard_normal(n)) * 0.0005).astype(np.float16)
+        out[b0:b1, 208:210] = d.view(np.uint8).reshape(n, 2)
+    return out.reshape(-1)
+
+
 def make_bf16(rng: np.random.Generator, shape) -> np.ndarray:
     """N(0,1) activations as bf16 bit patterns (uint16)."""
     return f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32))

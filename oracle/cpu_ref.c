@@ -99,6 +99,37 @@ void ckr_q4k_dequant(const uint8_t *qb, int64_t off, int64_t n, double *w) {
     }
 }
 
+/* ---------------------------------------------------------------- Q6_K
+ * form/form-stdlib/q6k-msl.fk:62-81 (q6m-flat-at) over q6k-dequant.fk:29-61's decomposition:
+ * block = idx/256 at 210-byte stride; ql[128] @+0, qh[64] @+128, scales[16] (signed) @+192,
+ * d f16 @+208.  i = idx mod 256, h = i/128, wi = i mod 128, l = wi mod 32, g = wi/32, is = l/16;
+ * nib = low nibble of ql[64h + l + 32 (g mod 2)] for g < 2 else the high one; hi = (qh[32h + l]
+ * / 4^g) mod 4; q = nib + 16 hi - 32; sc = s8(scales[8h + is + 2g]); w = (d * sc) * q. */
+uint32_t ckr_q6k_codes(const uint8_t *src, int64_t base, int64_t idx) {
+    const uint8_t *b = src + base + (idx / 256) * 210;
+    int i = (int)(idx % 256);
+    int h = i / 128, wi = i % 128, l = wi % 32, g = wi / 32, is = l / 16;
+    int qlb = b[64 * h + l + 32 * (g % 2)];
+    int nib = g / 2 == 0 ? qlb % 16 : qlb / 16;
+    static const int pow4[4] = {1, 4, 16, 64};
+    int hi = (b[128 + 32 * h + l] / pow4[g]) % 4;
+    int scb = b[192 + 8 * h + is + 2 * g];
+    /* the 6-bit code q + 32 (0..63) in bits 0..7 and the scale byte in bits 8..15 */
+    return (uint32_t)(nib + 16 * hi) | ((uint32_t)scb << 8);
+}
+double ckr_q6k_at(const uint8_t *src, int64_t base, int64_t idx) {
+    const uint8_t *b = src + base + (idx / 256) * 210;
+    uint32_t codes = ckr_q6k_codes(src, base, idx);
+    int q = (int)(codes & 0xFF) - 32;
+    int sc = (int)((codes >> 8) & 0xFF);
+    if (sc >= 128) sc -= 256;
+    double d = ckr_f16((uint32_t)b[208] + 256u * (uint32_t)b[209]);
+    return (d * (double)sc) * (double)q;
+}
+void ckr_q6k_dequant(const uint8_t *qb, int64_t off, int64_t n, double *w) {
+    for (int64_t i = 0; i < n; i++) w[i] = ckr_q6k_at(qb, 0, off + i);
+}
+
 /* ---------------------------------------------------------------- the right fold
  * form/form-stdlib/transformer-block.fk:25-26 tb-dot: a0*b0 + (a1*b1 + (... + (an*bn + 0.0))). */
 double ckr_dot(const double *a, const double *b, int64_t n) {
@@ -128,6 +159,15 @@ void ckr_q80_matvec(const uint8_t *qb, const double *x, double *y, int64_t rows,
     double *w = (double *)malloc(sizeof(double) * (size_t)cols);
     for (int64_t r = 0; r < rows; r++) {
         ckr_q80_dequant(qb, r * cols, cols, w);
+        y[r] = ckr_dot(w, x, cols);
+    }
+    free(w);
+}
+
+void ckr_q6k_matvec(const uint8_t *qb, const double *x, double *y, int64_t rows, int64_t cols) {
+    double *w = (double *)malloc(sizeof(double) * (size_t)cols);
+    for (int64_t r = 0; r < rows; r++) {
+        ckr_q6k_dequant(qb, r * cols, cols, w);
         y[r] = ckr_dot(w, x, cols);
     }
     free(w);

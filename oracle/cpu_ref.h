@@ -20,6 +20,13 @@ double ckr_bf16(uint32_t bits);
 
 /* form/form-stdlib/q8-0-msl.fk:53-72 (q80-flat-at): weight at a flat index, 34-byte blocks */
 double ckr_q80_at(const uint8_t *src, int64_t base, int64_t idx);
+/* form/form-stdlib/q6k-msl.fk:62-81 (q6m-flat-at): weight at a flat index, 210-byte superblocks;
+ * ckr_q6k_codes: the 6-bit code q + 32 (bits 0..7) and the raw scale byte (bits 8..15);
+ * ckr_q6k_dequant: the flat range [off, off+n); ckr_q6k_matvec: the right fold per row. */
+double ckr_q6k_at(const uint8_t *src, int64_t base, int64_t idx);
+uint32_t ckr_q6k_codes(const uint8_t *src, int64_t base, int64_t idx);
+void ckr_q6k_dequant(const uint8_t *qb, int64_t off, int64_t n, double *w);
+void ckr_q6k_matvec(const uint8_t *qb, const double *x, double *y, int64_t rows, int64_t cols);
 /* form/form-stdlib/q4k-msl.fk:55-86 (q4m-flat-at): weight at a flat index, 144-byte superblocks */
 double ckr_q4k_at(const uint8_t *src, int64_t base, int64_t idx);
 /* The decoded integer fields of a Q4_K weight (q4k-dequant.fk:19-43): 6-bit scale, 6-bit min and

@@ -40,17 +40,18 @@ def lib():
         L.ckr_f16.argtypes = [ctypes.c_uint32]
         L.ckr_bf16.restype = ctypes.c_double
         L.ckr_bf16.argtypes = [ctypes.c_uint32]
-        for n in ("ckr_q80_at", "ckr_q4k_at"):
+        for n in ("ckr_q80_at", "ckr_q4k_at", "ckr_q6k_at"):
             getattr(L, n).restype = ctypes.c_double
             getattr(L, n).argtypes = [_p, _c_i64, _c_i64]
-        L.ckr_q4k_codes.restype = ctypes.c_uint32
-        L.ckr_q4k_codes.argtypes = [_p, _c_i64, _c_i64]
-        for n in ("ckr_q80_dequant", "ckr_q4k_dequant"):
+        for n in ("ckr_q4k_codes", "ckr_q6k_codes"):
+            getattr(L, n).restype = ctypes.c_uint32
+            getattr(L, n).argtypes = [_p, _c_i64, _c_i64]
+        for n in ("ckr_q80_dequant", "ckr_q4k_dequant", "ckr_q6k_dequant"):
             getattr(L, n).restype = None
             getattr(L, n).argtypes = [_p, _c_i64, _c_i64, _p]
         L.ckr_dot.restype = ctypes.c_double
         L.ckr_dot.argtypes = [_p, _p, _c_i64]
-        for n in ("ckr_q80_matvec", "ckr_q4k_matvec"):
+        for n in ("ckr_q80_matvec", "ckr_q4k_matvec", "ckr_q6k_matvec"):
             getattr(L, n).restype = None
             getattr(L, n).argtypes = [_p, _p, _p, _c_i64, _c_i64]
         L.ckr_q4k_matmul.restype = None
@@ -97,6 +98,26 @@ def q4k_at(qb: np.ndarray, idx: int) -> float:
 def q4k_codes(qb: np.ndarray, idx: int):
     c = lib().ckr_q4k_codes(_ptr(qb), 0, idx)
     return c & 0xFF, (c >> 8) & 0xFF, c >> 16
+
+
+def q6k_dequant(qb: np.ndarray, off: int, n: int) -> np.ndarray:
+    w = np.empty(n, dtype=np.float64)
+    lib().ckr_q6k_dequant(_ptr(qb), off, n, _ptr(w))
+    return w
+
+
+def q6k_codes(qb: np.ndarray, idx: int):
+    """(q + 32, signed scale) of the weight at a flat index"""
+    c = lib().ckr_q6k_codes(_ptr(qb), 0, idx)
+    sc = (c >> 8) & 0xFF
+    return c & 0xFF, sc - 256 if sc >= 128 else sc
+
+
+def q6k_matvec(qb, x, rows, cols):
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    y = np.empty(rows, dtype=np.float64)
+    lib().ckr_q6k_matvec(_ptr(qb), _ptr(x), _ptr(y), rows, cols)
+    return y
 
 
 def q80_matvec(qb, x, rows, cols):

@@ -106,6 +106,62 @@ def golden_ref_fixtures(fr: FormRunner, ref: str):
     print("reference fixtures decoded:", len(np.array(rows4).reshape(-1)), "+", len(np.array(rows8).reshape(-1)))
 
 
+def q6k_band_vectors(ref: str):
+    """The real llama3.2:3b Q6_K superblock of the reference's q6k-dequant-band.fk (d, QL, QH,
+    SCALES given inline there) as 210 raw bytes, and the band's twelve (index, round(w * 1e6)) pins."""
+    import re
+    text = open(os.path.join(ref, "form", "form-stdlib", "tests", "q6k-dequant-band.fk")).read()
+    d = float(re.search(r"\(let d ([0-9.e-]+)\)", text).group(1))
+    lists = {}
+    for name in ("SCALES", "QL", "QH"):
+        body = re.search(r"\(let " + name + r" \(list([^)]*)\)\)", text).group(1)
+        lists[name] = [int(v) for v in body.split()]
+    assert [len(lists[k]) for k in ("QL", "QH", "SCALES")] == [128, 64, 16]
+    dh = np.array([d], dtype=np.float16)
+    assert float(dh[0]) == d, "d is an f16 value"
+    sb = np.concatenate([np.array(lists["QL"], dtype=np.uint8), np.array(lists["QH"], dtype=np.uint8),
+                         np.array(lists["SCALES"], dtype=np.uint8), dh.view(np.uint8)])
+    pins = [(int(i), int(v)) for i, v in
+            re.findall(r"\(q6k-at (\d+) +d QL QH SCALES\) 1000000\.0\)\) (-?\d+)\)", text)]
+    last = re.search(r"\(nth full 255\) 1000000\.0\)\) (-?\d+)\)", text)
+    pins.append((255, int(last.group(1))))
+    assert len(pins) == 12
+    return sb, pins
+
+
+def golden_q6k(fr: FormRunner, ref: str):
+    """Q6_K through the reference's own q6m-flat-at and tb-matvec: a seeded tensor whose rows
+    straddle superblocks (384 columns), the reference's two-superblock fixture, and the band's real
+    superblock, whose twelve pins are kept beside the fp64 values fkwu decodes from it."""
+    out = {}
+
+    def run(q, rows, cols, x):
+        fr.put("meta6.bin", np.array([rows, cols], dtype=np.uint32))
+        fr.put("q6.bin", q)
+        fr.put("x6.bin", x)
+        w, y = fr.run("ck_q6k.fk")
+        return np.array(w, dtype=np.float64).reshape(-1), np.array(y, dtype=np.float64)
+
+    rng = np.random.default_rng(6)
+    r6, c6 = 10, 384
+    q6 = synth.make_q6k(rng, r6 * c6)
+    x6 = rng.standard_normal(c6).astype(np.float32)
+    out["q6"], out["x6"], out["dims"] = q6, x6, np.array([r6, c6])
+    out["w6"], out["y6"] = run(q6, r6, c6, x6)
+    fx = os.path.join(ref, "form", "form-stdlib", "tests", "fixtures", "q6k-two-superblocks.bin")
+    data = open(fx, "rb").read()
+    assert len(data) == 420
+    print("q6k-two-superblocks.bin", hashlib.sha256(data).hexdigest())
+    out["fix"] = np.frombuffer(data, dtype=np.uint8)
+    out["fix_w"], _ = run(out["fix"], 2, 256, np.ones(256, dtype=np.float32))
+    sb, pins = q6k_band_vectors(ref)
+    out["band_sb"] = sb
+    out["band_pins"] = np.array(pins, dtype=np.int64)
+    out["band_w"], _ = run(sb, 1, 256, np.ones(256, dtype=np.float32))
+    np.savez_compressed(os.path.join(HERE, "q6k_golden.npz"), **out)
+    print("q6k golden:", len(out["y6"]), "rows,", len(out["fix_w"]), "fixture weights, 12 band pins")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("CK_REFERENCE"))
@@ -117,7 +173,7 @@ def main():
         subprocess.run(["make", "-s", "-C", os.path.join(REPO, "oracle"), "ref", f"REF={a.ref}"], check=True)
     fr = FormRunner(a.ref)
     try:
-        todo = a.only.split(",") if a.only else ["quant", "fixtures", "route", "moe"]
+        todo = a.only.split(",") if a.only else ["quant", "fixtures", "route", "moe", "q6k"]
         if "quant" in todo:
             golden_quant(fr)
         if "fixtures" in todo:
@@ -126,6 +182,8 @@ def main():
             golden_route(fr)
         if "moe" in todo:
             golden_moe(fr)
+        if "q6k" in todo:
+            golden_q6k(fr, a.ref)
     finally:
         fr.close()
 

@@ -51,6 +51,26 @@ def test_q4k_dequant_band_pins():
         assert round(w[i] * 1e6) == v, (i, w[i])
 
 
+def test_q6k_golden_bit_exact():
+    # fkwu's q6m-flat-at / tb-matvec (form-stdlib/q6k-msl.fk:62-81, transformer-block.fk:25-28) on a
+    # seeded tensor whose rows straddle superblocks, and on the reference's two-superblock fixture
+    g = np.load(os.path.join(G, "q6k_golden.npz"))
+    r6, c6 = (int(v) for v in g["dims"])
+    assert np.array_equal(O.q6k_dequant(g["q6"], 0, r6 * c6), g["w6"])
+    assert np.array_equal(O.q6k_matvec(g["q6"], g["x6"].astype(np.float64), r6, c6), g["y6"])
+    assert np.array_equal(O.q6k_dequant(g["fix"], 0, 512), g["fix_w"])
+
+
+def test_q6k_dequant_band_pins():
+    # form-stdlib/tests/q6k-dequant-band.fk: a real llama3.2:3b superblock (signed scales, both halves,
+    # all four sub-groups, both nibbles), 12 pinned round(w*1e6) from gguf's dequantize
+    g = np.load(os.path.join(G, "q6k_golden.npz"))
+    w = O.q6k_dequant(g["band_sb"], 0, 256)
+    assert np.array_equal(w, g["band_w"])  # fkwu's own decode of the same bytes
+    for i, v in g["band_pins"]:
+        assert round(w[i] * 1e6) == v, (i, w[i])
+
+
 def test_route_golden_bit_exact():
     g = np.load(os.path.join(G, "route_golden.npz"))
     for t in ("e64", "e256"):
