@@ -157,6 +157,15 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
     nb = R * C // 256 * 144 + 4 * (R + C)
     out["q4k_matvec_7168"] = {"us": round(us, 2), "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
     dense_us = us
+    # the sibling format: Q6_K decode matvec at the same 7168 x 7168 and at 4096 x 4096
+    for R in (7168, 4096):
+        q6 = [t(synth.make_q6k(np.random.default_rng([6, i]), R * R)) for i in range(16)]
+        x6 = t(np.random.default_rng(7).standard_normal(R).astype(np.float32))
+        y6 = torch.empty(R, device=dev)
+        us = _graph_us(torch, lambda i: ops.q6k_matvec(q6[i], x6, R, R, out=y6), 64, 16)
+        nb = R * R // 256 * 210 + 4 * 2 * R
+        out[f"q6k_matvec_{R}"] = {"us": round(us, 2), "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
+        del q6
     # config 2: Q4_K prefill 11008 x 4096
     R, C = workloads.Q4K_PREFILL
     qp = [t(synth.make_q4k(np.random.default_rng([4, i]), R * C)) for i in range(8)]

@@ -37,6 +37,10 @@ SIGNATURES = {
     "ck_q4k_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_matvec_ordered_f32": (_i32, [_i32, _p, _p, _p, _u32, _u32, _p]),
     "ck_q4k_matmul_batch_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
+    "ck_q6k_dequant_f32": (_i32, [_p, _p, _u64, _u64, _p]),
+    "ck_q6k_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
+    "ck_q6k_matmul_batch_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
+    "ck_q6k_matvec_part_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
     "ck_q4k_gemm_workspace_bytes": (_sz, [_u32]),
     "ck_q4k_gemm_bf16": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p, _sz, _p]),
     "ck_q4k_gemm_status": (_i32, [_u32, _p, _p]),

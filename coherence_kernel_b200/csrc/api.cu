@@ -167,9 +167,32 @@ int ck_q4k_matmul_batch_f32(const void *qb, const float *x, float *y, uint32_t r
     return fail(ck::launch_q4k_matvec((const uint8_t *)qb, x, y, rows, cols, ntok, S(s)), "ck_q4k_matmul_batch_f32");
 }
 int ck_matvec_ordered_f32(int t, const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, void *s) {
-    if (!qb || !x || !y || (t != 8 && t != 12)) return fail(CK_EARG, "ck_matvec_ordered_f32");
-    if ((t == 8 && cols % 32) || (t == 12 && ((uint64_t)rows * cols) % 256)) return fail(CK_ESHAPE, "ck_matvec_ordered_f32");
+    if (!qb || !x || !y || (t != 8 && t != 12 && t != 14)) return fail(CK_EARG, "ck_matvec_ordered_f32");
+    if ((t == 8 && cols % 32) || (t != 8 && ((uint64_t)rows * cols) % 256)) return fail(CK_ESHAPE, "ck_matvec_ordered_f32");
+    if (t == 14)
+        return fail(ck::launch_q6k_ordered((const uint8_t *)qb, x, y, rows, cols, S(s)), "ck_matvec_ordered_f32");
     return fail(ck::launch_matvec_ordered(t, (const uint8_t *)qb, x, y, rows, cols, S(s)), "ck_matvec_ordered_f32");
+}
+int ck_q6k_dequant_f32(const void *qb, float *w, uint64_t off, uint64_t n, void *s) {
+    if (!qb || !w) return fail(CK_EARG, "ck_q6k_dequant_f32");
+    return fail(ck::launch_q6k_dequant((const uint8_t *)qb, w, off, n, S(s)), "ck_q6k_dequant_f32");
+}
+int ck_q6k_matvec_f32(const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, void *s) {
+    if (!qb || !x || !y) return fail(CK_EARG, "ck_q6k_matvec_f32");
+    if (((uint64_t)rows * cols) % 256) return fail(CK_ESHAPE, "ck_q6k_matvec_f32");
+    return fail(ck::launch_q6k_matvec((const uint8_t *)qb, x, y, rows, cols, 1, S(s)), "ck_q6k_matvec_f32");
+}
+int ck_q6k_matmul_batch_f32(const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
+                            void *s) {
+    if (!qb || !x || !y || ntok == 0) return fail(CK_EARG, "ck_q6k_matmul_batch_f32");
+    if (((uint64_t)rows * cols) % 256) return fail(CK_ESHAPE, "ck_q6k_matmul_batch_f32");
+    return fail(ck::launch_q6k_matvec((const uint8_t *)qb, x, y, rows, cols, ntok, S(s)), "ck_q6k_matmul_batch_f32");
+}
+int ck_q6k_matvec_part_f32(const void *qb, const float *x, float *part, uint32_t rows, uint32_t cols, uint32_t parts,
+                           void *s) {
+    if (!qb || !x || !part || parts == 0) return fail(CK_EARG, "ck_q6k_matvec_part_f32");
+    if (((uint64_t)rows * cols) % 256) return fail(CK_ESHAPE, "ck_q6k_matvec_part_f32");
+    return fail(ck::launch_q6k_part((const uint8_t *)qb, x, part, rows, cols, parts, S(s)), "ck_q6k_matvec_part_f32");
 }
 
 size_t ck_q4k_gemm_workspace_bytes(uint32_t ntok) { return al(((size_t)ntok / 16 + 2) * 16) + 256 + 256; }

@@ -211,6 +211,45 @@ int L_q4k_matmul_batch(const Call &k, std::string &w) {
         return CK_ERR_ARG;
     return ck::launch_q4k_matvec((const uint8_t *)k.b[0], (const float *)k.b[1], (float *)k.b[2], k.c[0], k.c[1], k.c[2], k.s);
 }
+// ---- Q6_K (q6k-msl.fk, qk-matvec-lane.fk, qk-matvec-slot.fk, qk-matvec-split.fk, qk-matmul-batch.fk)
+unsigned long long q6kb(unsigned long long n) { return (n + 255) / 256 * 210; }
+int L_q6k_dequant(const Call &k, std::string &w) {
+    const unsigned long long off = k.c[0], n = k.c[1];
+    if (!need(k, 0, q6kb(off + n), w, "qb") || !need(k, 1, n * 4, w, "w")) return CK_ERR_ARG;
+    return ck::launch_q6k_dequant((const uint8_t *)k.b[0], (float *)k.b[1], off, n, k.s);
+}
+bool q6_mv_check(const Call &k, std::string &w) {
+    const unsigned long long rows = k.c[0], cols = k.c[1];
+    if ((rows * cols) % 256) { w = "rows*cols must be whole superblocks"; return false; }
+    return need(k, 0, q6kb(rows * cols), w, "qb") && need(k, 1, cols * 4, w, "x") && need(k, 2, rows * 4, w, "y");
+}
+int L_q6k_attestant(const Call &k, std::string &w) {
+    if (!q6_mv_check(k, w)) return CK_ERR_ARG;
+    return ck::launch_q6k_ordered((const uint8_t *)k.b[0], (const float *)k.b[1], (float *)k.b[2], k.c[0], k.c[1], k.s);
+}
+int L_q6k_fast(const Call &k, std::string &w) {
+    if (!q6_mv_check(k, w)) return CK_ERR_ARG;
+    return ck::launch_q6k_matvec((const uint8_t *)k.b[0], (const float *)k.b[1], (float *)k.b[2], k.c[0], k.c[1], 1,
+                                 k.s);
+}
+int L_q6k_part(const Call &k, std::string &w) {
+    const unsigned long long rows = k.c[0], cols = k.c[1], parts = k.c[2];
+    if (parts == 0) { w = "parts must be positive"; return CK_ERR_ARG; }
+    if ((rows * cols) % 256) { w = "rows*cols must be whole superblocks"; return CK_ERR_SHAPE; }
+    if (!need(k, 0, q6kb(rows * cols), w, "qb") || !need(k, 1, cols * 4, w, "x") || !need(k, 2, rows * parts * 4, w, "part"))
+        return CK_ERR_ARG;
+    return ck::launch_q6k_part((const uint8_t *)k.b[0], (const float *)k.b[1], (float *)k.b[2], k.c[0], k.c[1], k.c[2],
+                               k.s);
+}
+int L_q6k_matmul_batch(const Call &k, std::string &w) {
+    const unsigned long long rows = k.c[0], cols = k.c[1], ntok = k.c[2];
+    if ((rows * cols) % 256 || ntok == 0) { w = "rows*cols must be whole superblocks and ntok positive"; return CK_ERR_SHAPE; }
+    if (!need(k, 0, q6kb(rows * cols), w, "qb") || !need(k, 1, ntok * cols * 4, w, "x") ||
+        !need(k, 2, ntok * rows * 4, w, "y"))
+        return CK_ERR_ARG;
+    return ck::launch_q6k_matvec((const uint8_t *)k.b[0], (const float *)k.b[1], (float *)k.b[2], k.c[0], k.c[1],
+                                 k.c[2], k.s);
+}
 int L_f16_matvec(const Call &k, std::string &w) {
     const unsigned long long rows = k.c[0], cols = k.c[1];
     if (!need(k, 0, rows * cols * 2, w, "qb") || !need(k, 1, cols * 4, w, "x") || !need(k, 2, rows * 4, w, "y"))
@@ -322,6 +361,13 @@ const Entry REGISTRY[] = {
     {"form_q4k_matvec_slot_f32", 3, 2, L_q4k_fast},
     {"form_q4k_matvec_slot4_f32", 3, 2, L_q4k_fast},
     {"form_q4k_matmul_batch_f32", 3, 3, L_q4k_matmul_batch},
+    {"form_q6k_dequant_f32", 2, 2, L_q6k_dequant},
+    {"form_q6k_matvec_f32", 3, 2, L_q6k_attestant},
+    {"form_q6k_matvec_part_f32", 3, 3, L_q6k_part},
+    {"form_q6k_matvec_hoist_f32", 3, 3, L_q6k_part},
+    {"form_q6k_matvec_lane_f32", 3, 2, L_q6k_fast},
+    {"form_q6k_matvec_slot_f32", 3, 2, L_q6k_fast},
+    {"form_q6k_matmul_batch_f32", 3, 3, L_q6k_matmul_batch},
     {"form_f16_matvec_f32", 3, 2, L_f16_matvec},
     {"form_moe_route_f32", 3, 2, L_route},
     {"form_moe_route_wide_f32", 3, 2, L_route_wide},

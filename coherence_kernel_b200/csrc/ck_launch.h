@@ -19,6 +19,14 @@ int launch_matvec_ordered(int kind, const uint8_t *qb, const float *x, float *y,
 int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
                       cudaStream_t s);
 int launch_q80_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
+// Q6_K (q6k_kernels.cu): exact dequant, the attestant-order matvec, its column-split form, and the
+// decode / batched matvec (ntok tokens, token-major x and y)
+int launch_q6k_dequant(const uint8_t *qb, float *w, uint64_t off, uint64_t n, cudaStream_t s);
+int launch_q6k_ordered(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
+int launch_q6k_part(const uint8_t *qb, const float *x, float *part, uint32_t rows, uint32_t cols, uint32_t parts,
+                    cudaStream_t s);
+int launch_q6k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
+                      cudaStream_t s);
 // HBM-streaming decode matvec (gemv_stream.cu): kind 12 = Q4_K, 8 = Q8_0; cols % 256 == 0,
 // cols <= 8192, weights and x 16-byte aligned
 bool gemv_stream_ok(const void *qb, const float *x, uint32_t cols);

@@ -74,8 +74,38 @@ def q4k_matvec(qb, x, rows, cols, out=None):
     return y
 
 
+def q6k_nbytes(n_weights: int) -> int:
+    return (n_weights + 255) // 256 * 210
+
+
+def q6k_dequant(qb, off, n):
+    _dev(qb, "qb", torch.uint8, q6k_nbytes(off + n))
+    w = torch.empty(n, dtype=torch.float32, device=qb.device)
+    _lib.check(_lib.load().ck_q6k_dequant_f32(_ptr(qb), _ptr(w), off, n, _stream()), "ck_q6k_dequant_f32")
+    return w
+
+
+def q6k_matvec(qb, x, rows, cols, out=None):
+    _dev(qb, "qb", torch.uint8, q6k_nbytes(rows * cols))
+    _dev(x, "x", torch.float32, cols)
+    y = out if out is not None else torch.empty(rows, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.load().ck_q6k_matvec_f32(_ptr(qb), _ptr(x), _ptr(y), rows, cols, _stream()), "ck_q6k_matvec_f32")
+    return y
+
+
+def q6k_matmul_batch(qb, x, rows, cols):
+    """fp32 x [ntok, cols] -> fp32 y [ntok, rows]."""
+    ntok = x.shape[0]
+    _dev(qb, "qb", torch.uint8, q6k_nbytes(rows * cols))
+    _dev(x, "x", torch.float32, ntok * cols)
+    y = torch.empty((ntok, rows), dtype=torch.float32, device=x.device)
+    _lib.check(_lib.load().ck_q6k_matmul_batch_f32(_ptr(qb), _ptr(x), _ptr(y), rows, cols, ntok, _stream()),
+               "ck_q6k_matmul_batch_f32")
+    return y
+
+
 def matvec_ordered(ggml_type, qb, x, rows, cols):
-    nb = q8_0_nbytes(rows * cols) if ggml_type == 8 else q4k_nbytes(rows * cols)
+    nb = {8: q8_0_nbytes, 12: q4k_nbytes, 14: q6k_nbytes}[ggml_type](rows * cols)
     _dev(qb, "qb", torch.uint8, nb)
     _dev(x, "x", torch.float32, cols)
     y = torch.empty(rows, dtype=torch.float32, device=x.device)

@@ -45,9 +45,25 @@ int ck_q8_0_matvec_f32(const void *qb_dev, const float *x_dev, float *y_dev, uin
 int ck_q4k_matvec_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
                       void *stream);
 /* The attestant association: one thread per row, j counting down, acc = w*x + acc with no fused
- * multiply-add (q8-0-msl.fk:100-103, q4k-msl.fk:111-114).  ggml_type 8 = Q8_0, 12 = Q4_K. */
+ * multiply-add (q8-0-msl.fk:100-103, q4k-msl.fk:111-114, q6k-msl.fk:118-123).  ggml_type 8 = Q8_0,
+ * 12 = Q4_K, 14 = Q6_K. */
 int ck_matvec_ordered_f32(int ggml_type, const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows,
                           uint32_t cols, void *stream);
+/* ---- GGUF Q6_K (210 bytes / 256 weights: ql[128], qh[64], 16 signed int8 scales, f16 d), read by
+ * flat weight index like the others (form/form-stdlib/q6k-msl.fk:62-81).  rows*cols % 256 == 0.
+ * Dequant replaces form_q6k_dequant_f32 (q6k-msl.fk:109-113) and is bit-exact; the matvec replaces
+ * form_q6k_matvec_lane_f32 / _slot_f32 (qk-matvec-lane.fk:232-238, qk-matvec-slot.fk:163-166) --
+ * for the attestant association (form_q6k_matvec_f32) call ck_matvec_ordered_f32 with type 14;
+ * the batched form replaces form_q6k_matmul_batch_f32 (qk-matmul-batch.fk); the split form
+ * replaces form_q6k_matvec_part_f32 / _hoist_f32 (qk-matvec-split.fk:114-121): part[r*parts + p] =
+ * the right fold of row r over column chunk p (chunk = ceil(cols / parts)). */
+int ck_q6k_dequant_f32(const void *qb_dev, float *w_dev, uint64_t off, uint64_t n, void *stream);
+int ck_q6k_matvec_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
+                      void *stream);
+int ck_q6k_matmul_batch_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
+                            uint32_t ntok, void *stream);
+int ck_q6k_matvec_part_f32(const void *qb_dev, const float *x_dev, float *part_dev, uint32_t rows, uint32_t cols,
+                           uint32_t parts, void *stream);
 /* Batched matvec over ntok tokens, fp32 (replaces form_q4k_matmul_batch_f32,
  * qk-matmul-batch.fk:206-217): y[t*rows + r] = sum_j W[r, j] x[t*cols + j].  cols % 64 == 0. */
 int ck_q4k_matmul_batch_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
