@@ -48,3 +48,72 @@ def test_form_cell_drives_the_cuda_door(tmp_path, rows, cols):
     w = O.q4k_dequant(q, 0, rows * cols).reshape(rows, cols)
     bound = (2 * cols + 1) * 2.0 ** -24 * (np.abs(w) @ np.abs(x.astype(np.float64)))
     assert np.all(np.abs(gpu - form) <= bound)
+
+
+def _run_cell(stem, cwd):
+    image = os.path.join(REPO, "oracle", "_ref", "fk-cuda", stem + ".fkb")
+    if not (os.path.exists(FKWU_CUDA) and os.path.exists(image)):
+        pytest.skip("the reference runtime linked with the carrier was not built (no reference tree)")
+    p = subprocess.run([FKWU_CUDA, image], cwd=cwd, capture_output=True, text=True, timeout=900)
+    assert p.returncode == 0, p.stderr[-2000:]
+    line = [ln for ln in p.stdout.splitlines() if ln.startswith("[")][-1]
+    return ast.literal_eval(line.replace("true", "True").replace("false", "False"))
+
+
+@pytest.mark.parametrize("mode", [3, 4])
+def test_form_cell_runs_the_moe_layer_through_the_door(tmp_path, mode):
+    """The batched MoE layer as one enqueue of ck_moe_layer_bf16 from a Form cell on the reference
+    runtime (14 buffers, 11 constants): ids and counts bit-exact with the oracle's routing, outputs
+    within 2e-2 per token against the oracle's layer."""
+    from coherence_kernel_b200 import _lib, carrier, workloads
+    from coherence_kernel_b200.moe import MoeSpec
+    spec = (MoeSpec(512, 256, 16, 1, 4, 4, 4, 2, 2.5) if mode == 4 else MoeSpec(512, 384, 8, 2, 3, 3))
+    ntok = 12
+    w = workloads.make_moe(spec, ntok, seed=31 + mode)
+    inp = tmp_path / "ck_in"
+    inp.mkdir()
+    for k, f in (("x", "x.bin"), ("gate", "wg.bin"), ("up", "wu.bin"), ("down", "wd.bin"), ("s_gate", "sg.bin"),
+                 ("s_up", "su.bin"), ("s_down", "sd.bin"), ("router", "router.bin"), ("bias", "bias.bin")):
+        np.ascontiguousarray(w[k]).tofile(inp / f)
+    cfg = spec.cfg()
+    import ctypes
+    ws = _lib.load().ck_moe_workspace_bytes(ctypes.byref(cfg), ntok)
+    consts = [spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
+              spec.topk_groups, carrier.f32_bits(spec.wscale), carrier.f32_bits(spec.tau), ntok]
+    sizes = [w["x"].nbytes, w["gate"].nbytes, w["s_gate"].nbytes, w["router"].nbytes, w["bias"].nbytes, ws]
+    np.array(consts + sizes + [0, 0, 0], dtype=np.uint32).tofile(inp / "moe_meta.bin")
+    live, pipe, enq, synced, ids, counts, out = _run_cell("ck_door_moe", tmp_path)
+    assert live in (1, True) and pipe > 0 and enq == 1 and synced == 1
+    from oracle import oracle as O
+    ocfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
+                     spec.topk_groups, spec.wscale)
+    rids, _, rout = O.moe_layer(ocfg, w, w["x"], np.arange(ntok))
+    assert np.array_equal(np.array(ids).reshape(ntok, spec.nsel), rids)
+    assert np.array_equal(np.array(counts), np.bincount(rids.reshape(-1), minlength=spec.n_experts))
+    out = np.array(out).reshape(ntok, spec.hidden)
+    for t in range(ntok):
+        assert np.abs(out[t] - rout[t]).max() <= 2e-2 * np.abs(rout[t]).max(), t
+
+
+@pytest.mark.parametrize("rows,cols,ntok", [(256, 512, 20), (256, 512, 3)])
+def test_form_cell_runs_the_prefill_gemm_through_the_door(tmp_path, rows, cols, ntok):
+    """The tensor-core Q4_K GEMM as one enqueue of ck_q4k_gemm_bf16 from a Form cell (the dequantizing
+    GEMM at 20 tokens, the few-token tensor-core matvec at 3): within 2e-2 of sum |w x| per output."""
+    from coherence_kernel_b200 import _lib
+    rng = np.random.default_rng(rows + ntok)
+    q = synth.make_q4k(rng, rows * cols)
+    xb = synth.make_bf16(rng, (ntok, cols))
+    inp = tmp_path / "ck_in"
+    inp.mkdir()
+    q.tofile(inp / "q4.bin")
+    xb.tofile(inp / "xb.bin")
+    ws = _lib.load().ck_q4k_gemm_workspace_bytes(ntok)
+    np.array([rows, cols, ntok, ws], dtype=np.uint32).tofile(inp / "gemm_meta.bin")
+    live, pipe, enq, synced, y = _run_cell("ck_door_gemm", tmp_path)
+    assert live in (1, True) and pipe > 0 and enq == 1 and synced == 1
+    from oracle import oracle as O
+    w = O.q4k_dequant(q, 0, rows * cols).reshape(rows, cols)
+    x64 = synth.bf16_bits_to_f32(xb).astype(np.float64)
+    ref = x64 @ w.T
+    y = np.array(y).reshape(ntok, rows)
+    assert np.all(np.abs(y - ref) <= 2e-2 * (np.abs(x64) @ np.abs(w).T))
