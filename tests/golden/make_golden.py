@@ -162,6 +162,24 @@ def golden_q6k(fr: FormRunner, ref: str):
     print("q6k golden:", len(out["y6"]), "rows,", len(out["fix_w"]), "fixture weights, 12 band pins")
 
 
+def golden_gguf(ref: str):
+    """The reference's mini-GGUF (header, one key/value, one Q4_K tensor-info record, the pad, one real
+    superblock) from weight-load-q4k-band.fk, as bytes, with that band's pins: tensor-info start, type,
+    dim0, data offset, and round(w * 1e6) at eight indices."""
+    import re
+    text = open(os.path.join(ref, "form", "form-stdlib", "tests", "weight-load-q4k-band.fk")).read()
+    body = re.search(r"\(let g \(list(.*?)\)\)", text, re.S).group(1)
+    g = np.array([int(v) for v in body.split()], dtype=np.uint8)
+    pins = [(int(i), int(v)) for i, v in re.findall(r"\(wl-q4k-at g off (\d+) *\) +1000000\.0\)\) (-?\d+)\)", text)]
+    last = re.search(r"\(nth full 255\) 1000000\.0\)\) (-?\d+)\)", text)
+    pins.append((255, int(last.group(1))))
+    ti = int(re.search(r"\(eq ti (\d+)\)", text).group(1))
+    assert len(pins) == 8, pins
+    np.savez_compressed(os.path.join(HERE, "gguf_golden.npz"), band_gguf=g, band_pins=np.array(pins, dtype=np.int64),
+                        band_tinfo_start=np.array(ti))
+    print("gguf golden:", g.size, "bytes, tensor info at", ti, ",", len(pins), "pins")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("CK_REFERENCE"))
@@ -173,7 +191,7 @@ def main():
         subprocess.run(["make", "-s", "-C", os.path.join(REPO, "oracle"), "ref", f"REF={a.ref}"], check=True)
     fr = FormRunner(a.ref)
     try:
-        todo = a.only.split(",") if a.only else ["quant", "fixtures", "route", "moe", "q6k"]
+        todo = a.only.split(",") if a.only else ["quant", "fixtures", "route", "moe", "q6k", "gguf"]
         if "quant" in todo:
             golden_quant(fr)
         if "fixtures" in todo:
@@ -184,6 +202,8 @@ def main():
             golden_moe(fr)
         if "q6k" in todo:
             golden_q6k(fr, a.ref)
+        if "gguf" in todo:
+            golden_gguf(a.ref)
     finally:
         fr.close()
 

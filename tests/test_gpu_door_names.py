@@ -116,8 +116,8 @@ def test_f16_matvec_name(door):
     wh = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float16)
     x = rng.standard_normal(cols).astype(np.float32)
     w = np.array([[O.lib().ckr_f16(int(b)) for b in row] for row in wh.view(np.uint16)])
-    ref = np.array([O.lib().ckr_dot(np.ascontiguousarray(w[r]).ctypes.data,
-                                    x.astype(np.float64).ctypes.data, cols) for r in range(rows)])
+    x64 = x.astype(np.float64)  # named: the C call reads through its pointer
+    ref = np.array([O.lib().ckr_dot(w[r].ctypes.data, x64.ctypes.data, cols) for r in range(rows)])
     hw, hx, hy = door.buf(wh), door.buf(x), door.buf(nbytes=rows * 4)
     door.run("form_f16_matvec_f32", [hw, hx, hy], [rows, cols], rows)
     y = door.read(hy, rows)

@@ -117,3 +117,57 @@ def test_form_cell_runs_the_prefill_gemm_through_the_door(tmp_path, rows, cols, 
     ref = x64 @ w.T
     y = np.array(y).reshape(ntok, rows)
     assert np.all(np.abs(y - ref) <= 2e-2 * (np.abs(x64) @ np.abs(w).T))
+
+
+def _gguf_case(tmp_path, raw_file: bytes, align=32):
+    inp = tmp_path / "ck_in"
+    inp.mkdir(exist_ok=True)
+    (inp / "model.gguf").write_bytes(raw_file)
+    np.array([len(raw_file), align], dtype=np.uint32).tofile(inp / "gguf_meta.bin")
+    return _run_cell("ck_door_gguf", tmp_path)
+
+
+def test_gguf_ingest_through_the_door(tmp_path):
+    """GGUF ingest: a Form cell walks a model file's tensor table with the reference's egg-* recipes,
+    binds every tensor's bytes in HBM with metal_buf_from_file at its absolute offset, and dequantizes
+    it on the device through the door (Q4_K, Q6_K, Q8_0; F32 read back); the device weights equal the
+    Form recipes' decode of the same file bytes (Q6_K, Q8_0 and F32 bit for bit, Q4_K within one
+    rounding), and the table agrees with the host reader coherence_kernel_b200.gguf."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from gguf_file import write_gguf
+    from coherence_kernel_b200 import gguf
+    rng = np.random.default_rng(40)
+    g6 = np.load(os.path.join(REPO, "tests", "golden", "q6k_golden.npz"))
+    ts = [("blk.0.ffn_gate.weight", (256, 2), 12, synth.make_q4k(rng, 512).tobytes()),
+          ("token_embd.weight", (256, 2), 14, np.concatenate([g6["band_sb"], synth.make_q6k(rng, 256)]).tobytes()),
+          ("blk.0.attn_q.weight", (64, 2), 8, synth.make_q8_0(rng, 128).tobytes()),
+          ("blk.0.ffn_gate_inp.weight", (8, 3), 0, rng.standard_normal(24).astype(np.float32).tobytes())]
+    path = tmp_path / "written.gguf"
+    write_gguf(str(path), ts, kv={"general.architecture": "llama"})
+    table, base, _ = gguf.read_table(str(path))
+    live, ok, ntens, start, dbase, tensors = _gguf_case(tmp_path, path.read_bytes())
+    assert live in (1, True) and ok == 1 and ntens == len(ts) and dbase == base
+    for (name, dims, t, raw), row in zip(ts, tensors):
+        nlen, rt, nd, d0, d1, off, nbytes, h, gpu, form = row
+        assert (nlen, rt, nd, d0, d1) == (len(name), t, 2, dims[0], dims[1])
+        assert off == table[name].offset and nbytes == table[name].nbytes == len(raw) and h > 0
+        gpu, form = np.array(gpu, dtype=np.float64), np.array(form, dtype=np.float64)
+        if t == 12:
+            assert np.all(np.abs(gpu - form) <= 2.0 ** -24 * np.abs(form)), name
+        else:
+            assert np.array_equal(gpu, form.astype(np.float32).astype(np.float64)), name
+
+
+def test_reference_mini_gguf_through_the_door(tmp_path):
+    """The reference's own mini-GGUF (weight-load-q4k-band.fk): tensor info at byte 41, data base 96,
+    one Q4_K superblock bound in HBM through the door and dequantized there; the band's weight pins
+    hold on the device values."""
+    g = np.load(os.path.join(REPO, "tests", "golden", "gguf_golden.npz"))
+    live, ok, ntens, start, dbase, tensors = _gguf_case(tmp_path, g["band_gguf"].tobytes())
+    assert ok == 1 and ntens == 1 and start == int(g["band_tinfo_start"]) and dbase == 96
+    (nlen, t, nd, d0, d1, off, nbytes, h, gpu, form), = tensors
+    assert t == 12 and d0 == 256 and off == 96 and nbytes == 144
+    gpu = np.array(gpu, dtype=np.float64)
+    for i, v in g["band_pins"]:
+        assert round(gpu[i] * 1e6) == v, (i, gpu[i])
