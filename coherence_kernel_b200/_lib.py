@@ -85,6 +85,9 @@ SIGNATURES = {
     "fk_metal_buf_free_external": (_ll, [_ll]),
     "fk_metal_submit_external": (_ll, []),
     "fk_metal_fence_wait_external": (_ll, [_ll]),
+    "fk_cuda_go_external": (_ll, [_p, _p, _p, _u32, _u32, ctypes.c_char_p, _ll]),
+    "fk_cuda_matvec_f32_external": (_ll, [_p, _p, _p, _u32, _u32]),
+    "fk_cuda_matvec_fixture_external": (_ll, []),
     "fk_metal_matvec_fixture_external": (_ll, [ctypes.c_char_p, _ll]),
     "fk_metal_matvec_f32_external": (_ll, [ctypes.c_char_p, _ll, ctypes.c_char_p, _ll, ctypes.c_char_p, _ll,
                                            ctypes.c_char_p, _ll]),

@@ -44,6 +44,21 @@ long long fk_metal_matvec_fixture_external(char *out, long long cap);
 long long fk_metal_matvec_f32_external(const char *msl, long long msl_len, const char *kernel, long long kernel_len,
                                        const char *model, long long model_len, char *out, long long cap);
 
+/* ---- the CUDA matvec doors, tag 232 (fixture witness) and tag 233 `(cuda_matvec_f32 W x)`, which the
+ * reference serves only on Windows through nvcuda.dll (runtime/fkwu-uni.c:4753-5050).
+ * fkwu-uni.c:4764 fk_cuda_go -- y = W.x with W [rows*cols], x [cols], y [rows] in HOST memory, one
+ * device thread per row folding j downward with two roundings per term (no fused multiply-add);
+ * the device name into gname.  0, or the first refusal's negative code (-3 no driver, -4 no device,
+ * -9 launch failed, -10 device allocation or copy failed). */
+long long fk_cuda_go_external(const float *W, const float *x, float *y, unsigned rows, unsigned cols, char *gname,
+                              long long gcap);
+/* fkwu-uni.c:4976 fk_cuda_matvec_f32 -- the tag-233 door's work: fk_cuda_go, then the same fold on the
+ * CPU; answers the number of rows that agree bit for bit (the `agree` head of the returned list), or
+ * a negative code; -1 for the door's own refusals (cols == 0, more than 4194304 weights). */
+long long fk_cuda_matvec_f32_external(const float *W, const float *x, float *y, unsigned rows, unsigned cols);
+/* fkwu-uni.c:4907 fk_cuda_matvec -- tag 232: the fixed 3x4 witness; answers the rows that agree (3) */
+long long fk_cuda_matvec_fixture_external(void);
+
 #ifdef __cplusplus
 }
 #endif
