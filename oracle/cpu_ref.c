@@ -255,6 +255,17 @@ double ckr_sqrt(double v) {
     return g;
 }
 
+/* llama-numerics.fk:40-50 ln-rmsnorm: o_i = (x_i * (1 / rms)) * g_i, rms = tn-sqrt(ms + eps), ms =
+ * the left-fold sum of x_i * x_i divided by the float-counted length (tn-flen). */
+void ckr_rmsnorm(const double *x, const double *g, int64_t n, double eps, double *out) {
+    double acc = 0.0;
+    for (int64_t i = 0; i < n; i++) acc = acc + x[i] * x[i];
+    double flen = 0.0;
+    for (int64_t i = 0; i < n; i++) flen = 1.0 + flen;
+    double s = 1.0 / ckr_sqrt(acc / flen + eps);
+    for (int64_t i = 0; i < n; i++) out[i] = (x[i] * s) * g[i];
+}
+
 /* trig.fk:40-53 fln: e*LN2 + ln-m(mantissa), ln-m(m) = 2*(z + sum_j z^(2j+3)/(2j+3)), 14 terms. */
 double ckr_ln(double x) {
     double xf = x * 1.0;

@@ -20,6 +20,8 @@ double ckr_bf16(uint32_t bits);
 
 /* form/form-stdlib/q8-0-msl.fk:53-72 (q80-flat-at): weight at a flat index, 34-byte blocks */
 double ckr_q80_at(const uint8_t *src, int64_t base, int64_t idx);
+/* llama-numerics.fk:40-50 ln-rmsnorm over n values with gain g */
+void ckr_rmsnorm(const double *x, const double *g, int64_t n, double eps, double *out);
 /* form/form-stdlib/q6k-msl.fk:62-81 (q6m-flat-at): weight at a flat index, 210-byte superblocks;
  * ckr_q6k_codes: the 6-bit code q + 32 (bits 0..7) and the raw scale byte (bits 8..15);
  * ckr_q6k_dequant: the flat range [off, off+n); ckr_q6k_matvec: the right fold per row. */

@@ -59,6 +59,8 @@ def lib():
         for n in ("ckr_exp", "ckr_sqrt", "ckr_ln", "ckr_sigmoid", "ckr_silu"):
             getattr(L, n).restype = ctypes.c_double
             getattr(L, n).argtypes = [ctypes.c_double]
+        L.ckr_rmsnorm.restype = None
+        L.ckr_rmsnorm.argtypes = [_p, _p, _c_i64, ctypes.c_double, _p]
         L.ckr_route_softmax.restype = None
         L.ckr_route_softmax.argtypes = [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p, _p]
         L.ckr_route_dsv4.restype = None
@@ -118,6 +120,14 @@ def q6k_matvec(qb, x, rows, cols):
     y = np.empty(rows, dtype=np.float64)
     lib().ckr_q6k_matvec(_ptr(qb), _ptr(x), _ptr(y), rows, cols)
     return y
+
+
+def rmsnorm(x, g, eps):
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    g = np.ascontiguousarray(g, dtype=np.float64)
+    out = np.empty_like(x)
+    lib().ckr_rmsnorm(_ptr(x), _ptr(g), x.size, eps, _ptr(out))
+    return out
 
 
 def q80_matvec(qb, x, rows, cols):

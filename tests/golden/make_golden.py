@@ -180,6 +180,26 @@ def golden_gguf(ref: str):
     print("gguf golden:", g.size, "bytes, tensor info at", ti, ",", len(pins), "pins")
 
 
+def golden_norm(fr: FormRunner):
+    """ln-rmsnorm (llama-numerics.fk:40-50) on the reference runtime: a hidden-size vector and a
+    short one with a large eps."""
+    out = {}
+    rng = np.random.default_rng(12)
+    for tag, n, eps in (("h", 7168, 1e-6), ("s", 37, 0.25)):
+        x = (rng.standard_normal(n) * 3).astype(np.float32)
+        g = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+        meta = np.zeros(2, dtype=np.uint32)
+        meta[0] = n
+        meta[1] = np.array([eps], dtype=np.float32).view(np.uint32)[0]
+        fr.put("norm_meta.bin", meta)
+        fr.put("xn.bin", x)
+        fr.put("gn.bin", g)
+        out[tag + "_x"], out[tag + "_g"], out[tag + "_eps"] = x, g, np.float32(eps)
+        out[tag + "_out"] = np.array(fr.run("ck_norm.fk"), dtype=np.float64)
+    np.savez_compressed(os.path.join(HERE, "norm_golden.npz"), **out)
+    print("norm golden:", len(out["h_out"]), "+", len(out["s_out"]))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("CK_REFERENCE"))
@@ -191,7 +211,7 @@ def main():
         subprocess.run(["make", "-s", "-C", os.path.join(REPO, "oracle"), "ref", f"REF={a.ref}"], check=True)
     fr = FormRunner(a.ref)
     try:
-        todo = a.only.split(",") if a.only else ["quant", "fixtures", "route", "moe", "q6k", "gguf"]
+        todo = a.only.split(",") if a.only else ["quant", "fixtures", "route", "moe", "q6k", "gguf", "norm"]
         if "quant" in todo:
             golden_quant(fr)
         if "fixtures" in todo:
@@ -204,6 +224,8 @@ def main():
             golden_q6k(fr, a.ref)
         if "gguf" in todo:
             golden_gguf(a.ref)
+        if "norm" in todo:
+            golden_norm(fr)
     finally:
         fr.close()
 

@@ -71,6 +71,14 @@ def test_q6k_dequant_band_pins():
         assert round(w[i] * 1e6) == v, (i, w[i])
 
 
+def test_rmsnorm_golden_bit_exact():
+    # fkwu's ln-rmsnorm (llama-numerics.fk:40-50) with its tn-sqrt Newton iteration
+    g = np.load(os.path.join(G, "norm_golden.npz"))
+    for t in ("h", "s"):
+        out = O.rmsnorm(g[t + "_x"].astype(np.float64), g[t + "_g"].astype(np.float64), float(g[t + "_eps"]))
+        assert np.array_equal(out, g[t + "_out"]), t
+
+
 def test_route_golden_bit_exact():
     g = np.load(os.path.join(G, "route_golden.npz"))
     for t in ("e64", "e256"):
