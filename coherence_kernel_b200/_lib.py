@@ -26,6 +26,11 @@ class MoeConfig(ctypes.Structure):
                 ("mode", _u32), ("ngroups", _u32), ("topk_groups", _u32), ("wscale", _f), ("tau", _f)]
 
 
+class DecodeConfig(ctypes.Structure):
+    """ck_decode_config (include/ck_b200.h)."""
+    _fields_ = [("hidden", _u32), ("max_tokens", _u32), ("eps", _f), ("moe", MoeConfig)]
+
+
 # name -> (restype, argtypes); every symbol include/*.h declares
 SIGNATURES = {
     "ck_last_error": (ctypes.c_char_p, []),
@@ -72,6 +77,13 @@ SIGNATURES = {
     "ck_gather_rows": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_ep_dispatch_plan": (_i32, [_p, _p, _u32, _u32, _u32, _u32, _p, _p, _p, _p, _p, _p]),
     "ck_wait_selftest": (_i32, [_u64, _p, _p, _p]),
+    "ck_decode_step_workspace_bytes": (_sz, [ctypes.POINTER(DecodeConfig)]),
+    "ck_decode_step_create": (_p, [ctypes.POINTER(DecodeConfig)] + [_p] * 16 + [_sz]),
+    "ck_decode_step_run": (_i32, [_p, _p, _p, _p, _p, _u32, _p]),
+    "ck_decode_step_capture": (_i32, [_p, _p, _p, _p, _p, _u32, _p]),
+    "ck_decode_step_replay": (_i32, [_p, _p]),
+    "ck_decode_step_status": (_i32, [_p, _u32, _p]),
+    "ck_decode_step_destroy": (None, [_p]),
     # the handle door
     "fk_metal_pipeline_external": (_ll, [ctypes.c_char_p, _ll, ctypes.c_char_p, _ll]),
     "fk_metal_buf_alloc_external": (_ll, [_ll]),

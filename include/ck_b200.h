@@ -202,6 +202,42 @@ int ck_ep_dispatch_plan(const int32_t *ids_dev, const float *wts_dev, uint32_t n
                         uint32_t n_experts, uint32_t world, int32_t *counts_dev, int64_t *sizes_dev,
                         int32_t *send_tok_dev, int32_t *meta_dev, int32_t *ret_pos_dev, void *stream);
 
+/* ---- a device-resident decode step of a transformer block with an MoE feed-forward (no single
+ * counterpart in the reference, whose decode token is ~400 separate host dispatches; its measured
+ * seam cost is receipts/2026-07-22-ship-the-slot-map.md:135-145).  Per token, in one stream:
+ *   a = rmsnorm(h, g_attn) (ln-rmsnorm, llama-numerics.fk:40-50); q = Wq a, k = Wk a, v = Wv a;
+ *   h += Wo v (attention at a single position, whose output is v); b = bf16(rmsnorm(h, g_ffn));
+ *   h += ck_moe_layer_bf16(b).
+ * Wq/Wk/Wv/Wo are Q4_K [hidden x hidden]; g_* fp32 [hidden]; the MoE weights as for
+ * ck_moe_layer_bf16 (moe.hidden == hidden).  h fp32 [ntok, hidden] is updated in place; q, k, v
+ * are fp32 [ntok, hidden] outputs.  hidden % 256 == 0, ntok <= max_tokens.  All scratch comes from
+ * the caller's workspace (ck_decode_step_workspace_bytes).  ck_decode_step_run issues the step;
+ * ck_decode_step_capture records one run with these buffer addresses into a CUDA graph on a
+ * non-default stream (make one ck_decode_step_run first: it loads the kernels), and
+ * ck_decode_step_replay launches that graph -- the whole step as one launch. */
+typedef struct {
+    uint32_t hidden, max_tokens;
+    float eps;
+    ck_moe_config moe;
+} ck_decode_config;
+typedef struct ck_decode_step ck_decode_step;
+size_t ck_decode_step_workspace_bytes(const ck_decode_config *cfg);
+/* NULL on a bad configuration, a short workspace or a missing weight */
+ck_decode_step *ck_decode_step_create(const ck_decode_config *cfg, const void *wq_dev, const void *wk_dev,
+                                      const void *wv_dev, const void *wo_dev, const float *g_attn_dev,
+                                      const float *g_ffn_dev, const void *w_gate_dev, const void *w_up_dev,
+                                      const void *w_down_dev, const void *s_gate_dev, const void *s_up_dev,
+                                      const void *s_down_dev, const float *router_w_dev, const float *bias_dev,
+                                      void *workspace_dev, size_t workspace_bytes);
+int ck_decode_step_run(ck_decode_step *step, float *h_dev, float *q_dev, float *k_dev, float *v_dev, uint32_t ntok,
+                       void *stream);
+int ck_decode_step_capture(ck_decode_step *step, float *h_dev, float *q_dev, float *k_dev, float *v_dev,
+                           uint32_t ntok, void *stream);
+int ck_decode_step_replay(ck_decode_step *step, void *stream);
+/* synchronizes; CK_ETIMEOUT when a device wait of the step's MoE layer over ntok tokens gave up */
+int ck_decode_step_status(ck_decode_step *step, uint32_t ntok, void *stream);
+void ck_decode_step_destroy(ck_decode_step *step);
+
 /* Failure-path self-test (no counterpart in the reference).  Runs the library's bounded device wait
  * on an mbarrier that nothing ever arrives on, with a time limit of limit_ns (1 ns .. 2 s): the wait
  * gives up, writes code 77 to *err_dev (which the caller zeroes first) and the time it waited to
