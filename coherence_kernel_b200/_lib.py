@@ -78,7 +78,7 @@ SIGNATURES = {
     "ck_ep_dispatch_plan": (_i32, [_p, _p, _u32, _u32, _u32, _u32, _p, _p, _p, _p, _p, _p]),
     "ck_wait_selftest": (_i32, [_u64, _p, _p, _p]),
     "ck_decode_step_workspace_bytes": (_sz, [ctypes.POINTER(DecodeConfig)]),
-    "ck_decode_step_create": (_p, [ctypes.POINTER(DecodeConfig)] + [_p] * 16 + [_sz]),
+    "ck_decode_step_create": (_p, [ctypes.POINTER(DecodeConfig)] + [_p] * 15 + [_sz]),
     "ck_decode_step_run": (_i32, [_p, _p, _p, _p, _p, _u32, _p]),
     "ck_decode_step_capture": (_i32, [_p, _p, _p, _p, _p, _u32, _p]),
     "ck_decode_step_replay": (_i32, [_p, _p]),

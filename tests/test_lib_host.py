@@ -71,3 +71,24 @@ def test_synth_bf16_round_to_nearest_even():
     back = synth.bf16_bits_to_f32(b)
     ref = torch.tensor(x).to(torch.bfloat16).to(torch.float32).numpy()
     assert np.array_equal(back, ref)
+
+
+def test_decode_step_create_and_destroy_on_the_host(cuda_lib):
+    """ck_decode_step_create only records pointers and carves the workspace (no device work), so its
+    argument list, its refusals and ck_decode_step_destroy are checked here without a GPU."""
+    import ctypes
+
+    from coherence_kernel_b200 import _lib, workloads
+    L = _lib.load()
+    cfg = _lib.DecodeConfig(7168, 16, 1e-6, workloads.MOE_DSV3.cfg())
+    need = L.ck_decode_step_workspace_bytes(ctypes.byref(cfg))
+    assert need > 0
+    fake = [ctypes.c_void_p(0x10000 * (i + 1)) for i in range(15)]
+    h = L.ck_decode_step_create(ctypes.byref(cfg), *fake[:14], fake[14], need)
+    assert h
+    L.ck_decode_step_destroy(h)
+    assert not L.ck_decode_step_create(ctypes.byref(cfg), *fake[:14], fake[14], need - 1)   # short workspace
+    assert not L.ck_decode_step_create(ctypes.byref(cfg), None, *fake[1:14], fake[14], need)  # missing weight
+    bad = _lib.DecodeConfig(7000, 16, 1e-6, workloads.MOE_DSV3.cfg())
+    assert L.ck_decode_step_workspace_bytes(ctypes.byref(bad)) == 0                          # hidden mismatch
+    assert L.ck_decode_step_replay(None, None) == -3
