@@ -468,23 +468,94 @@ def cpu_baseline(spec, w, target_s=12.0):
                       f"shared SwiGLU experts, combine) on the oracle, {nth} host threads, {dt:.1f} s"}
 
 
+FKWU = os.path.join(REPO, "oracle", "_ref", "fkwu")
+FKWU_ROWS = os.path.join(REPO, "oracle", "_ref", "fk", "ck_rows.fkb")
+
+
+def fkwu_sample(spec, steps, warmup, rows=3, nproc=None):
+    """The reference's own CPU path, timed: its runtime (fkwu, compiled from runtime/fkwu-uni.c) runs
+    the Form recipes of the layer's dominant work -- right folds (tb-dot) of Q4_K expert rows decoded
+    weight by weight (q4m-flat-at) and of fp32 router rows -- one process per host core, all at once.
+    Each step every process folds `rows` expert rows of `hidden` weights and one router row; the step
+    is timed from the first start to the last exit, process start-up included.  Tokens/s is
+    extrapolated by weights: a token of the layer folds 9 x 3 expert matrices (8 routed + 1 shared,
+    inter x hidden each) and the 256 x hidden router."""
+    import shutil
+    import tempfile
+    from coherence_kernel_b200 import synth
+    nproc = nproc or min(os.cpu_count() or 1, 16)
+    tmp = tempfile.mkdtemp(prefix="ck_fkwu_")
+    try:
+        H = spec.hidden
+        for p in range(nproc):
+            d = os.path.join(tmp, f"p{p}", "ck_in")
+            os.makedirs(d)
+            rng = np.random.default_rng([9, p])
+            np.array([rows, H, 1, H], dtype=np.uint32).tofile(os.path.join(d, "rows_meta.bin"))
+            synth.make_q4k(rng, rows * H).tofile(os.path.join(d, "rq4.bin"))
+            rng.standard_normal(H).astype(np.float32).tofile(os.path.join(d, "rx4.bin"))
+            synth.make_router(rng, 1, H).tofile(os.path.join(d, "rr.bin"))
+            rng.standard_normal(H).astype(np.float32).tofile(os.path.join(d, "rxr.bin"))
+        times = []
+        for _ in range(warmup + steps):
+            t0 = time.perf_counter()
+            procs = [subprocess.Popen([FKWU, FKWU_ROWS], cwd=os.path.join(tmp, f"p{p}"), stdout=subprocess.DEVNULL,
+                                      stderr=subprocess.DEVNULL) for p in range(nproc)]
+            rcs = [pr.wait() for pr in procs]
+            times.append(time.perf_counter() - t0)
+            if any(rcs):
+                raise RuntimeError(f"fkwu exited with {rcs}")
+        dt = sum(times[warmup:]) / max(1, steps)
+        weights_step = nproc * (rows * H + H)
+        weights_token = (spec.nsel + spec.n_shared) * 3 * spec.inter * H + spec.n_experts * H
+        value = weights_step / dt / weights_token
+        return {"value": value, "unit": "tokens/s", "cores": nproc, "kind": "reference", "step_s": dt,
+                "sample": f"fkwu, the reference's runtime, {nproc} processes at once; per process and step "
+                          f"{rows} Q4_K expert rows of {H} weights (q4m-flat-at + tb-dot) and 1 fp32 router "
+                          f"row; {weights_step} weights per step in {dt:.2f} s, extrapolated to "
+                          f"{weights_token} weights per token"}
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def run_reference(args, rank, world):
-    """The reference arm: the reference path's CPU implementation on the host cores, same workload."""
+    """The reference arm: the reference path's own CPU implementation on the host cores, same
+    workload -- fkwu (the reference's runtime) where it was built with the repository, else the
+    oracle's C restatement of its recipes."""
     from coherence_kernel_b200 import workloads
     if rank != 0:
         return
     spec = workloads.MOE_DSV3
-    nthreads = min(os.cpu_count() or 1, 16)
-    # only the experts the sampled tokens touch are needed; generate the full set lazily by id
-    probe = workloads.make_moe(spec, workloads.MOE_DSV3_TOKENS, seed=0, experts=[])
+    if os.path.exists(FKWU) and os.path.exists(FKWU_ROWS):
+        cb = fkwu_sample(spec, args.steps, args.warmup)
+        value, dt, dtype = cb["value"], cb["step_s"], "f64"
+        sample = {"sample_weights_per_step": "see cpu_baseline.sample"}
+    else:
+        cb = port_reference(spec, args)
+        value, dt, dtype = cb["value"], cb["step_s"], "f64"
+        sample = {"sample_tokens_per_step": cb["cores"]}
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "config": dict({"workload": WORKLOAD, "tokens": workloads.MOE_DSV3_TOKENS}, **sample),
+            "cpu_baseline": cb,
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def port_reference(spec, args):
+    """The oracle (the C restatement of the reference's recipes) on whole tokens of the layer, one per
+    host thread, when the reference's runtime was not built."""
+    from coherence_kernel_b200 import workloads
     from oracle import oracle as O
+    nthreads = min(os.cpu_count() or 1, 16)
+    probe = workloads.make_moe(spec, workloads.MOE_DSV3_TOKENS, seed=0, experts=[])
     cfg = O.moe_cfg(spec.hidden, spec.inter, spec.n_experts, spec.n_shared, spec.nsel, spec.mode, spec.ngroups,
                     spec.topk_groups, spec.wscale)
     toks = np.arange(nthreads)
     ids, _, _ = O.moe_route(cfg, probe["router"], probe["bias"], probe["x"][:nthreads], nthreads=nthreads)
     used = sorted(set(ids.reshape(-1).tolist()))
     sub = workloads.make_moe(spec, workloads.MOE_DSV3_TOKENS, seed=0, experts=used)
-    # place the touched experts at their ids in sparse full-size arrays is wasteful; remap instead
     remap = {e: i for i, e in enumerate(used)}
     mb = spec.matrix_bytes
     full = {}
@@ -501,16 +572,8 @@ def run_reference(args, rank, world):
         O.moe_layer(cfg, full, full["x"], toks, nthreads=nthreads)
         times.append(time.perf_counter() - t0)
     dt = sum(times[args.warmup:]) / max(1, args.steps)
-    value = nthreads / dt
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": workloads.MOE_DSV3_TOKENS,
-                       "sample_tokens_per_step": int(nthreads)},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
-                             "sample": f"{nthreads} tokens of the layer per step, one per host thread"},
-            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    return {"value": nthreads / dt, "unit": "tokens/s", "cores": nthreads, "kind": "port", "step_s": dt,
+            "sample": f"{nthreads} tokens of the layer per step on the oracle, one per host thread"}
 
 
 def main():
@@ -753,7 +816,12 @@ def main():
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(spec, {k: w[k] for k in w}) if len(experts) == spec.n_experts else None
+            port = cpu_baseline(spec, {k: w[k] for k in w}) if len(experts) == spec.n_experts else None
+            if os.path.exists(FKWU) and os.path.exists(FKWU_ROWS):
+                cpu = fkwu_sample(spec, steps=3, warmup=1)
+                cpu["port"] = port
+            else:
+                cpu = port
         # our kernels per step: route 7 (split, tiles, logits GEMM, select, the two forms of the
         # exact logits, exact select), permute 3, GEMM 2, combine 1; expert parallel plans the
         # exchange (1) and gathers the dispatch rows (1) in place of the source permute, regroups on
