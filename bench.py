@@ -411,16 +411,40 @@ def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, 
             step(k)
         torch.cuda.synchronize()
         dist.barrier()
+        graphed = hasattr(lay, "peers")  # the peer-memory exchange never waits on the host
+        if graphed:
+            # a decode engine replays its step as a CUDA graph: four steps (all 16 dense weight
+            # copies) captured once per rank; the replays meet at the layer's device barriers
+            gs = torch.cuda.Stream()
+            with torch.cuda.stream(gs):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=gs):
+                    for k in range(4):
+                        step(k)
+            torch.cuda.synchronize()
+            dist.barrier()
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for k in range(steps):
-            step(k)
+        if graphed:
+            for _ in range(max(1, steps // 4)):
+                g.replay()
+        else:
+            for k in range(steps):
+                step(k)
         b.record()
         torch.cuda.synchronize()
-        us = torch.tensor([a.elapsed_time(b) * 1e3 / steps], dtype=torch.float64, device=dev)
+        nsteps = 4 * max(1, steps // 4) if graphed else steps
+        us = torch.tensor([a.elapsed_time(b) * 1e3 / nsteps], dtype=torch.float64, device=dev)
         dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        if graphed:
+            del g
+            lay.check()
         out_b, ids_b, wts_b, _ = step(0)
-        used = torch.tensor([float(int((lay.counts2 > 0).sum().item()) if lay.last_recv_pairs else 0)],
+        used = torch.tensor([float(int((lay.counts2 > 0).sum().item()))],
                             dtype=torch.float64, device=dev)
         mine = float(4 * dense_b + (used.item() + spec.n_shared) * 3 * spec.matrix_bytes)
         tot = torch.tensor([mine], dtype=torch.float64, device=dev)
@@ -430,7 +454,8 @@ def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, 
         sweep[f"b{bsz}"] = {"tokens_per_rank": bsz, "tokens_per_step": bsz * world, "us_per_step": round(us, 1),
                             "experts_touched": int(used.item()), "bytes_per_token": int(tot.item() / (bsz * world)),
                             "roofline": _roof("hbm", tot.item() / world / us / 1e3, hbm, "GB/s"),
-                            "timing": "eager steps, CUDA events, max over ranks"}
+                            "timing": ("CUDA graph of 4 decode steps replayed, CUDA events, max over ranks" if graphed
+                                       else "eager steps, CUDA events, max over ranks")}
         if bsz == 16:
             # parity of the skewed decode batch (every token's routing, a sample of outputs)
             wb = dict(w)
@@ -440,6 +465,8 @@ def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, 
                                            wfull=None if wfull is None else dict(wfull, bias=wb["bias"]))
             if not okp:
                 raise SystemExit("decode sweep parity failed")
+    if hasattr(lay, "close"):
+        lay.close()
     del lay, q4
     torch.cuda.synchronize()
     return {"steps": sweep, "layout": "data-parallel attention stand-in, expert-parallel MoE",
@@ -584,6 +611,9 @@ def main():
     ap.add_argument("--impl", default="ck", choices=["ck", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub", action="store_true", help="skip the other configurations' sub-benchmarks")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: the expert-parallel exchange over NVLink peer memory (device-driven, no host "
+                         "wait) or over NCCL all-to-alls")
     ap.add_argument("--shard", type=int, default=1,
                     help="run one GPU's share of an N-way expert-parallel layer on one GPU (256/N experts, "
                          "8192/N tokens): the small case a profiler capture uses")
@@ -599,6 +629,7 @@ def main():
     import torch
     import torch.distributed as dist
     from coherence_kernel_b200 import _lib, workloads
+    from coherence_kernel_b200.ep_peer import PeerExpertParallelMoE
     from coherence_kernel_b200.moe import ExpertParallelMoE, MoELayer
 
     torch.cuda.set_device(local)
@@ -625,7 +656,8 @@ def main():
     if world == 1:
         layer = MoELayer(spec, wg, wu, wd, sg, su, sd, router, bias, max_tokens=T)
     else:
-        layer = ExpertParallelMoE(spec, wg, wu, wd, sg, su, sd, router, bias, max_tokens=T)
+        ep_cls = PeerExpertParallelMoE if args.exchange == "peer" else ExpertParallelMoE
+        layer = ep_cls(spec, wg, wu, wd, sg, su, sd, router, bias, max_tokens=T)
     out = torch.empty((T, spec.hidden), dtype=torch.bfloat16, device=dev)
     ids = torch.empty((T, spec.nsel), dtype=torch.int32, device=dev)
     wts = torch.empty((T, spec.nsel), dtype=torch.float32, device=dev)
@@ -718,7 +750,8 @@ def main():
         label = {"permute": "plan", "shared": "shared_launch", "experts": "pair_order"}
         phases = {label.get(k, k): round(float(v), 4) for (b, k), v in zip(names, vec.tolist())}
         # the dominant kernel: the receiver's grouped gate/up GEMM over the (row, slot) pairs it received
-        pairs = torch.tensor([float(layer.last_recv_pairs)], dtype=torch.float64, device=dev)
+        npairs = layer.recv_pairs() if args.exchange == "peer" else layer.last_recv_pairs
+        pairs = torch.tensor([float(npairs)], dtype=torch.float64, device=dev)
         gu_ms = float(mine[5])
         ach_local = 2.0 * float(pairs) * 2 * spec.inter * spec.hidden / (gu_ms / 1e3) / 1e12
         fr = torch.tensor([ach_local / tc_burst], dtype=torch.float64, device=dev)
@@ -811,7 +844,9 @@ def main():
         if parity_ok and not args.no_sub:
             del layer, wg, wu, wd, o_p
             torch.cuda.empty_cache()
-            subs = {"decode_sweep_ep": decode_sweep_ep(torch, dist, ExpertParallelMoE, spec, w, experts, rank,
+            if args.exchange == "peer":
+                layer.close()
+            subs = {"decode_sweep_ep": decode_sweep_ep(torch, dist, ep_cls, spec, w, experts, rank,
                                                        world, dev, hbm, wfull)}
     if rank == 0:
         cpu = None
@@ -827,7 +862,10 @@ def main():
         # exchange (1) and gathers the dispatch rows (1) in place of the source permute, regroups on
         # the receiver (permute 3), restores the pair order (1), and runs the shared expert's token
         # tiles + 2 GEMMs per shared expert on a side stream
-        launches_per_step = 13 if world == 1 else 16 + 1 + 2 * spec.n_shared
+        # over peer memory: begin, route 7, plan, dispatch, signal, wait, regroup 3, GEMM 2, return,
+        # signal, wait, combine, + the shared expert's token tiles and 2 GEMMs per shared expert
+        launches_per_step = (13 if world == 1 else 16 + 1 + 2 * spec.n_shared if args.exchange == "nccl"
+                             else 21 + 1 + 2 * spec.n_shared)
         line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",

@@ -77,6 +77,17 @@ SIGNATURES = {
     "ck_gather_rows": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_ep_dispatch_plan": (_i32, [_p, _p, _u32, _u32, _u32, _u32, _p, _p, _p, _p, _p, _p]),
     "ck_wait_selftest": (_i32, [_u64, _p, _p, _p]),
+    "ck_ep_arena_alloc": (_i32, [_sz, _p]),
+    "ck_ep_arena_free": (_i32, [_p]),
+    "ck_ipc_get_handle": (_i32, [_p, _p]),
+    "ck_ipc_open_handle": (_i32, [_p, _p]),
+    "ck_ipc_close": (_i32, [_p]),
+    "ck_ep_peer_status": (_i32, [_p, _p]),
+    "ck_ep_peer_begin": (_i32, [_p, _p]),
+    "ck_ep_peer_dispatch": (_i32, [_p, _p, _p, _p, _p, _u32, _p]),
+    "ck_ep_peer_signal": (_i32, [_p, _i32, _p]),
+    "ck_ep_peer_wait": (_i32, [_p, _i32, _u64, _p]),
+    "ck_ep_peer_return": (_i32, [_p, _p, _p, _p, _p, _p]),
     "ck_decode_step_workspace_bytes": (_sz, [ctypes.POINTER(DecodeConfig)]),
     "ck_decode_step_create": (_p, [ctypes.POINTER(DecodeConfig)] + [_p] * 15 + [_sz]),
     "ck_decode_step_run": (_i32, [_p, _p, _p, _p, _p, _u32, _p]),

@@ -238,6 +238,47 @@ int ck_decode_step_replay(ck_decode_step *step, void *stream);
 int ck_decode_step_status(ck_decode_step *step, uint32_t ntok, void *stream);
 void ck_decode_step_destroy(ck_decode_step *step);
 
+/* ---- expert parallelism over NVLink peer memory (no counterpart in the reference, whose MoE runs on
+ * one device).  Each rank owns a zeroed device arena (ck_ep_arena_alloc) that its peers map with CUDA
+ * IPC (ck_ipc_get_handle / ck_ipc_open_handle).  ck_ep_peers names, for this rank, where its stores
+ * go in every peer's arena and where its own flags, step counter and error word are.  One forward:
+ * ck_ep_peer_begin (step += 1), ck_ep_dispatch_plan, ck_ep_peer_dispatch (every dispatch row into
+ * region `rank` of its destination; the unused rows of that region get expert -1), signal / wait
+ * (which = 0), the receiver's ck_moe_permute over world * cap rows and expert GEMMs,
+ * ck_ep_peer_return (every computed (row, slot) pair into its source's return buffer at row
+ * token * nsel + slot), signal / wait (which = 1), ck_moe_combine.  No host synchronization: the
+ * step count is a device value, so a forward can be captured in a CUDA graph.  Every wait is
+ * bounded; a timeout sets the error word (20 dispatch, 21 return) and the step's outputs are not
+ * valid.  All ranks must run the same sequence of forwards. */
+#define CK_EP_MAX_RANKS 32
+typedef struct {
+    uint32_t world, rank, cap, nsel, hidden, reserved;
+    void *recv_x[CK_EP_MAX_RANKS];                 /* peer d's region for this rank: bf16 [cap, hidden] */
+    int32_t *recv_ids[CK_EP_MAX_RANKS];            /* int32 [cap, nsel] local experts, -1 = none */
+    float *recv_w[CK_EP_MAX_RANKS];                /* fp32 [cap, nsel] route weights */
+    int32_t *recv_tok[CK_EP_MAX_RANKS];            /* int32 [cap] the source's token numbers */
+    void *ret_y[CK_EP_MAX_RANKS];                  /* peer s's return buffer, bf16 rows t * nsel + k */
+    unsigned long long *dflag[CK_EP_MAX_RANKS];    /* peer d's dispatch flag slot for this rank */
+    unsigned long long *rflag[CK_EP_MAX_RANKS];    /* peer s's return flag slot for this rank */
+    unsigned long long *my_dflags, *my_rflags;     /* this rank's flag arrays [world] */
+    unsigned long long *ctr;                       /* this rank's step counter */
+    int *err;                                      /* this rank's error word */
+} ck_ep_peers;
+int ck_ep_arena_alloc(size_t bytes, void **dev_ptr_out);
+int ck_ep_arena_free(void *dev_ptr);
+int ck_ipc_get_handle(const void *dev_ptr, void *handle_out /* 64 bytes */);
+int ck_ipc_open_handle(const void *handle /* 64 bytes */, void **dev_ptr_out);
+int ck_ipc_close(void *dev_ptr);
+int ck_ep_peer_begin(const ck_ep_peers *peers, void *stream);
+/* synchronizes; CK_ETIMEOUT when a wait (or an expert GEMM wait) of this rank gave up */
+int ck_ep_peer_status(const ck_ep_peers *peers, void *stream);
+int ck_ep_peer_dispatch(const ck_ep_peers *peers, const void *x_bf16_dev, const int32_t *send_tok_dev,
+                        const int32_t *meta_dev, const int64_t *sizes_dev, uint32_t ntok, void *stream);
+int ck_ep_peer_signal(const ck_ep_peers *peers, int which, void *stream);
+int ck_ep_peer_wait(const ck_ep_peers *peers, int which, uint64_t limit_ns, void *stream);
+int ck_ep_peer_return(const ck_ep_peers *peers, const void *y2_bf16_dev, const int32_t *pair_pos2_dev,
+                      const int32_t *ids_own_dev, const int32_t *tok_own_dev, void *stream);
+
 /* Failure-path self-test (no counterpart in the reference).  Runs the library's bounded device wait
  * on an mbarrier that nothing ever arrives on, with a time limit of limit_ns (1 ns .. 2 s): the wait
  * gives up, writes code 77 to *err_dev (which the caller zeroes first) and the time it waited to

@@ -1,4 +1,4 @@
-"""Expert parallelism over NCCL on two and four GPUs: the expert-parallel layer's output, ids and
+"""Expert parallelism on two and four GPUs, over NCCL collectives and over NVLink peer memory: the expert-parallel layer's output, ids and
 weights equal the single-GPU layer's bit for bit (each token row is computed by the same kernels in
 the same K order whichever tile it lands in, and the combine keeps the reference's order).  The
 decode-sized cases (64 tokens in all) take the few-token grouped matvec on both sides.
@@ -29,12 +29,13 @@ def _free_port():
     return port
 
 
-def _rank(rank, world, port, name, NTOK, q):
+def _rank(rank, world, port, name, NTOK, transport, q):
     import datetime
 
     import torch.distributed as dist
 
     from coherence_kernel_b200 import workloads
+    from coherence_kernel_b200.ep_peer import PeerExpertParallelMoE
     from coherence_kernel_b200.moe import ExpertParallelMoE, MoELayer, MoeSpec
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -50,7 +51,8 @@ def _rank(rank, world, port, name, NTOK, q):
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
         T = NTOK // world
         x = t(w["x"][rank * T:(rank + 1) * T].view(np.int16))
-        lay = ExpertParallelMoE(spec, t(w["gate"]), t(w["up"]), t(w["down"]), t(w["s_gate"]), t(w["s_up"]),
+        cls = PeerExpertParallelMoE if transport == "peer" else ExpertParallelMoE
+        lay = cls(spec, t(w["gate"]), t(w["up"]), t(w["down"]), t(w["s_gate"]), t(w["s_up"]),
                                 t(w["s_down"]), t(w["router"]), t(w["bias"]), max_tokens=T)
         out, ids, wts, _ = lay(x)
         lay.check()
@@ -69,7 +71,14 @@ def _rank(rank, world, port, name, NTOK, q):
             ref.status(NTOK)
             same = (torch.equal(torch.cat(outs).view(torch.int16), rout.view(torch.int16)) and
                     torch.equal(torch.cat(idss), rids) and torch.equal(torch.cat(wtss), rwts))
-            q.put(("ok" if same else "differs", lay.last_recv_rows))
+            q.put(("ok" if same else "differs", transport))
+        if transport == "peer":
+            # a second forward over the same buffers (the barriers' step counters move on)
+            dist.barrier()
+            out2, ids2, _, _ = lay(x)
+            lay.check()
+            assert torch.equal(out2.view(torch.int16), out.view(torch.int16)) and torch.equal(ids2, ids)
+            lay.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
@@ -77,16 +86,17 @@ def _rank(rank, world, port, name, NTOK, q):
         raise
 
 
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
 @pytest.mark.parametrize("name,world,ntok", [("dsv4", 2, 512), ("softmax", 2, 512), ("dsv4", 4, 512),
                                              ("softmax", 4, 768), ("dsv4", 2, 64), ("dsv4", 4, 64)])
-def test_expert_parallel_matches_single_gpu(name, world, ntok):
+def test_expert_parallel_matches_single_gpu(name, world, ntok, transport):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, name, ntok, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, name, ntok, transport, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
