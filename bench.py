@@ -842,10 +842,10 @@ def main():
         layer.check()
         parity, wfull, parity_ok = ep_parity(torch, dist, spec, w, experts, i_p, w_p, o_p, rank, world, dev)
         if parity_ok and not args.no_sub:
-            del layer, wg, wu, wd, o_p
-            torch.cuda.empty_cache()
             if args.exchange == "peer":
                 layer.close()
+            del layer, wg, wu, wd, o_p
+            torch.cuda.empty_cache()
             subs = {"decode_sweep_ep": decode_sweep_ep(torch, dist, ep_cls, spec, w, experts, rank,
                                                        world, dev, hbm, wfull)}
     if rank == 0:
