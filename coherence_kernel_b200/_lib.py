@@ -88,6 +88,11 @@ SIGNATURES = {
     "ck_ep_peer_signal": (_i32, [_p, _i32, _p]),
     "ck_ep_peer_wait": (_i32, [_p, _i32, _u64, _p]),
     "ck_ep_peer_return": (_i32, [_p, _p, _p, _p, _p, _p]),
+    "ck_ep_group_create": (_p, [ctypes.POINTER(MoeConfig), _u32, _p, _u32]),
+    "ck_ep_group_load": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "ck_ep_group_forward": (_i32, [_p, _p, _u32, _p, _p, _p, _p, _p]),
+    "ck_ep_group_status": (_i32, [_p]),
+    "ck_ep_group_destroy": (None, [_p]),
     "ck_decode_step_workspace_bytes": (_sz, [ctypes.POINTER(DecodeConfig)]),
     "ck_decode_step_create": (_p, [ctypes.POINTER(DecodeConfig)] + [_p] * 15 + [_sz]),
     "ck_decode_step_run": (_i32, [_p, _p, _p, _p, _p, _u32, _p]),

@@ -337,6 +337,63 @@ int L_moe_layer(const Call &k, std::string &w) {
                              (const float *)k.b[8], (int32_t *)k.b[9], (float *)k.b[10], (int32_t *)k.b[11], k.b[12],
                              k.b[13], k.blen[13], k.s);
 }
+// ck_moe_layer_ep_bf16: the same 14 buffers and 11 constants as ck_moe_layer_bf16, then `world`:
+// the layer over GPUs carrier_dev .. carrier_dev + world - 1 (modulo the device count) as one
+// expert-parallel group.  The group is built at the first dispatch for a set of weight buffers
+// (experts shared out to the members once) and kept for later dispatches with the same weights,
+// configuration and width; the workspace buffer is not used.
+struct EpKey {
+    const void *wg, *wu, *wd;
+    unsigned world, ntok_cap;
+    ck_moe_config cfg;
+};
+struct EpEntry {
+    EpKey key;
+    ck_ep_group *g;
+};
+std::vector<EpEntry> g_ep_groups;
+int L_moe_layer_ep(const Call &k, std::string &w) {
+    ck_moe_config c = {k.c[0], k.c[1], k.c[2], k.c[3], k.c[4], k.c[5], k.c[6], k.c[7], f32_of(k.c[8]), f32_of(k.c[9])};
+    const unsigned long long T = k.c[10], H = c.hidden, I = c.inter, E = c.n_experts, NS = c.n_shared, K = c.nsel;
+    const unsigned world = k.c[11];
+    int ndev = 0, dev = 0;
+    cudaGetDeviceCount(&ndev);
+    cudaGetDevice(&dev);
+    if (world == 0 || world > CK_EP_MAX_RANKS || (int)world > ndev || E % world) {
+        w = "ck_moe_layer_ep_bf16 needs 1 <= world <= the device count with the experts dividing evenly";
+        return CK_ERR_SHAPE;
+    }
+    if (ck_moe_workspace_bytes(&c, 1) == 0) { w = "unsupported MoE configuration"; return CK_ERR_SHAPE; }
+    const unsigned long long mb = q4kb(I * H);
+    if (!need(k, 0, T * H * 2, w, "x") || !need(k, 1, E * mb, w, "w_gate") || !need(k, 2, E * mb, w, "w_up") ||
+        !need(k, 3, E * mb, w, "w_down") || !need(k, 4, NS * mb, w, "s_gate") || !need(k, 5, NS * mb, w, "s_up") ||
+        !need(k, 6, NS * mb, w, "s_down") || !need(k, 7, E * H * 4, w, "router") ||
+        !need(k, 8, c.mode == 4 ? E * 4 : 0, w, "bias") || !need(k, 9, T * K * 4, w, "ids") ||
+        !need(k, 10, T * K * 4, w, "wts") || !need(k, 11, E * 4, w, "counts") || !need(k, 12, T * H * 2, w, "out"))
+        return CK_ERR_ARG;
+    const unsigned cap = (unsigned)((T + world - 1) / world);
+    ck_ep_group *grp = nullptr;
+    for (auto &e : g_ep_groups)
+        if (e.key.wg == k.b[1] && e.key.wu == k.b[2] && e.key.wd == k.b[3] && e.key.world == world &&
+            e.key.ntok_cap >= cap && !memcmp(&e.key.cfg, &c, sizeof(c)))
+            grp = e.g;
+    if (!grp) {
+        int devs[CK_EP_MAX_RANKS];
+        for (unsigned d = 0; d < world; ++d) devs[d] = (dev + (int)d) % ndev;
+        grp = ck_ep_group_create(&c, world, devs, cap);
+        if (!grp) { w = "expert-parallel group could not be built (peer access or memory)"; return CK_ERR_ARG; }
+        const int rc = ck_ep_group_load(grp, k.b[1], k.b[2], k.b[3], k.b[4], k.b[5], k.b[6], (const float *)k.b[7],
+                                        (const float *)k.b[8]);
+        if (rc) {
+            ck_ep_group_destroy(grp);
+            w = "expert-parallel group could not load the weights";
+            return rc;
+        }
+        g_ep_groups.push_back({{k.b[1], k.b[2], k.b[3], world, cap, c}, grp});
+    }
+    return ck_ep_group_forward(grp, k.b[0], (uint32_t)T, (int32_t *)k.b[9], (float *)k.b[10], (int32_t *)k.b[11],
+                               k.b[12], k.s);
+}
 // ck_q4k_gemm_bf16: buffers qb x y workspace; constants rows cols ntok
 int L_q4k_gemm(const Call &k, std::string &w) {
     const unsigned long long rows = k.c[0], cols = k.c[1], ntok = k.c[2];
@@ -382,6 +439,7 @@ const Entry REGISTRY[] = {
     {"form_dsv4_swiglu_experts", 4, 3, L_swiglu_experts},
     {"form_dsv4_moe_reduce", 2, 2, L_moe_reduce},
     {"ck_moe_layer_bf16", 14, 11, L_moe_layer},
+    {"ck_moe_layer_ep_bf16", 14, 12, L_moe_layer_ep},
     {"ck_q4k_gemm_bf16", 4, 3, L_q4k_gemm},
 };
 constexpr int NREG = sizeof(REGISTRY) / sizeof(REGISTRY[0]);

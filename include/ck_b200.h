@@ -279,6 +279,25 @@ int ck_ep_peer_wait(const ck_ep_peers *peers, int which, uint64_t limit_ns, void
 int ck_ep_peer_return(const ck_ep_peers *peers, const void *y2_bf16_dev, const int32_t *pair_pos2_dev,
                       const int32_t *ids_own_dev, const int32_t *tok_own_dev, void *stream);
 
+/* ---- one process, several GPUs (no counterpart in the reference): the same expert-parallel layer for
+ * a host that owns the box's GPUs itself (the reference runtime with this carrier is one).  A group
+ * of `world` member GPUs (devices[0] first) with peer access between them; every member holds
+ * E / world experts, replicas of the router and shared expert(s), and room for `cap` tokens.
+ * ck_ep_group_load copies the member shares from full weight arrays anywhere in device memory.
+ * ck_ep_group_forward splits ntok <= world * cap tokens evenly over the members, runs the layer
+ * over peer memory and gathers ids, weights, per-expert counts and out back; x / ids / wts /
+ * counts / out live on devices[0] and `stream` is a stream of devices[0].  The host never waits;
+ * ck_ep_group_status synchronizes and answers CK_ETIMEOUT when a member's device wait gave up. */
+typedef struct ck_ep_group ck_ep_group;
+ck_ep_group *ck_ep_group_create(const ck_moe_config *cfg, uint32_t world, const int *devices, uint32_t cap);
+int ck_ep_group_load(ck_ep_group *group, const void *w_gate_dev, const void *w_up_dev, const void *w_down_dev,
+                     const void *s_gate_dev, const void *s_up_dev, const void *s_down_dev, const float *router_w_dev,
+                     const float *bias_dev);
+int ck_ep_group_forward(ck_ep_group *group, const void *x_bf16_dev, uint32_t ntok, int32_t *ids_dev, float *wts_dev,
+                        int32_t *counts_dev, void *out_bf16_dev, void *stream);
+int ck_ep_group_status(ck_ep_group *group);
+void ck_ep_group_destroy(ck_ep_group *group);
+
 /* Failure-path self-test (no counterpart in the reference).  Runs the library's bounded device wait
  * on an mbarrier that nothing ever arrives on, with a time limit of limit_ns (1 ns .. 2 s): the wait
  * gives up, writes code 77 to *err_dev (which the caller zeroes first) and the time it waited to
