@@ -398,8 +398,15 @@ def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, 
     dense_b = R * C // 256 * 144
     sweep = {}
     parity = None
+    cal = lay
     for bsz in (1, 4, 16, 64):
-        # rank r's batch: tokens [r*b, (r+1)*b) of the seeded stream
+        # rank r's batch: tokens [r*b, (r+1)*b) of the seeded stream; the layer is sized for the
+        # batch (a decode server sizes its exchange for its decode batch, not its prefill)
+        if hasattr(cal, "close"):
+            if lay is not cal:
+                lay.close()
+            lay = layer_cls(spec, cal.w[0], cal.w[1], cal.w[2], cal.s[0], cal.s[1], cal.s[2], cal.router_w,
+                            cal.bias, max_tokens=bsz)
         xb = t(xall[rank * bsz:(rank + 1) * bsz].view(np.int16))
         o = torch.empty((bsz, spec.hidden), dtype=torch.bfloat16, device=dev)
 
@@ -467,7 +474,9 @@ def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, 
                 raise SystemExit("decode sweep parity failed")
     if hasattr(lay, "close"):
         lay.close()
-    del lay, q4
+        if lay is not cal:
+            cal.close()
+    del lay, cal, q4
     torch.cuda.synchronize()
     return {"steps": sweep, "layout": "data-parallel attention stand-in, expert-parallel MoE",
             "zipf": {"c": round(zipf_c, 3), "measured_slope": round(zipf_slope, 3), "tokens": ncal * world},
