@@ -372,6 +372,123 @@ __global__ void __launch_bounds__(256) k_exact_select(const double *__restrict__
     }
 }
 
+// The middle tier of a large batch's route: fp64 logits of the flagged tokens accurate to a few
+// roundings of sum|w x|, without the reference's sequential fold.  The tiles are those of
+// k_exact_logits, but every thread keeps eight interleaved partial sums per token (column j feeds
+// partial j mod 8) of the exact fp64 products, so a chain is hidden / 8 terms long and a thread has
+// 32 independent chains in flight; the eight are summed in a fixed order at the end (deterministic).
+// The error against the exact dot is at most (hidden / 8 + 3) * 2^-53 * sum|w x|, and the
+// reference's own fold differs from it by at most hidden * 2^-53 * sum|w x|: the fp64 selection that
+// follows flags a token for the sequential fold only when its margin is below 16 * 2^-40 of its
+// largest sum|w x| -- in practice only exact ties.  sum|w x| (fp32) is written beside each logit.
+// Block 0 also clears the count of the list that selection fills.
+__global__ void __launch_bounds__(256) k_accurate_logits(const uint16_t *__restrict__ x, const float *__restrict__ W,
+                                                         const uint32_t *__restrict__ flag_list,
+                                                         const uint32_t *__restrict__ flag_count,
+                                                         double *__restrict__ out, float *__restrict__ out_abs,
+                                                         uint32_t *__restrict__ next_count, uint32_t ne,
+                                                         uint32_t hidden) {
+    grid_dep_trigger_small();
+    grid_dep_wait();
+    if (blockIdx.x == 0 && threadIdx.x == 0) *next_count = 0u;
+    __shared__ float wt[2][XL_EXP][XL_J + 1];
+    __shared__ __align__(16) float xt[2][XL_TOK][XL_J];
+    const uint32_t nflag = *flag_count;
+    const int tid = threadIdx.x;
+    const int el = tid & (XL_EXP - 1);
+    const int q = tid / XL_EXP;
+    const uint32_t ntg = (nflag + XL_TOK - 1) / XL_TOK, neg = (ne + XL_EXP - 1) / XL_EXP;
+    const int ntile = (int)(hidden / XL_J);
+    constexpr int WPT = XL_EXP * XL_J / 256;
+    constexpr int XPT = XL_TOK * XL_J / 256;
+    constexpr int NP = 8;
+    for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
+        const uint32_t f0 = (item / neg) * XL_TOK, e0 = (item % neg) * XL_EXP;
+        const float *wrow[WPT];
+        const uint16_t *xrow[XPT];
+#pragma unroll
+        for (int k = 0; k < WPT; ++k) {
+            const uint32_t e = e0 + (uint32_t)((tid + 256 * k) / XL_J);
+            wrow[k] = e < ne ? W + (size_t)e * hidden : nullptr;
+        }
+#pragma unroll
+        for (int k = 0; k < XPT; ++k) {
+            const uint32_t f = min(f0 + (uint32_t)((tid + 256 * k) / XL_J), nflag - 1);
+            xrow[k] = x + (size_t)flag_list[f] * hidden;
+        }
+        const int jc = tid % XL_J;
+        float wv[WPT];
+        uint16_t xv[XPT];
+        auto fetch = [&](int tile) {
+            const int j0 = XL_J * tile;
+#pragma unroll
+            for (int k = 0; k < WPT; ++k) wv[k] = wrow[k] ? __ldg(wrow[k] + j0 + jc) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < XPT; ++k) xv[k] = __ldg(xrow[k] + j0 + jc);
+        };
+        auto stage = [&](int b) {
+#pragma unroll
+            for (int k = 0; k < WPT; ++k) wt[b][(tid + 256 * k) / XL_J][jc] = wv[k];
+#pragma unroll
+            for (int k = 0; k < XPT; ++k) xt[b][(tid + 256 * k) / XL_J][jc] = bf16_bits_to_float(xv[k]);
+        };
+        fetch(0);
+        stage(0);
+        __syncthreads();
+        double a[XL_TPT][NP];
+        float ab[XL_TPT];
+#pragma unroll
+        for (int t = 0; t < XL_TPT; ++t) {
+            ab[t] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NP; ++i) a[t][i] = 0.0;
+        }
+        for (int tile = 0; tile < ntile; ++tile) {
+            const int b = tile & 1;
+            if (tile + 1 < ntile) fetch(tile + 1);
+#pragma unroll
+            for (int j = 0; j < XL_J; ++j) {
+                const float w = wt[b][el][j];
+                const double wd = (double)w;
+#pragma unroll
+                for (int t = 0; t < XL_TPT; ++t) {
+                    const float xf = xt[b][XL_TPT * q + t][j];
+                    a[t][j % NP] = __fma_rn(wd, (double)xf, a[t][j % NP]);  // the product is exact in fp64
+                    ab[t] = fmaf(fabsf(w), fabsf(xf), ab[t]);
+                }
+            }
+            if (tile + 1 < ntile) stage(b ^ 1);
+            __syncthreads();
+        }
+        const uint32_t e = e0 + el;
+        if (e < ne) {
+#pragma unroll
+            for (int t = 0; t < XL_TPT; ++t) {
+                const uint32_t f = f0 + XL_TPT * q + t;
+                if (f < nflag) {
+                    const double s = ((a[t][0] + a[t][1]) + (a[t][2] + a[t][3])) +
+                                     ((a[t][4] + a[t][5]) + (a[t][6] + a[t][7]));
+                    out[(size_t)f * ne + e] = s;
+                    out_abs[(size_t)f * ne + e] = ab[t] * 1.0001f;  // covers the fp32 sum's own rounding
+                }
+            }
+        }
+    }
+}
+
+int launch_accurate_logits(const uint16_t *x, const float *w, const uint32_t *flag_list, const uint32_t *flag_count,
+                           double *out, float *out_abs, uint32_t *next_count, uint32_t ne, uint32_t hidden,
+                           cudaStream_t s) {
+    if (ne > 256 || hidden % XL_J != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+        return CK_ERR_SHAPE;
+    int dev = 0, nsm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const cudaError_t e = launch_pdl(k_accurate_logits, dim3(nsm * 2), dim3(256), 0, s, x, w, flag_list, flag_count,
+                                     out, out_abs, next_count, ne, hidden);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
 int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int32_t *ids, float *wts,
                        const uint32_t *flag_list, const uint32_t *flag_count, double *scratch,
                        const RouteParams &p, cudaStream_t s) {
