@@ -12,6 +12,20 @@
 
 namespace ck {
 
+// Kernel attributes such as the dynamic shared-memory limit belong to a device, so a process that
+// drives several GPUs sets them on each: one bit per device (up to 64) of a call site's `done` word.
+inline bool attr_pending(unsigned long long done) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return !((done >> (dev & 63)) & 1ull);
+}
+inline void attr_mark(unsigned long long &done) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    done |= 1ull << (dev & 63);
+}
+
+
 // ----------------------------------------------------------------------------- GGUF fields
 // block_q8_0: f16 d @0, int8 qs[32] @2 (34 bytes); block_q4_K: f16 d @0, f16 dmin @2,
 // scales[12] @4, qs[128] @16 (144 bytes).  The f16 decode is IEEE half -> float (exact).

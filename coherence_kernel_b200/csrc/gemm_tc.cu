@@ -593,12 +593,12 @@ static int make_packed_map(CUtensorMap *m, const void *base, uint32_t count, uin
 template <int DUAL, int DENSE, int PT>
 static int launch_t(const GemmParams &p, cudaStream_t s) {
     using C = Cfg<DUAL, DENSE, PT>;
-    static bool attr = false;
-    if (!attr) {
+    static unsigned long long attr = 0;
+    if (attr_pending(attr)) {
         cudaError_t e =
             cudaFuncSetAttribute(k_gemm_q4k<DUAL, DENSE, PT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return (int)e;
-        attr = true;
+        attr_mark(attr);
     }
     CUtensorMap mx, ma;
     int rc = make_map(&mx, p.x, p.x_rows, DENSE && p.kx ? p.kx : p.K, DENSE ? C::DENSE_TILE : B_BOX);

@@ -358,12 +358,12 @@ uint32_t pow2_ceil(uint32_t v) {
 
 template <int KIND>
 cudaError_t launch_kind(const cudaLaunchConfig_t &cfg, const uint8_t *qb, const float *x, float *y, const Geo &g) {
-    static bool set = false;
-    if (!set) {
+    static unsigned long long set = 0;
+    if (attr_pending(set)) {
         const cudaError_t e =
             cudaFuncSetAttribute(k_gemv_stream<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
         if (e != cudaSuccess) return e;
-        set = true;
+        attr_mark(set);
     }
     return cudaLaunchKernelEx(&cfg, k_gemv_stream<KIND>, qb, x, y, g);
 }

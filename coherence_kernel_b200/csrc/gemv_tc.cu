@@ -402,12 +402,12 @@ static int launch(const uint8_t *qb, const float *x, float *y, uint32_t rows, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return CK_ERR_ARG;
     const uint32_t tiles = (rows + trows - 1) / trows;
-    static bool set = false;
-    if (!set) {
+    static unsigned long long set = 0;
+    if (attr_pending(set)) {
         cudaError_t e = cudaFuncSetAttribute(gtc::k_gemv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, gtc::SMEM);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(gtc::k_gemv_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return (int)e;
-        set = true;
+        attr_mark(set);
     }
     gtc::Params p = {x, y, rows, cols, nsb, csize, trows};
     cudaLaunchAttribute attr[2];

@@ -471,11 +471,11 @@ __global__ void __launch_bounds__(NTHR, 1)
 
 template <int NN>
 static int launch_nn(const CUtensorMap (&maps)[4], const Params &prm, uint32_t grid, cudaStream_t s) {
-    static bool set = false;
-    if (!set) {
+    static unsigned long long set = 0;
+    if (attr_pending(set)) {
         const cudaError_t e = cudaFuncSetAttribute(k_moe_gemv<NN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
         if (e != cudaSuccess) return (int)e;
-        set = true;
+        attr_mark(set);
     }
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

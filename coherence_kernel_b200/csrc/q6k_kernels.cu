@@ -315,14 +315,14 @@ int launch_q6k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows
     const bool stream = q6::plan(rows, cols, g) && (reinterpret_cast<uintptr_t>(qb) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (cols * 4) % 16 == 0;
     if (stream) {
-        static bool set = false;
-        if (!set) {
+        static unsigned long long set = 0;
+        if (attr_pending(set)) {
             for (auto fn : {q6::k_q6k_stream<1>, q6::k_q6k_stream<2>, q6::k_q6k_stream<4>}) {
                 const cudaError_t e =
                     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, q6::SMEM_MAX);
                 if (e != cudaSuccess) return (int)e;
             }
-            set = true;
+            attr_mark(set);
         }
         auto fn = g.upt == 1 ? q6::k_q6k_stream<1> : g.upt == 2 ? q6::k_q6k_stream<2> : q6::k_q6k_stream<4>;
         int dev = 0, nsm = 0;

@@ -312,10 +312,12 @@ int launch_q80_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows
         return launch_gemv_stream(8, qb, x, y, rows, cols, s);
     } else if (cols % 256 == 0 && (size_t)cols / 32 * Q80_BYTES * 8 <= 200 * 1024) {
         size_t smem = (size_t)cols / 32 * Q80_BYTES * 8;
-        static bool attr_set = false;
-        if (!attr_set) {
-            cudaFuncSetAttribute(k_q80_matvec_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            attr_set = true;
+        static unsigned long long attr_set = 0;
+        if (attr_pending(attr_set)) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(k_q80_matvec_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            if (e != cudaSuccess) return (int)e;
+            attr_mark(attr_set);
         }
         k_q80_matvec_fast<<<nblk(rows, 8), 256, smem, s>>>(qb, x, y, rows, cols);
     } else {

@@ -496,12 +496,12 @@ int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    static bool few_attr = false;
-    if (!few_attr) {
+    static unsigned long long few_attr = 0;
+    if (attr_pending(few_attr)) {
         const cudaError_t e = cudaFuncSetAttribute(k_exact_logits_few, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)(XF_WARPS * sizeof(XfRing)));
         if (e != cudaSuccess) return (int)e;
-        few_attr = true;
+        attr_mark(few_attr);
     }
     // both forms are launched; each returns at once unless the flagged count is its own
     cudaError_t e = launch_pdl(k_exact_logits_few, dim3(2 * nsm), dim3(XF_WARPS * 32), XF_WARPS * sizeof(XfRing), s, x,
