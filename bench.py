@@ -866,15 +866,15 @@ def main():
                 cpu["port"] = port
             else:
                 cpu = port
-        # our kernels per step: route 7 (split, tiles, logits GEMM, select, the two forms of the
-        # exact logits, exact select), permute 3, GEMM 2, combine 1; expert parallel plans the
+        # our kernels per step: route 8 (split, tiles, logits GEMM, select, the router in fp64, the
+        # two forms of the exact logits, exact select), permute 3, GEMM 2, combine 1; expert parallel plans the
         # exchange (1) and gathers the dispatch rows (1) in place of the source permute, regroups on
         # the receiver (permute 3), restores the pair order (1), and runs the shared expert's token
         # tiles + 2 GEMMs per shared expert on a side stream
-        # over peer memory: begin, route 7, plan, dispatch, signal, wait, regroup 3, GEMM 2, return,
+        # over peer memory: begin, route 8, plan, dispatch, signal, wait, regroup 3, GEMM 2, return,
         # signal, wait, combine, + the shared expert's token tiles and 2 GEMMs per shared expert
-        launches_per_step = (13 if world == 1 else 16 + 1 + 2 * spec.n_shared if args.exchange == "nccl"
-                             else 21 + 1 + 2 * spec.n_shared)
+        launches_per_step = (14 if world == 1 else 17 + 1 + 2 * spec.n_shared if args.exchange == "nccl"
+                             else 22 + 1 + 2 * spec.n_shared)
         line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",

@@ -63,6 +63,7 @@ SIGNATURES = {
     "ck_moe_layer_status": (_i32, [ctypes.POINTER(MoeConfig), _u32, _p, _p]),
     "ck_moe_route_workspace_bytes": (_sz, [ctypes.POINTER(MoeConfig), _u32]),
     "ck_moe_route": (_i32, [ctypes.POINTER(MoeConfig), _p, _u32, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "ck_router_exact_logits": (_i32, [_p, _p, _p, _p, _u32, _u32, _p, _p, _p]),
     "ck_moe_route_flagged": (_i32, [ctypes.POINTER(MoeConfig), _u32, _p, _p]),
     "ck_moe_permute_workspace_bytes": (_sz, [_u32, _u32, _u32]),
     "ck_moe_max_tiles": (_u32, [_u32, _u32, _u32, _u32]),

@@ -32,9 +32,9 @@ struct RouteWs {
     int32_t *ntiles;
     int *err;
     uint32_t *flags;
-    uint32_t *flags2;  // large batches: the tokens still within the accurate logits' error (count first)
     double *exact;  // fp64 logits of the flagged tokens (and of every token on the decode-batch path)
     float *sabs;    // sum |w x| per logit on the decode-batch path
+    double *w64;    // the router in fp64, for the exact re-route
     size_t total;
 };
 RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
@@ -47,9 +47,9 @@ RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
     w.ntiles = (int32_t *)take(4);
     w.err = (int *)take(4);
     w.flags = (uint32_t *)take(((size_t)ntok + 1) * 4);
-    w.flags2 = (uint32_t *)take(((size_t)ntok + 1) * 4);
     w.exact = (double *)take((size_t)ntok * c->n_experts * 8);
     w.sabs = (float *)take((size_t)ntok * c->n_experts * 4);
+    w.w64 = (double *)take((size_t)c->n_experts * c->hidden * 8);
     w.total = o;
     return w;
 }
@@ -348,24 +348,11 @@ int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const flo
         if (rc) return fail(rc, "ck_moe_route logits");
         rc = ck::launch_route_select(logits, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
         if (rc) return fail(rc, "ck_moe_route select");
-        // the tokens within tau of a decision: fp64 logits accurate to a few roundings of sum|w x|
-        // (eight interleaved partial sums of the exact products, no sequential fold), selected again
-        // in fp64; only those still within that accuracy take the reference's sequential fold
-        rc = ck::launch_accurate_logits((const uint16_t *)x, rw, w.flags + 1, w.flags, w.exact, w.sabs, w.flags2,
-                                        c->n_experts, c->hidden, S(s));
-        if (rc) return fail(rc, "ck_moe_route accurate logits");
-        ck::RouteParams p2 = p;
-        p2.tau = 0.0f;
-        rc = ck::launch_route_select_d_subset(w.exact, w.sabs, bias, ids, wts, w.flags + 1, w.flags, w.flags2 + 1,
-                                              w.flags2, p2, S(s));
-        if (rc) return fail(rc, "ck_moe_route accurate select");
-        rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, w.flags2 + 1, w.flags2, w.exact, p,
-                                    S(s));
-        return fail(rc, "ck_moe_route exact");
     } else {
         return fail(rc, "ck_moe_route logits");
     }
-    rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, w.flags + 1, w.flags, w.exact, p, S(s));
+    rc = ck::launch_route_exact((const uint16_t *)x, rw, bias, ids, wts, w.flags + 1, w.flags, w.exact, w.w64, p,
+                                S(s));
     return fail(rc, "ck_moe_route exact");
 }
 
@@ -378,6 +365,15 @@ int ck_moe_route_flagged(const ck_moe_config *c, uint32_t ntok, const void *ws, 
     if (r == cudaSuccess) r = cudaStreamSynchronize(S(s));
     if (r != cudaSuccess) return fail((int)r, "ck_moe_route_flagged");
     return (int)n;
+}
+
+// The reference's router logits (tb-dot's right fold in fp64) of the listed tokens.
+int ck_router_exact_logits(const void *x, const float *rw, const uint32_t *tokens, const uint32_t *count,
+                           uint32_t n_experts, uint32_t hidden, double *out, double *router_f64, void *s) {
+    if (!x || !rw || !tokens || !count || !out || !router_f64) return fail(CK_EARG, "ck_router_exact_logits");
+    return fail(ck::launch_exact_logits((const uint16_t *)x, rw, tokens, count, out, router_f64, n_experts, hidden,
+                                        S(s)),
+                "ck_router_exact_logits");
 }
 
 int ck_moe_permute(const int32_t *ids, const float *wts, const void *x, uint32_t ntok, uint32_t nsel,

@@ -64,15 +64,13 @@ int launch_route_select_d(const double *L, const float *sabs, const float *bias,
 int launch_route_select(const float *logits, const float *bias, int32_t *ids, float *wts, uint32_t *flag_list,
                         uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
 // scratch: fp64 [ntok, ne] (the exact logits of the flagged tokens)
-int launch_route_select_d_subset(const double *L, const float *sabs, const float *bias, int32_t *ids, float *wts,
-                                 const uint32_t *subset, const uint32_t *subset_count, uint32_t *flag_list,
-                                 uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
-int launch_accurate_logits(const uint16_t *x, const float *w, const uint32_t *flag_list, const uint32_t *flag_count,
-                           double *out, float *out_abs, uint32_t *next_count, uint32_t ne, uint32_t hidden,
-                           cudaStream_t s);
+// out fp64 [*flag_count, ne]: the right-fold logits of the listed tokens (at most 256 experts,
+// hidden % 32 == 0); w64: scratch for the router in fp64, ne * hidden doubles
+int launch_exact_logits(const uint16_t *x_bf16, const float *w, const uint32_t *flag_list, const uint32_t *flag_count,
+                        double *out, double *w64, uint32_t ne, uint32_t hidden, cudaStream_t s);
 int launch_route_exact(const uint16_t *x_bf16, const float *w, const float *bias, int32_t *ids, float *wts,
-                       const uint32_t *flag_list, const uint32_t *flag_count, double *scratch, const RouteParams &p,
-                       cudaStream_t s);
+                       const uint32_t *flag_list, const uint32_t *flag_count, double *scratch, double *w64,
+                       const RouteParams &p, cudaStream_t s);
 
 // The grouped GEMM's largest token tile: its accumulators (gate and up, or two buffers) and its
 // tensor-memory A stages share the 512 TMEM columns.  Every token-tile table is built with it.

@@ -12,10 +12,9 @@
 //   mode 3  mm-softmax (max, tn-exp, left-fold sum, * 1/sum) and mm-topk (moe-msl.fk:73-99)
 // Explicit round-to-nearest intrinsics keep the compiler from contracting a multiply and an add.
 //
-// Two kernels: k_exact_logits spreads (token, expert) right folds over the whole GPU (each fold is a
-// 7168-long dependent chain, so many chains must be in flight) -- tiled over 16 tokens x 64 experts
-// when more than 128 tokens are flagged, one chain per lane fed by a cp.async ring
-// (k_exact_logits_few) when at most 128 are; k_exact_select is one CTA per token.
+// The logits: k_exact_logits spreads (token, expert) right folds over the whole GPU -- tiled over
+// 16 tokens x 64 experts when more than 128 tokens are flagged, one chain per lane fed by a cp.async
+// ring (k_exact_logits_few) when at most 128 are; k_exact_select is one CTA per token.
 #include "ck_common.cuh"
 #include "ck_launch.h"
 
@@ -41,29 +40,51 @@ CK_DEV double ref_exp(double x) {
 }
 CK_DEV double ref_sigmoid(double x) { return __ddiv_rn(1.0, __dadd_rn(1.0, ref_exp(__dsub_rn(0.0, x)))); }
 
-constexpr int XL_TOK = 16;   // flagged tokens per work item
-constexpr int XL_EXP = 64;   // experts per work item
-constexpr int XL_J = 32;     // columns per shared-memory tile
-constexpr int XL_TPT = 4;    // tokens (independent fold chains) per thread
-
 // out[f * ne + e] = right fold of router row e with flagged token f's activations, fp64.
 // The product of an fp32 weight and a bf16 activation has at most 32 significant bits, so it is
-// exact in fp64 and fma(w, x, acc) rounds once exactly as acc + (w * x) does: one DFMA per term.
-// 256 threads = 64 experts x 4 token groups; each thread folds 4 tokens.  The W and x tiles are
-// converted to double once per tile into shared memory, double-buffered: the next tile's global
-// loads are in registers while the current tile is folded.
-// Few flagged tokens (a decode step): the tiled form below would leave most of the GPU idle and fold
-// padding, so each warp takes one (token, 32 experts) item and every lane one fold chain.  A chain
-// is a dependent sequence of DFMAs, so its inputs must arrive far ahead: each lane copies its
-// router row's next columns eight at a time (two 16-byte cp.async) into a per-warp ring of
-// XF_NB stages in shared memory, lane 0 copies the token's eight activations beside them, and the
-// chain consumes stage i while stages i+1 .. i+XF_NB-1 are in flight.  Same fold, same bits.
-constexpr uint32_t XL_FEW = 128;  // 8 items per token: one item per warp at two CTAs per SM
-constexpr int XF_NB = 24;       // ring stages per warp (8 columns each)
-constexpr int XF_WARPS = 4;     // warps per CTA in the few-token form
+// exact in fp64 and fma(w, x, acc) rounds once exactly as acc + (w * x) does: one DFMA per term,
+// j descending.  A fold is a dependent chain of `hidden` DFMAs (about 9 cycles a step), so many
+// chains must run at once and their operands must be in registers when the chain reaches them.
+// This GPU converts fp32 to fp64 at a quarter of its DFMA rate, so an operand shared by several
+// chains is converted once.
+//
+// Many flagged tokens (k_exact_logits): the router is first converted to fp64 (k_router_f64,
+// skipped otherwise).  A work item is 16 tokens x 64 experts on a CTA of four warps; warp q folds
+// tokens 4q .. 4q+3 and lane l experts l and l + 32, eight chains per thread.  Tiles of 32 columns
+// (the last tile first) arrive by cp.async in a ring of XT_NS stages; the router rows are read from
+// the ring with 16-byte loads at a 34-double pitch (conflict-free per quarter warp), the tile's
+// activations are converted into one of two fp64 buffers a tile ahead.  One CTA barrier per tile.
+// Few flagged tokens (a decode step, or a rank's share of a batch; k_exact_logits_few): a work
+// item is 4 tokens x 32 experts on a CTA of four warps, warp q folding token q, lane l expert l --
+// enough warps to fill the GPU, each folding one chain.  Stages of 16 columns go through a CTA-wide
+// cp.async ring of XF_NB stages: the 32 experts' fp32 row pieces (four threads to a row, so each
+// copy instruction moves whole lines; a thread per row would keep 32 scattered sectors in flight
+// per instruction and run into the SM's limit on outstanding requests) and the four tokens'
+// activations, converted to fp64 once, two stages ahead.  The router is shared by the item's four
+// tokens through the ring (one read of it from L2 per four tokens), and each lane converts its 16
+// router values of the next stage while it folds the current one (converting them once per CTA
+// into shared memory instead measured slower).  It is launched without programmatic dependent
+// launch: launched early, beside the kernels before it, its CTAs were placed so that up to 51
+// flagged tokens took twice the time that 65 did.
+constexpr int XL_J = 32;          // columns per tile
+constexpr int XT_TOK = 16;        // flagged tokens per work item
+constexpr int XT_EXP = 64;        // experts per work item
+constexpr int XT_NS = 6;          // cp.async ring stages
+constexpr int XT_THREADS = 128;
+constexpr int XT_WP = XL_J + 2;   // router row pitch in the ring, in doubles
+struct XtSmem {
+    double w[XT_NS][XT_EXP][XT_WP];     // router rows of the tile (fp64)
+    uint16_t x[XT_NS][XT_TOK][XL_J];    // activations of the tile, as copied
+    double xd[2][XT_TOK][XL_J];         // converted
+};
+constexpr uint32_t XL_FEW = 128;  // at most this many flagged tokens take the few-token form
+constexpr int XF_C = 16;          // columns per stage
+constexpr int XF_NB = 8;          // ring stages
+constexpr int XF_W = 4;           // warps per CTA = tokens per work item
 struct XfRing {
-    float4 w[XF_NB][32][2];     // [stage][lane][columns 8j .. 8j+3, 8j+4 .. 8j+7]
-    uint4 x[XF_NB];             // the token's eight bf16 activations of the stage
+    float4 w[XF_NB][32][XF_C / 4 + 1];  // [stage][expert][column quad], one pad quad: conflict-free per quarter warp
+    uint4 x[XF_NB][XF_W][2];            // [stage][token][8 columns]
+    double xd[XF_NB][XF_W][XF_C];       // [stage][token][column]
 };
 CK_DEV void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -72,141 +93,199 @@ CK_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memor
 template <int N>
 CK_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-CK_DEV void exact_logits_few(const uint16_t *__restrict__ x, const float *__restrict__ W,
-                             const uint32_t *__restrict__ flag_list, uint32_t nflag, double *__restrict__ out,
-                             uint32_t ne, uint32_t hidden, XfRing &r) {
-    const int lane = threadIdx.x & 31;
-    const uint32_t neg = (ne + 31) / 32, nwarp = gridDim.x * (blockDim.x >> 5);
-    const int nst = (int)hidden / 8;
-    for (uint32_t item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < nflag * neg; item += nwarp) {
-        const uint32_t f = item / neg, e = (item % neg) * 32 + lane;
-        const bool live = e < ne;
-        const float *wr = W + (size_t)(live ? e : 0) * hidden;
-        const uint16_t *xr = x + (size_t)flag_list[f] * hidden;
-        // stage s holds columns 8 (nst-1-s) .. +7 (the fold runs from the last column down)
+// The router in fp64 (n4 groups of four values), for the tiled form.
+__global__ void __launch_bounds__(256) k_router_f64(const float4 *__restrict__ w, double2 *__restrict__ wd, size_t n4,
+                                                    const uint32_t *__restrict__ flag_count) {
+    grid_dep_trigger_small();
+    grid_dep_wait();
+    if (*flag_count <= XL_FEW) return;  // only the tiled form reads it
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = __ldg(w + i);
+        wd[2 * i] = make_double2(v.x, v.y);
+        wd[2 * i + 1] = make_double2(v.z, v.w);
+    }
+}
+
+__global__ void __launch_bounds__(XF_W * 32) k_exact_logits_few(const uint16_t *__restrict__ x,
+                                                                const float *__restrict__ W,
+                                                                const uint32_t *__restrict__ flag_list,
+                                                                const uint32_t *__restrict__ flag_count,
+                                                                double *__restrict__ out, uint32_t ne, uint32_t hidden) {
+    extern __shared__ __align__(16) uint8_t xf_smem[];
+    XfRing &r = *reinterpret_cast<XfRing *>(xf_smem);
+    const uint32_t nflag = *flag_count;
+    if (nflag == 0 || nflag > XL_FEW) return;  // nothing flagged, or the tiled kernel takes them
+    const int tid = threadIdx.x, lane = tid & 31, wq = tid >> 5;
+    const uint32_t ntg = (nflag + XF_W - 1) / XF_W, neg = (ne + 31) / 32;
+    const int nst = (int)hidden / XF_C;
+    for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
+        const uint32_t f0 = (item / neg) * XF_W, e = (item % neg) * 32 + lane, f = f0 + wq;
+        const bool live = e < ne && f < nflag;
+        // thread i copies chunk i % 4 of router row i / 4 (rows past ne repeat the last row) and,
+        // for i < 8, half i % 2 of token i / 2's activations (tokens past nflag repeat the last one)
+        const float *wr = W + (size_t)min((item % neg) * 32 + (uint32_t)(tid / 4), ne - 1) * hidden + 4 * (tid % 4);
+        const uint16_t *xr = x + (size_t)flag_list[min(f0 + (uint32_t)(tid / 2 % XF_W), nflag - 1)] * hidden +
+                             8 * (tid % 2);
+        // stage s holds columns 16 (nst-1-s) .. +15 (the fold runs from the last column down)
         auto issue = [&](int s) {
             if (s < nst) {
-                const int j = 8 * (nst - 1 - s), b = s % XF_NB;
-                cp_async16(&r.w[b][lane][0], wr + j);
-                cp_async16(&r.w[b][lane][1], wr + j + 4);
-                if (lane == 0) cp_async16(&r.x[b], xr + j);
+                const int j = XF_C * (nst - 1 - s), b = s % XF_NB;
+                cp_async16(&r.w[b][tid / 4][tid % 4], wr + j);
+                if (tid < 2 * XF_W) cp_async16(&r.x[b][tid / 2][tid % 2], xr + j);
             }
             cp_async_commit();  // an empty group past the end keeps the wait count uniform
         };
-        __syncwarp();  // the previous item's reads of the ring are done
-        for (int s = 0; s < XF_NB - 1; ++s) issue(s);
-        double acc = 0.0;
-        for (int s = 0; s < nst; ++s) {
-            issue(s + XF_NB - 1);
-            cp_async_wait<XF_NB - 1>();
-            __syncwarp();
+        auto convert_x = [&](int s) {  // the stage's 64 activations, one per thread of warps 0-1
+            if (s < nst && tid < XF_C * XF_W) {
+                const int b = s % XF_NB, t = tid / XF_C, c = tid % XF_C;
+                const uint16_t h = reinterpret_cast<const uint16_t *>(&r.x[b][t][0])[c];
+                r.xd[b][t][c] = (double)bf16_bits_to_float(h);
+            }
+        };
+        auto load_w = [&](int s, double (&wv)[XF_C]) {  // the lane's 16 router values, in fp64
             const int b = s % XF_NB;
-            const float4 lo = r.w[b][lane][0], hi = r.w[b][lane][1];
-            const uint4 xv = r.x[b];
-            acc = __fma_rn((double)hi.w, (double)__uint_as_float(xv.w & 0xFFFF0000u), acc);
-            acc = __fma_rn((double)hi.z, (double)__uint_as_float(xv.w << 16), acc);
-            acc = __fma_rn((double)hi.y, (double)__uint_as_float(xv.z & 0xFFFF0000u), acc);
-            acc = __fma_rn((double)hi.x, (double)__uint_as_float(xv.z << 16), acc);
-            acc = __fma_rn((double)lo.w, (double)__uint_as_float(xv.y & 0xFFFF0000u), acc);
-            acc = __fma_rn((double)lo.z, (double)__uint_as_float(xv.y << 16), acc);
-            acc = __fma_rn((double)lo.y, (double)__uint_as_float(xv.x & 0xFFFF0000u), acc);
-            acc = __fma_rn((double)lo.x, (double)__uint_as_float(xv.x << 16), acc);
-            __syncwarp();  // every lane has read stage b before issue() refills it next iteration
+#pragma unroll
+            for (int c = 0; c < XF_C / 4; ++c) {
+                const float4 v = r.w[b][lane][c];
+                wv[4 * c] = v.x;
+                wv[4 * c + 1] = v.y;
+                wv[4 * c + 2] = v.z;
+                wv[4 * c + 3] = v.w;
+            }
+        };
+        double acc = 0.0;
+        // one stage: refill, wait, convert two stages ahead, load the next stage's router values,
+        // then fold this stage (column 15 first)
+        auto step = [&](int s, const double (&wc)[XF_C], double (&wn)[XF_C]) {
+            issue(s + XF_NB - 1);        // into the slot of stage s - 1, read in an earlier step
+            cp_async_wait<XF_NB - 3>();  // stages up to s + 2 have landed
+            __syncthreads();             // every thread's copies and conversions are visible
+            convert_x(s + 2);
+            if (s + 1 < nst) load_w(s + 1, wn);
+            const double2 *xv = reinterpret_cast<const double2 *>(r.xd[s % XF_NB][wq]);
+#pragma unroll
+            for (int c = XF_C / 2 - 1; c >= 0; --c) {
+                const double2 xx = xv[c];
+                acc = __fma_rn(wc[2 * c + 1], xx.y, acc);
+                acc = __fma_rn(wc[2 * c], xx.x, acc);
+            }
+        };
+        __syncthreads();  // the previous item's reads of the ring are done
+        for (int s = 0; s < XF_NB - 1; ++s) issue(s);
+        cp_async_wait<XF_NB - 3>();  // stages 0 and 1 have landed
+        __syncthreads();
+        convert_x(0);
+        convert_x(1);
+        double wa[XF_C], wb[XF_C];
+        load_w(0, wa);
+        int s = 0;
+        for (; s + 1 < nst; s += 2) {
+            step(s, wa, wb);
+            step(s + 1, wb, wa);
         }
+        if (s < nst) step(s, wa, wb);
         cp_async_wait<0>();
         if (live) out[(size_t)f * ne + e] = acc;
     }
 }
-__global__ void __launch_bounds__(XF_WARPS * 32) k_exact_logits_few(const uint16_t *__restrict__ x,
-                                                                    const float *__restrict__ W,
-                                                                    const uint32_t *__restrict__ flag_list,
-                                                                    const uint32_t *__restrict__ flag_count,
-                                                                    double *__restrict__ out, uint32_t ne,
-                                                                    uint32_t hidden) {
-    grid_dep_trigger_small();
-    grid_dep_wait();
-    extern __shared__ __align__(16) uint8_t xf_smem[];
-    const uint32_t nflag = *flag_count;
-    if (nflag > XL_FEW) return;  // the tiled kernel takes them
-    XfRing &r = reinterpret_cast<XfRing *>(xf_smem)[threadIdx.x >> 5];
-    exact_logits_few(x, W, flag_list, nflag, out, ne, hidden, r);
-}
 
-__global__ void __launch_bounds__(256) k_exact_logits(const uint16_t *__restrict__ x, const float *__restrict__ W,
-                                                      const uint32_t *__restrict__ flag_list,
-                                                      const uint32_t *__restrict__ flag_count, double *__restrict__ out,
-                                                      uint32_t ne, uint32_t hidden) {
+__global__ void __launch_bounds__(XT_THREADS) k_exact_logits(const uint16_t *__restrict__ x, const double *__restrict__ W,
+                                                             const uint32_t *__restrict__ flag_list,
+                                                             const uint32_t *__restrict__ flag_count,
+                                                             double *__restrict__ out, uint32_t ne, uint32_t hidden) {
     grid_dep_trigger_small();
     grid_dep_wait();
-    __shared__ double wt[2][XL_EXP][XL_J + 1];
-    __shared__ __align__(16) double xt[2][XL_TOK][XL_J];
+    extern __shared__ __align__(16) uint8_t xt_smem[];
+    XtSmem &S = *reinterpret_cast<XtSmem *>(xt_smem);
     const uint32_t nflag = *flag_count;
     if (nflag <= XL_FEW) return;  // k_exact_logits_few takes them
-    const int tid = threadIdx.x;
-    const int el = tid & (XL_EXP - 1);
-    const int q = tid / XL_EXP;  // 0..3: this thread folds tokens 4q .. 4q+3 of the item
-    const uint32_t ntg = (nflag + XL_TOK - 1) / XL_TOK, neg = (ne + XL_EXP - 1) / XL_EXP;
+    const int tid = threadIdx.x, lane = tid & 31, q = tid >> 5;
+    const uint32_t ntg = (nflag + XT_TOK - 1) / XT_TOK, neg = (ne + XT_EXP - 1) / XT_EXP;
     const int ntile = (int)(hidden / XL_J);
-    constexpr int WPT = XL_EXP * XL_J / 256;  // W floats each thread stages per tile (8)
-    constexpr int XPT = XL_TOK * XL_J / 256;  // x values each thread stages per tile (2)
     for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
-        const uint32_t f0 = (item / neg) * XL_TOK, e0 = (item % neg) * XL_EXP;
-        const float *wrow[WPT];
-        const uint16_t *xrow[XPT];
+        const uint32_t f0 = (item / neg) * XT_TOK, e0 = (item % neg) * XT_EXP;
+        // this thread's 16-byte pieces of a tile: eight of router rows (16 per row; rows past ne
+        // repeat the last row: read, never written) and, for threads 0-63, a quarter of a token row
+        const double *wsrc[8];
 #pragma unroll
-        for (int k = 0; k < WPT; ++k) {
-            const uint32_t e = e0 + (uint32_t)((tid + 256 * k) / XL_J);
-            wrow[k] = e < ne ? W + (size_t)e * hidden : nullptr;
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t e = min(e0 + (uint32_t)(tid / 16 + 8 * k), ne - 1);
+            wsrc[k] = W + (size_t)e * hidden + 2 * (tid % 16);
         }
+        const uint32_t fx = min(f0 + (uint32_t)(tid / 4 % XT_TOK), nflag - 1);
+        const uint16_t *xsrc = x + (size_t)flag_list[fx] * hidden + 8 * (tid % 4);
+        auto issue = [&](int tile) {  // tile t covers columns hidden - 32 (t + 1) .. hidden - 32 t - 1
+            if (tile < ntile) {
+                const int slot = tile % XT_NS, j0 = (int)hidden - XL_J * (tile + 1);
 #pragma unroll
-        for (int k = 0; k < XPT; ++k) {
-            const uint32_t f = min(f0 + (uint32_t)((tid + 256 * k) / XL_J), nflag - 1);
-            xrow[k] = x + (size_t)flag_list[f] * hidden;
-        }
-        const int jc = tid % XL_J;
-        float wv[WPT];
-        uint16_t xv[XPT];
-        auto fetch = [&](int tile) {  // tile t covers columns hidden - 32 (t + 1) .. hidden - 32 t - 1
-            const int j0 = (int)hidden - XL_J * (tile + 1);
-#pragma unroll
-            for (int k = 0; k < WPT; ++k) wv[k] = wrow[k] ? __ldg(wrow[k] + j0 + jc) : 0.0f;
-#pragma unroll
-            for (int k = 0; k < XPT; ++k) xv[k] = __ldg(xrow[k] + j0 + jc);
+                for (int k = 0; k < 8; ++k) cp_async16(&S.w[slot][tid / 16 + 8 * k][2 * (tid % 16)], wsrc[k] + j0);
+                if (tid < 4 * XT_TOK) cp_async16(&S.x[slot][tid / 4][8 * (tid % 4)], xsrc + j0);
+            }
+            cp_async_commit();
         };
-        auto stage = [&](int b) {
+        auto convert = [&](int tile) {  // the tile's activations into fp64 buffer tile & 1
+            if (tile < ntile) {
+                const int slot = tile % XT_NS, b = tile & 1;
 #pragma unroll
-            for (int k = 0; k < WPT; ++k) wt[b][(tid + 256 * k) / XL_J][jc] = (double)wv[k];
-#pragma unroll
-            for (int k = 0; k < XPT; ++k) xt[b][(tid + 256 * k) / XL_J][jc] = (double)bf16_bits_to_float(xv[k]);
-        };
-        fetch(0);
-        stage(0);
-        __syncthreads();
-        double a[XL_TPT];
-#pragma unroll
-        for (int t = 0; t < XL_TPT; ++t) a[t] = 0.0;
-        for (int tile = 0; tile < ntile; ++tile) {
-            const int b = tile & 1;
-            if (tile + 1 < ntile) fetch(tile + 1);
-#pragma unroll
-            for (int jj = XL_J - 2; jj >= 0; jj -= 2) {  // columns jj + 1, then jj: descending j
-                const double w1 = wt[b][el][jj + 1], w0 = wt[b][el][jj];
-#pragma unroll
-                for (int t = 0; t < XL_TPT; ++t) {
-                    const double2 xx = *reinterpret_cast<const double2 *>(&xt[b][XL_TPT * q + t][jj]);
-                    a[t] = __fma_rn(w1, xx.y, a[t]);
-                    a[t] = __fma_rn(w0, xx.x, a[t]);
+                for (int k = 0; k < XT_TOK * XL_J / XT_THREADS; ++k) {
+                    const int i = tid + XT_THREADS * k;
+                    S.xd[b][i / XL_J][i % XL_J] = (double)bf16_bits_to_float(S.x[slot][i / XL_J][i % XL_J]);
                 }
             }
-            if (tile + 1 < ntile) stage(b ^ 1);
-            __syncthreads();
-        }
-        const uint32_t e = e0 + el;
-        if (e < ne) {
+        };
+        __syncthreads();  // the previous item's reads of the ring and buffers are done
+        for (int t = 0; t < XT_NS - 1; ++t) issue(t);
+        cp_async_wait<XT_NS - 2>();  // tile 0 has landed
+        __syncthreads();
+        convert(0);
+        double a[4][2];
 #pragma unroll
-            for (int t = 0; t < XL_TPT; ++t) {
-                const uint32_t f = f0 + XL_TPT * q + t;
-                if (f < nflag) out[(size_t)f * ne + e] = a[t];
+        for (int t = 0; t < 4; ++t) a[t][0] = a[t][1] = 0.0;
+        for (int tile = 0; tile < ntile; ++tile) {
+            cp_async_wait<XT_NS - 3>();  // tiles up to tile + 1 have landed
+            __syncthreads();             // ... for every thread; tile - 1 is folded, buffer tile & 1 converted
+            issue(tile + XT_NS - 1);     // into the slot of tile - 1
+            convert(tile + 1);
+            const int slot = tile % XT_NS, b = tile & 1;
+            // columns jj + 1, then jj: descending j; the next pair's operands load while this one folds
+            double2 wa = *reinterpret_cast<const double2 *>(&S.w[slot][lane][XL_J - 2]);
+            double2 wb = *reinterpret_cast<const double2 *>(&S.w[slot][lane + 32][XL_J - 2]);
+            double2 xx[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) xx[t] = *reinterpret_cast<const double2 *>(&S.xd[b][4 * q + t][XL_J - 2]);
+#pragma unroll
+            for (int jj = XL_J - 2; jj >= 0; jj -= 2) {
+                double2 wa2 = wa, wb2 = wb, xx2[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) xx2[t] = xx[t];
+                if (jj >= 2) {
+                    wa2 = *reinterpret_cast<const double2 *>(&S.w[slot][lane][jj - 2]);
+                    wb2 = *reinterpret_cast<const double2 *>(&S.w[slot][lane + 32][jj - 2]);
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) xx2[t] = *reinterpret_cast<const double2 *>(&S.xd[b][4 * q + t][jj - 2]);
+                }
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    a[t][0] = __fma_rn(wa.y, xx[t].y, a[t][0]);
+                    a[t][1] = __fma_rn(wb.y, xx[t].y, a[t][1]);
+                    a[t][0] = __fma_rn(wa.x, xx[t].x, a[t][0]);
+                    a[t][1] = __fma_rn(wb.x, xx[t].x, a[t][1]);
+                }
+                wa = wa2;
+                wb = wb2;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) xx[t] = xx2[t];
+            }
+        }
+        cp_async_wait<0>();
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t f = f0 + 4 * q + t;
+            if (f >= nflag) continue;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const uint32_t e = e0 + lane + 32 * c;
+                if (e < ne) out[(size_t)f * ne + e] = a[t][c];
             }
         }
     }
@@ -372,146 +451,51 @@ __global__ void __launch_bounds__(256) k_exact_select(const double *__restrict__
     }
 }
 
-// The middle tier of a large batch's route: fp64 logits of the flagged tokens accurate to a few
-// roundings of sum|w x|, without the reference's sequential fold.  The tiles are those of
-// k_exact_logits, but every thread keeps eight interleaved partial sums per token (column j feeds
-// partial j mod 8) of the exact fp64 products, so a chain is hidden / 8 terms long and a thread has
-// 32 independent chains in flight; the eight are summed in a fixed order at the end (deterministic).
-// The error against the exact dot is at most (hidden / 8 + 3) * 2^-53 * sum|w x|, and the
-// reference's own fold differs from it by at most hidden * 2^-53 * sum|w x|: the fp64 selection that
-// follows flags a token for the sequential fold only when its margin is below 16 * 2^-40 of its
-// largest sum|w x| -- in practice only exact ties.  sum|w x| (fp32) is written beside each logit.
-// Block 0 also clears the count of the list that selection fills.
-__global__ void __launch_bounds__(256) k_accurate_logits(const uint16_t *__restrict__ x, const float *__restrict__ W,
-                                                         const uint32_t *__restrict__ flag_list,
-                                                         const uint32_t *__restrict__ flag_count,
-                                                         double *__restrict__ out, float *__restrict__ out_abs,
-                                                         uint32_t *__restrict__ next_count, uint32_t ne,
-                                                         uint32_t hidden) {
-    grid_dep_trigger_small();
-    grid_dep_wait();
-    if (blockIdx.x == 0 && threadIdx.x == 0) *next_count = 0u;
-    __shared__ float wt[2][XL_EXP][XL_J + 1];
-    __shared__ __align__(16) float xt[2][XL_TOK][XL_J];
-    const uint32_t nflag = *flag_count;
-    const int tid = threadIdx.x;
-    const int el = tid & (XL_EXP - 1);
-    const int q = tid / XL_EXP;
-    const uint32_t ntg = (nflag + XL_TOK - 1) / XL_TOK, neg = (ne + XL_EXP - 1) / XL_EXP;
-    const int ntile = (int)(hidden / XL_J);
-    constexpr int WPT = XL_EXP * XL_J / 256;
-    constexpr int XPT = XL_TOK * XL_J / 256;
-    constexpr int NP = 8;
-    for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
-        const uint32_t f0 = (item / neg) * XL_TOK, e0 = (item % neg) * XL_EXP;
-        const float *wrow[WPT];
-        const uint16_t *xrow[XPT];
-#pragma unroll
-        for (int k = 0; k < WPT; ++k) {
-            const uint32_t e = e0 + (uint32_t)((tid + 256 * k) / XL_J);
-            wrow[k] = e < ne ? W + (size_t)e * hidden : nullptr;
-        }
-#pragma unroll
-        for (int k = 0; k < XPT; ++k) {
-            const uint32_t f = min(f0 + (uint32_t)((tid + 256 * k) / XL_J), nflag - 1);
-            xrow[k] = x + (size_t)flag_list[f] * hidden;
-        }
-        const int jc = tid % XL_J;
-        float wv[WPT];
-        uint16_t xv[XPT];
-        auto fetch = [&](int tile) {
-            const int j0 = XL_J * tile;
-#pragma unroll
-            for (int k = 0; k < WPT; ++k) wv[k] = wrow[k] ? __ldg(wrow[k] + j0 + jc) : 0.0f;
-#pragma unroll
-            for (int k = 0; k < XPT; ++k) xv[k] = __ldg(xrow[k] + j0 + jc);
-        };
-        auto stage = [&](int b) {
-#pragma unroll
-            for (int k = 0; k < WPT; ++k) wt[b][(tid + 256 * k) / XL_J][jc] = wv[k];
-#pragma unroll
-            for (int k = 0; k < XPT; ++k) xt[b][(tid + 256 * k) / XL_J][jc] = bf16_bits_to_float(xv[k]);
-        };
-        fetch(0);
-        stage(0);
-        __syncthreads();
-        double a[XL_TPT][NP];
-        float ab[XL_TPT];
-#pragma unroll
-        for (int t = 0; t < XL_TPT; ++t) {
-            ab[t] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < NP; ++i) a[t][i] = 0.0;
-        }
-        for (int tile = 0; tile < ntile; ++tile) {
-            const int b = tile & 1;
-            if (tile + 1 < ntile) fetch(tile + 1);
-#pragma unroll
-            for (int j = 0; j < XL_J; ++j) {
-                const float w = wt[b][el][j];
-                const double wd = (double)w;
-#pragma unroll
-                for (int t = 0; t < XL_TPT; ++t) {
-                    const float xf = xt[b][XL_TPT * q + t][j];
-                    a[t][j % NP] = __fma_rn(wd, (double)xf, a[t][j % NP]);  // the product is exact in fp64
-                    ab[t] = fmaf(fabsf(w), fabsf(xf), ab[t]);
-                }
-            }
-            if (tile + 1 < ntile) stage(b ^ 1);
-            __syncthreads();
-        }
-        const uint32_t e = e0 + el;
-        if (e < ne) {
-#pragma unroll
-            for (int t = 0; t < XL_TPT; ++t) {
-                const uint32_t f = f0 + XL_TPT * q + t;
-                if (f < nflag) {
-                    const double s = ((a[t][0] + a[t][1]) + (a[t][2] + a[t][3])) +
-                                     ((a[t][4] + a[t][5]) + (a[t][6] + a[t][7]));
-                    out[(size_t)f * ne + e] = s;
-                    out_abs[(size_t)f * ne + e] = ab[t] * 1.0001f;  // covers the fp32 sum's own rounding
-                }
-            }
-        }
-    }
-}
-
-int launch_accurate_logits(const uint16_t *x, const float *w, const uint32_t *flag_list, const uint32_t *flag_count,
-                           double *out, float *out_abs, uint32_t *next_count, uint32_t ne, uint32_t hidden,
-                           cudaStream_t s) {
-    if (ne > 256 || hidden % XL_J != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+// The reference's right-fold logits of the listed tokens: out[f * ne + e] for f < *count; w64 is
+// scratch for the router in fp64 (ne * hidden doubles).
+int launch_exact_logits(const uint16_t *x, const float *w, const uint32_t *flag_list, const uint32_t *flag_count,
+                        double *out, double *w64, uint32_t ne, uint32_t hidden, cudaStream_t s) {
+    if (ne == 0 || ne > 256 || hidden == 0 || hidden % XL_J != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(w64) & 15))
         return CK_ERR_SHAPE;
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const cudaError_t e = launch_pdl(k_accurate_logits, dim3(nsm * 2), dim3(256), 0, s, x, w, flag_list, flag_count,
-                                     out, out_abs, next_count, ne, hidden);
+    static unsigned long long attrs = 0;
+    if (attr_pending(attrs)) {
+        cudaError_t e = cudaFuncSetAttribute(k_exact_logits_few, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(XfRing));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_exact_logits, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sizeof(XtSmem));
+        if (e != cudaSuccess) return (int)e;
+        attr_mark(attrs);
+    }
+    cudaError_t e = launch_pdl(k_router_f64, dim3(nsm), dim3(256), 0, s, reinterpret_cast<const float4 *>(w),
+                               reinterpret_cast<double2 *>(w64), (size_t)ne * hidden / 4, flag_count);
+    // both forms are launched; each returns at once unless the flagged count is its own.  The tiled
+    // form runs one CTA per SM (shared-memory bandwidth is its bound) over its work items.
+    if (e == cudaSuccess) {
+        k_exact_logits_few<<<2 * nsm, XF_W * 32, sizeof(XfRing), s>>>(x, w, flag_list, flag_count, out, ne, hidden);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+        e = launch_pdl(k_exact_logits, dim3(nsm), dim3(XT_THREADS), sizeof(XtSmem), s, x, (const double *)w64,
+                       flag_list, flag_count, out, ne, hidden);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int32_t *ids, float *wts,
-                       const uint32_t *flag_list, const uint32_t *flag_count, double *scratch,
+                       const uint32_t *flag_list, const uint32_t *flag_count, double *scratch, double *w64,
                        const RouteParams &p, cudaStream_t s) {
-    if (p.ne > 256 || p.hidden % XL_J != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) || p.nsel > 16 || (p.mode == 4 && p.ngroups > 32)) return CK_ERR_SHAPE;
+    if (p.nsel > 16 || (p.mode == 4 && p.ngroups > 32)) return CK_ERR_SHAPE;
+    int rc = launch_exact_logits(x, w, flag_list, flag_count, scratch, w64, p.ne, p.hidden, s);
+    if (rc) return rc;
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    static unsigned long long few_attr = 0;
-    if (attr_pending(few_attr)) {
-        const cudaError_t e = cudaFuncSetAttribute(k_exact_logits_few, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)(XF_WARPS * sizeof(XfRing)));
-        if (e != cudaSuccess) return (int)e;
-        attr_mark(few_attr);
-    }
-    // both forms are launched; each returns at once unless the flagged count is its own
-    cudaError_t e = launch_pdl(k_exact_logits_few, dim3(2 * nsm), dim3(XF_WARPS * 32), XF_WARPS * sizeof(XfRing), s, x,
-                               w, flag_list, flag_count, scratch, p.ne, p.hidden);
-    if (e == cudaSuccess)
-        e = launch_pdl(k_exact_logits, dim3(nsm * 2), dim3(256), 0, s, x, w, flag_list, flag_count, scratch, p.ne,
-                       p.hidden);
-    if (e == cudaSuccess)
-        e = launch_pdl(k_exact_select, dim3(nsm * 2), dim3(256), 0, s, scratch, bias, ids, wts, flag_list, flag_count,
-                       p);
+    const cudaError_t e = launch_pdl(k_exact_select, dim3(nsm * 2), dim3(256), 0, s, scratch, bias, ids, wts, flag_list,
+                                     flag_count, p);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

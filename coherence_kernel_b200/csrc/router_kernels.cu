@@ -212,17 +212,13 @@ CK_DEV T warp_sum_t(T v) {
 template <typename T>
 __global__ void k_route_select(const T *__restrict__ L, const float *__restrict__ sabs,
                                const float *__restrict__ bias, int32_t *__restrict__ ids, float *__restrict__ wts,
-                               uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p,
-                               const uint32_t *__restrict__ subset, const uint32_t *__restrict__ subset_count) {
+                               uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p) {
     grid_dep_trigger_small();
     grid_dep_wait();
     constexpr bool CTA = sizeof(T) == 8;  // the fp64 form: a CTA of 256 threads per token
     const int lane = threadIdx.x & 31;
-    // row: the logits row this CTA / warp reads; t: the token it routes (with a subset, row i of the
-    // logits belongs to token subset[i] and only *subset_count rows exist)
-    const uint32_t row = CTA ? blockIdx.x : (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (subset_count ? row >= *subset_count : row >= p.ntok) return;
-    const uint32_t t = subset_count ? subset[row] : row;
+    const uint32_t t = CTA ? blockIdx.x : (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= p.ntok) return;
     const T NEG = (T)-3.0e38f;
     T sc[RMAX], pr[RMAX];
     const int nreg = (int)((p.ne + 31) / 32);
@@ -237,8 +233,8 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
         __shared__ float s_lmax[8];
         const int e = threadIdx.x;
         const bool v = e < (int)p.ne;
-        const T l = v ? L[(size_t)row * p.ne + e] : NEG;
-        float lm = v ? sabs[(size_t)row * p.ne + e] : 0.0f;
+        const T l = v ? L[(size_t)t * p.ne + e] : NEG;
+        float lm = v ? sabs[(size_t)t * p.ne + e] : 0.0f;
         T prv = (T)0, scv = NEG;
         if (v) {
             prv = p.mode == 4 ? (T)1 / ((T)1 + sel_exp(-l)) : l;
@@ -280,8 +276,8 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
         for (int i = 0; i < RMAX; ++i) {
             const int e = 32 * i + lane;
             const bool v = i < nreg && e < (int)p.ne;
-            const T l = v ? L[(size_t)row * p.ne + e] : NEG;
-            if (v) lmax = fmaxf(lmax, sabs ? sabs[(size_t)row * p.ne + e] : fabsf((float)l));
+            const T l = v ? L[(size_t)t * p.ne + e] : NEG;
+            if (v) lmax = fmaxf(lmax, sabs ? sabs[(size_t)t * p.ne + e] : fabsf((float)l));
             if (p.mode == 4) {
                 pr[i] = v ? (T)1 / ((T)1 + sel_exp(-l)) : (T)0;
                 sc[i] = v ? pr[i] + (T)bias[e] : NEG;
@@ -583,7 +579,7 @@ int launch_route_select(const float *L, const float *bias, int32_t *ids, float *
     cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
     if (p.ntok)
         k_route_select<float><<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, nullptr, bias, ids, wts, flag_list,
-                                                                          flag_count, p, nullptr, nullptr);
+                                                                          flag_count, p);
     return (int)cudaGetLastError();
 }
 int launch_route_select_d(const double *L, const float *sabs, const float *bias, int32_t *ids, float *wts,
@@ -597,25 +593,7 @@ int launch_route_select_d(const double *L, const float *sabs, const float *bias,
     // flag_count was cleared by launch_router_logits_few, the kernel before this one
     if (p.ntok) {
         const cudaError_t e = launch_pdl(k_route_select<double>, dim3(p.ntok), dim3(256), 0, s, L, sabs, bias, ids, wts,
-                                         flag_list, flag_count, p, (const uint32_t *)nullptr, (const uint32_t *)nullptr);
-        if (e != cudaSuccess) return (int)e;
-    }
-    return (int)cudaGetLastError();
-}
-// The fp64 selection over the rows of a subset of the tokens: row i of L / sabs belongs to token
-// subset[i], i < *subset_count (at most p.ntok rows); tokens whose margin is within the logits' error
-// go to flag_list / flag_count (cleared by the kernel before this one).
-int launch_route_select_d_subset(const double *L, const float *sabs, const float *bias, int32_t *ids, float *wts,
-                                 const uint32_t *subset, const uint32_t *subset_count, uint32_t *flag_list,
-                                 uint32_t *flag_count, const RouteParams &p, cudaStream_t s) {
-    if (p.ne == 0 || p.ne > 32 * RMAX || p.nsel == 0 || p.nsel > 16 || p.nsel > p.ne) return CK_ERR_SHAPE;
-    if (p.mode == 4 && (p.ngroups == 0 || p.ngroups > 32 || p.ne % p.ngroups || p.topk_groups == 0 ||
-                        p.topk_groups > p.ngroups || p.nsel > p.topk_groups * (p.ne / p.ngroups)))
-        return CK_ERR_SHAPE;
-    if ((p.mode == 4 && !bias) || !sabs || !subset || !subset_count) return CK_ERR_ARG;
-    if (p.ntok) {
-        const cudaError_t e = launch_pdl(k_route_select<double>, dim3(p.ntok), dim3(256), 0, s, L, sabs, bias, ids, wts,
-                                         flag_list, flag_count, p, subset, subset_count);
+                                         flag_list, flag_count, p);
         if (e != cudaSuccess) return (int)e;
     }
     return (int)cudaGetLastError();

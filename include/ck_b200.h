@@ -149,6 +149,15 @@ int ck_moe_route(const ck_moe_config *cfg, const void *x_bf16_dev, uint32_t ntok
                  const float *bias_dev, float *logits_dev, int32_t *ids_dev, float *wts_dev, void *route_ws_dev,
                  size_t route_ws_bytes, void *stream);
 int ck_moe_route_flagged(const ck_moe_config *cfg, uint32_t ntok, const void *route_ws_dev, void *stream);
+/* The reference's router logits for a list of tokens: out[f * n_experts + e] = tb-dot's right fold
+ * (transformer-block.fk:25-26) of router row e with token tokens[f]'s bf16 activations, in fp64 and
+ * bit-identical to the reference, for f < *count_dev (device memory, read by the kernels).  The
+ * route's exact re-route runs these kernels on its near-tie tokens.  router_f64_dev is scratch
+ * (n_experts * hidden doubles) that receives the router in fp64.  n_experts <= 256,
+ * hidden % 32 == 0, x, the router and the scratch 16-byte aligned. */
+int ck_router_exact_logits(const void *x_bf16_dev, const float *router_w_dev, const uint32_t *tokens_dev,
+                           const uint32_t *count_dev, uint32_t n_experts, uint32_t hidden, double *out_dev,
+                           double *router_f64_dev, void *stream);
 size_t ck_moe_permute_workspace_bytes(uint32_t ntok, uint32_t nsel, uint32_t n_experts);
 uint32_t ck_moe_max_tiles(uint32_t ntok, uint32_t nsel, uint32_t n_experts, uint32_t n_shared);
 int ck_moe_permute(const int32_t *ids_dev, const float *wts_dev, const void *x_bf16_dev, uint32_t ntok,

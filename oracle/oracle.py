@@ -130,6 +130,19 @@ def rmsnorm(x, g, eps):
     return out
 
 
+def dot_rows(a, b):
+    """out[i, k] = tb-dot's right fold of a[i] with b[k] (fp64 rows of equal length)."""
+    a = np.ascontiguousarray(a, dtype=np.float64)
+    b = np.ascontiguousarray(b, dtype=np.float64)
+    out = np.empty((a.shape[0], b.shape[0]), dtype=np.float64)
+    n, L = a.shape[1], lib()
+    pa, pb = a.ctypes.data, b.ctypes.data
+    for i in range(a.shape[0]):
+        for k in range(b.shape[0]):
+            out[i, k] = L.ckr_dot(ctypes.c_void_p(pa + 8 * n * i), ctypes.c_void_p(pb + 8 * n * k), n)
+    return out
+
+
 def q80_matvec(qb, x, rows, cols):
     x = np.ascontiguousarray(x, dtype=np.float64)
     y = np.empty(rows, dtype=np.float64)
