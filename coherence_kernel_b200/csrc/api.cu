@@ -22,6 +22,12 @@ int fail(int rc, const char *what) {
     return rc;
 }
 inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+// The router logits GEMM gives each K-chunk accumulator a work unit of its own when its unsplit
+// units (64-token tiles x 128-expert blocks) would fill at most half the GPU's 148 SMs; beyond that
+// the short units' pipeline fills and the partial planes' traffic cost more than they save.
+inline bool route_ksplit(const ck_moe_config *c, uint32_t ntok) {
+    return ntok > CK_MOE_DECODE_TOKENS && (uint64_t)((ntok + 63) / 64) * ((c->n_experts + 127) / 128) <= 74;
+}
 inline size_t al(size_t b) { return (b + 255) & ~(size_t)255; }
 
 // The router's scratch: the three-term bf16 split of the router, its token tiles, the flagged-
@@ -35,6 +41,7 @@ struct RouteWs {
     double *exact;  // fp64 logits of the flagged tokens (and of every token on the decode-batch path)
     float *sabs;    // sum |w x| per logit on the decode-batch path
     double *w64;    // the router in fp64, for the exact re-route
+    float *planes;  // the logits GEMM's K-chunk partial sums 1 .. 7 (chunk 0 in the logits)
     size_t total;
 };
 RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
@@ -50,6 +57,7 @@ RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
     w.exact = (double *)take((size_t)ntok * c->n_experts * 8);
     w.sabs = (float *)take((size_t)ntok * c->n_experts * 4);
     w.w64 = (double *)take((size_t)c->n_experts * c->hidden * 8);
+    w.planes = route_ksplit(c, ntok) ? (float *)take((size_t)7 * ntok * c->n_experts * 4) : nullptr;
     w.total = o;
     return w;
 }
@@ -344,9 +352,17 @@ int ck_moe_route(const ck_moe_config *c, const void *x, uint32_t ntok, const flo
         g.ntiles = w.ntiles;
         g.max_tiles = ntok / 16 + 2;
         g.err = w.err;
+        // a small batch: each of the GEMM's eight K-chunk accumulators is a unit of its own (eight
+        // times the CTAs: 1024 tokens otherwise ran on 32 of them), and the selection adds the
+        // chunks in order -- the same sums as the unsplit epilogue's, so the same logits
+        const bool split = route_ksplit(c, ntok);
+        g.ksplit = split ? 8 : 1;
+        g.out_planes = w.planes;
         rc = ck::launch_gemm_dense(g, S(s));
         if (rc) return fail(rc, "ck_moe_route logits");
-        rc = ck::launch_route_select(logits, bias, ids, wts, w.flags + 1, w.flags, p, S(s));
+        const int nk = (int)(3 * c->hidden / 64), kchunk = (nk + 7) / 8;
+        rc = ck::launch_route_select(logits, w.planes, split ? (nk + kchunk - 1) / kchunk - 1 : 0, bias, ids, wts,
+                                     w.flags + 1, w.flags, p, S(s));
         if (rc) return fail(rc, "ck_moe_route select");
     } else {
         return fail(rc, "ck_moe_route logits");

@@ -61,8 +61,10 @@ int launch_router_logits_few(const uint16_t *x, const float *w, float *L, double
 // the fast selection over fp64 logits (the decode-batch form); its margin scales with sabs
 int launch_route_select_d(const double *L, const float *sabs, const float *bias, int32_t *ids, float *wts,
                           uint32_t *flag_list, uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
-int launch_route_select(const float *logits, const float *bias, int32_t *ids, float *wts, uint32_t *flag_list,
-                        uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
+// the fast selection over the tensor-core logits; `planes` holds nplanes (<= 7) more K-chunk partial
+// planes of [ntok, ne] to add to `logits` in chunk order first (the sums are written to `logits`)
+int launch_route_select(float *logits, const float *planes, int nplanes, const float *bias, int32_t *ids, float *wts,
+                        uint32_t *flag_list, uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
 // scratch: fp64 [ntok, ne] (the exact logits of the flagged tokens)
 // out fp64 [*flag_count, ne]: the right-fold logits of the listed tokens (at most 256 experts,
 // hidden % 32 == 0); w64: scratch for the router in fp64, ne * hidden doubles
@@ -121,6 +123,11 @@ struct GemmParams {
     const void *a_dense;
     uint32_t kx;
     float *out_f32;
+    // ksplit > 1: every K-chunk accumulator of the dense form is a unit of its own; chunk 0 goes to
+    // out_f32 and chunk c > 0 to plane c - 1 of out_planes ([DENSE_ACC - 1][out_rows, N]), for the
+    // reader to add in chunk order (the sums the unsplit form's epilogue makes)
+    float *out_planes;
+    uint32_t ksplit;
     // a bound on the tokens of every tile (0: none known); 1..8 runs the few-token grouped matvec
     // (moe_gemv.cu) where its shape rules hold
     uint32_t max_tile_tok;

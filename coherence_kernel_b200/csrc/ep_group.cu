@@ -10,7 +10,8 @@
 // sequence a rank of PeerExpertParallelMoE runs (route, dispatch plan, shared expert, dispatch
 // stores, barrier, regroup, expert GEMMs, return stores, barrier, combine; ep_peer.cu), and
 // gathers ids, weights, per-expert counts and outputs back to the caller's device.  The host
-// issues every member's work without waiting: members meet only at the bounded device barriers.
+// issues every member's work without waiting, phase by phase across the members (member_forward):
+// members meet only at the bounded device barriers.
 #include "../../include/ck_b200.h"
 #include "ck_common.cuh"
 #include "ck_launch.h"
@@ -173,8 +174,13 @@ void fill_peers(ck_ep_group *g) {
     }
 }
 
-// One member's whole forward over its T tokens, issued on its stream.
-int member_forward(ck_ep_group *g, uint32_t d, uint32_t T) {
+// One member's forward over its T tokens, issued on its stream in three phases: 0 up to the
+// dispatch signal, 1 from the dispatch barrier to the return signal, 2 from the return barrier on.
+// The group issues phase p of every member before phase p + 1 of any: a member's barrier then only
+// ever waits on work already queued on its peers, so no host call that blocks until a device is
+// idle (a kernel's first launch on a device loads its module) can wait on a barrier whose signal
+// the host has not issued yet.
+int member_forward(ck_ep_group *g, uint32_t d, uint32_t T, int phase) {
     Member &m = g->m[d];
     const ck_moe_config &c = g->cfg;
     const uint32_t W = g->world, K = c.nsel, H = c.hidden, I = c.inter, E = c.n_experts, NS = c.n_shared;
@@ -183,10 +189,35 @@ int member_forward(ck_ep_group *g, uint32_t d, uint32_t T) {
     void *s = m.st;
     const ck_ep_peers *pe = &m.peers;
     int rc = cudaSetDevice(m.dev);
+    uint8_t *ret_y = m.arena + m.a_ret_y;
+    int32_t *rids = (int32_t *)(m.arena + m.a_recv_ids);
+    if (phase == 2) {
+        if (!rc) rc = ck_ep_peer_wait(pe, 1, WAIT_NS, s);
+        if (!rc && T)
+            rc = ck_moe_combine(ret_y, m.ids, m.wts, m.iota, T, K, NS, H, c.mode == 3, m.out, nullptr, s);
+        return rc;
+    }
+    if (phase == 1) {
+        if (!rc) rc = ck_ep_peer_wait(pe, 0, WAIT_NS, s);
+        if (!rc)
+            rc = ck_moe_permute(rids, (const float *)(m.arena + m.a_recv_w), m.arena + m.a_recv_x, R, K, g->el, 0, H,
+                                c.mode == 4, m.xp2, m.row_w2, m.pair_pos2, m.counts2, m.tiles2, m.ntiles2, m.perm_ws2,
+                                s);
+        const uint32_t bound = R <= CK_MOE_DECODE_TOKENS ? (R < CK_MOE_FEW_TOKENS ? R : CK_MOE_FEW_TOKENS) : 0;
+        if (!rc)
+            rc = ck_moe_expert_gemm_bounded(1, m.wg, m.wu, nullptr, nullptr, mb, g->el, 0, m.xp2, R * K, m.h2, R * K,
+                                            m.row_w2, m.tiles2, m.ntiles2, m.mt2, I, H, 0, bound, pe->err, s);
+        if (!rc)
+            rc = ck_moe_expert_gemm_bounded(0, m.wd, nullptr, nullptr, nullptr, mb, g->el, 0, m.h2, R * K, m.y2, R * K,
+                                            nullptr, m.tiles2, m.ntiles2, m.mt2, H, I, 1, bound, pe->err, s);
+        if (!rc)
+            rc = ck_ep_peer_return(pe, m.y2, m.pair_pos2, rids, (const int32_t *)(m.arena + m.a_recv_tok), s);
+        if (!rc) rc = ck_ep_peer_signal(pe, 1, s);
+        return rc;
+    }
     if (!rc) rc = ck_ep_peer_begin(pe, s);
     if (!rc && T) rc = ck_moe_route(&c, m.x, T, m.router, m.bias, m.logits, m.ids, m.wts, m.route_ws, m.route_ws_bytes, s);
     if (!rc) rc = ck_ep_dispatch_plan(m.ids, m.wts, T, K, E, W, m.counts, m.sizes, m.send_tok, m.send_meta, m.ret_pos, s);
-    uint8_t *ret_y = m.arena + m.a_ret_y;
     if (!rc && NS && T) {
         const uint32_t bound = T <= CK_MOE_DECODE_TOKENS ? (T < CK_MOE_FEW_TOKENS ? T : CK_MOE_FEW_TOKENS) : 0;
         rc = ck_token_tiles_n(m.sh_tiles, m.sh_ntiles, T, bound ? CK_MOE_FEW_TOKENS : 192, s);
@@ -203,24 +234,6 @@ int member_forward(ck_ep_group *g, uint32_t d, uint32_t T) {
     }
     if (!rc) rc = ck_ep_peer_dispatch(pe, m.x, m.send_tok, m.send_meta, m.sizes, T, s);
     if (!rc) rc = ck_ep_peer_signal(pe, 0, s);
-    if (!rc) rc = ck_ep_peer_wait(pe, 0, WAIT_NS, s);
-    int32_t *rids = (int32_t *)(m.arena + m.a_recv_ids);
-    if (!rc)
-        rc = ck_moe_permute(rids, (const float *)(m.arena + m.a_recv_w), m.arena + m.a_recv_x, R, K, g->el, 0, H,
-                            c.mode == 4, m.xp2, m.row_w2, m.pair_pos2, m.counts2, m.tiles2, m.ntiles2, m.perm_ws2, s);
-    const uint32_t bound = R <= CK_MOE_DECODE_TOKENS ? (R < CK_MOE_FEW_TOKENS ? R : CK_MOE_FEW_TOKENS) : 0;
-    if (!rc)
-        rc = ck_moe_expert_gemm_bounded(1, m.wg, m.wu, nullptr, nullptr, mb, g->el, 0, m.xp2, R * K, m.h2, R * K,
-                                        m.row_w2, m.tiles2, m.ntiles2, m.mt2, I, H, 0, bound, pe->err, s);
-    if (!rc)
-        rc = ck_moe_expert_gemm_bounded(0, m.wd, nullptr, nullptr, nullptr, mb, g->el, 0, m.h2, R * K, m.y2, R * K,
-                                        nullptr, m.tiles2, m.ntiles2, m.mt2, H, I, 1, bound, pe->err, s);
-    if (!rc)
-        rc = ck_ep_peer_return(pe, m.y2, m.pair_pos2, rids, (const int32_t *)(m.arena + m.a_recv_tok), s);
-    if (!rc) rc = ck_ep_peer_signal(pe, 1, s);
-    if (!rc) rc = ck_ep_peer_wait(pe, 1, WAIT_NS, s);
-    if (!rc && T)
-        rc = ck_moe_combine(ret_y, m.ids, m.wts, m.iota, T, K, NS, H, c.mode == 3, m.out, nullptr, s);
     return rc;
 }
 
@@ -321,26 +334,34 @@ int ck_ep_group_forward(ck_ep_group *g, const void *x_bf16, uint32_t ntok, int32
     uint32_t off[CK_EP_MAX_RANKS + 1];
     off[0] = 0;
     for (uint32_t d = 0; d < W; ++d) off[d + 1] = (uint32_t)(((uint64_t)ntok * (d + 1)) / W);
-    for (uint32_t d = 0; d < W && !rc; ++d) {
-        Member &m = g->m[d];
-        const uint32_t T = off[d + 1] - off[d];
-        cudaSetDevice(m.dev);
-        rc = (int)cudaStreamWaitEvent(m.st, start, 0);
-        if (!rc && T)
-            rc = (int)cudaMemcpyAsync(m.x, (const uint8_t *)x_bf16 + (size_t)off[d] * H * 2, (size_t)T * H * 2,
-                                      cudaMemcpyDefault, m.st);
-        if (!rc) rc = member_forward(g, d, T);
-        if (!rc && T) {
-            rc = (int)cudaMemcpyAsync((uint8_t *)out_bf16 + (size_t)off[d] * H * 2, m.out, (size_t)T * H * 2,
-                                      cudaMemcpyDefault, m.st);
+    for (int phase = 0; phase < 3 && !rc; ++phase) {
+        for (uint32_t d = 0; d < W && !rc; ++d) {
+            Member &m = g->m[d];
+            const uint32_t T = off[d + 1] - off[d];
+            cudaSetDevice(m.dev);
+            if (phase == 0) {
+                rc = (int)cudaStreamWaitEvent(m.st, start, 0);
+                if (!rc && T)
+                    rc = (int)cudaMemcpyAsync(m.x, (const uint8_t *)x_bf16 + (size_t)off[d] * H * 2, (size_t)T * H * 2,
+                                              cudaMemcpyDefault, m.st);
+            }
+            if (!rc) rc = member_forward(g, d, T, phase);
+            if (phase < 2) continue;
+            if (!rc && T) {
+                rc = (int)cudaMemcpyAsync((uint8_t *)out_bf16 + (size_t)off[d] * H * 2, m.out, (size_t)T * H * 2,
+                                          cudaMemcpyDefault, m.st);
+                if (!rc)
+                    rc = (int)cudaMemcpyAsync(ids + (size_t)off[d] * K, m.ids, (size_t)T * K * 4, cudaMemcpyDefault,
+                                              m.st);
+                if (!rc)
+                    rc = (int)cudaMemcpyAsync(wts + (size_t)off[d] * K, m.wts, (size_t)T * K * 4, cudaMemcpyDefault,
+                                              m.st);
+            }
             if (!rc)
-                rc = (int)cudaMemcpyAsync(ids + (size_t)off[d] * K, m.ids, (size_t)T * K * 4, cudaMemcpyDefault, m.st);
-            if (!rc)
-                rc = (int)cudaMemcpyAsync(wts + (size_t)off[d] * K, m.wts, (size_t)T * K * 4, cudaMemcpyDefault, m.st);
+                rc = (int)cudaMemcpyAsync(g->count_parts + (size_t)d * E, m.counts, (size_t)E * 4, cudaMemcpyDefault,
+                                          m.st);
+            if (!rc) rc = (int)cudaEventRecord(m.done, m.st);
         }
-        if (!rc)
-            rc = (int)cudaMemcpyAsync(g->count_parts + (size_t)d * E, m.counts, (size_t)E * 4, cudaMemcpyDefault, m.st);
-        if (!rc) rc = (int)cudaEventRecord(m.done, m.st);
     }
     cudaSetDevice(prev);
     for (uint32_t d = 0; d < W && !rc; ++d) rc = (int)cudaStreamWaitEvent(cs, g->m[d].done, 0);

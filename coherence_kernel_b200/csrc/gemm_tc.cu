@@ -187,8 +187,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = min(*p.ntiles, (int)p.max_tiles);
     const int nrt = (int)((p.N + BM - 1) / BM);
-    const int nunits = ntiles * nrt;
     const int nk = (int)(p.K / BK);
+    // The dense form may give each of its K-chunk accumulators a unit of its own (p.ksplit > 1):
+    // unit u is then (tile, row block) u / ks and K chunk u % ks, and writes that chunk's sums to
+    // plane u % ks of the output for the caller to add in chunk order.
+    const int kchunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
+    const int ks = DENSE && p.ksplit > 1 ? (nk + kchunk - 1) / kchunk : 1;
+    const int nunits = ntiles * nrt * ks;
+    auto krange = [&](int u, int &kb0, int &kb1) {
+        kb0 = ks > 1 ? (u % ks) * kchunk : 0;
+        kb1 = ks > 1 ? min(nk, kb0 + kchunk) : nk;
+    };
     // the x operand's own K steps: the dense form walks x once per bf16 term of the split A
     const int nkx = DENSE && p.kx ? (int)(p.kx / BK) : nk;
 
@@ -227,15 +236,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             int it = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-                const Tile t = load_tile(p.tiles, u / nrt);
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                const Tile t = load_tile(p.tiles, u / ks / nrt);
+                int kb0, kb1;
+                krange(u, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % C::B_ST;
                     const uint32_t ph = (uint32_t)(it / C::B_ST) & 1u;
                     if (!mbar_wait_bounded(&b_empty[s], ph ^ 1u, p.err, 1)) { ok = false; break; }
                     uint8_t *st = smem + C::B_OFF + s * C::B_STAGE;
                     if (DENSE) {
                         mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
-                        tma_load_2d(st, &tmap_a, &b_full[s], kb * BK, (u % nrt) * BM);
+                        tma_load_2d(st, &tmap_a, &b_full[s], kb * BK, (u / ks % nrt) * BM);
                         tma_load_2d(st + A_BYTES, &tmap_x, &b_full[s], (kb % nkx) * BK, t.xrow);
                     } else {
                         // only the boxes that hold the tile's tokens (the MMA reads round16(ntok))
@@ -294,13 +305,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             int sb = 0, sa = 0, ut = 0;
             uint32_t phb = 0, pha = 0;
             bool ok = true;
-            const int chunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
+            const int chunk = kchunk;
             const uint64_t bdesc0 = sdesc_k_sw128(smem_u32(smem + C::B_OFF) + (DENSE ? A_BYTES : 0));
             const uint64_t adesc0 = sdesc_k_sw128(smem_u32(smem + C::B_OFF));  // dense form's A
             const uint32_t atm0 = tmem_base + (uint32_t)C::A_TOFF;              // first A stage (TMEM)
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++ut) {
-                const Tile t = load_tile(p.tiles, u / nrt);
-                if (p.tiles[u / nrt].w > BN) atomicCAS(p.err, 0, 9);
+                const Tile t = load_tile(p.tiles, u / ks / nrt);
+                if (p.tiles[u / ks / nrt].w > BN) atomicCAS(p.err, 0, 9);
+                int kb0, kb1;
+                krange(u, kb0, kb1);
                 int nmma = ((t.ntok + 15) / 16) * 16;
                 const int nmax = DENSE ? C::DENSE_TILE : BN;
                 nmma = nmma < 16 ? 16 : (nmma > nmax ? nmax : nmma);
@@ -310,7 +323,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!mbar_wait_bounded(&acc_empty[ab], aph ^ 1u, p.err, 2)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
-                for (int kb = 0; kb < nk; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if ((!DENSE && !mbar_wait_bounded(&a_full[sa], pha, p.err, 3)) ||
                         !mbar_wait_bounded(&b_full[sb], phb, p.err, 4)) {
                         ok = false;
@@ -454,8 +467,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             return (DUAL && p.row_w && cb * 32 + lane < t.ntok) ? p.row_w[t.orow + cb * 32 + lane] : 1.0f;
         };
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ut) {
-            const Tile t = load_tile(p.tiles, u / nrt);
-            const int n0 = (u % nrt) * BM;
+            const Tile t = load_tile(p.tiles, u / ks / nrt);
+            const int n0 = (u / ks % nrt) * BM;
+            const int kc = u % ks;  // the dense form's K chunk when split over units
             const int ab = ut % C::NBUF;
             const uint32_t aph = (uint32_t)(ut / C::NBUF) & 1u;
             float rw_lane = route_w(t, 0);
@@ -471,10 +485,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (DUAL) tmem_ld32(tbase + BN + cb * 32, v);
                 const float rw_next = route_w(t, cb + 1);
                 tmem_ld_wait();
-                if (DENSE) {
+                if (DENSE && ks > 1 && kc > 0) {
+                    // a split unit holds one K chunk, in accumulator kc
+                    tmem_ld32(tbase + kc * C::DENSE_TILE + cb * 32, g);
+                    tmem_ld_wait();
+                } else if (DENSE && ks == 1) {
                     // sum the K-chunk accumulators in fp32, in chunk order; with fewer than
                     // DENSE_ACC K steps per chunk only the first ceil(nk / chunk) were written
-                    const int kchunk = (nk + C::DENSE_ACC - 1) / C::DENSE_ACC;
                     const int nacc = (nk + kchunk - 1) / kchunk;
 #pragma unroll 1
                     for (int a = 1; a < nacc; ++a) {
@@ -520,7 +537,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 val = __fdividef(val, 1.0f + __expf(-val)) * up * rw;
                             }
                             if (DENSE)
-                                p.out_f32[(uint64_t)(t.orow + tok) * p.N + row] = val;
+                                (kc == 0 ? p.out_f32 : p.out_planes + (uint64_t)(kc - 1) * p.out_rows * p.N)
+                                    [(uint64_t)(t.orow + tok) * p.N + row] = val;
                             else
                                 out[(uint64_t)(t.orow + tok) * p.N + row] = __float2bfloat16_rn(val);
                         }
@@ -625,7 +643,8 @@ static int launch_t(const GemmParams &p, cudaStream_t s) {
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const long long units = (long long)p.max_tiles * ((p.N + BM - 1) / BM);
+    long long units = (long long)p.max_tiles * ((p.N + BM - 1) / BM);
+    if (DENSE && p.ksplit > 1) units *= C::DENSE_ACC;
     const int grid = (int)(units < nsm ? units : nsm);
     if (grid <= 0) return 0;
     k_gemm_q4k<DUAL, DENSE, PT><<<grid, NTHREADS, C::SMEM, s>>>(mx, ma, pm, p);
@@ -650,7 +669,8 @@ int launch_gemm_q4k(const GemmParams &p, cudaStream_t s) {
 }
 
 int launch_gemm_dense(const GemmParams &p, cudaStream_t s) {
-    if (!p.a_dense || !p.x || !p.out_f32 || !p.tiles || !p.ntiles || !p.err) return CK_ERR_ARG;
+    if (!p.a_dense || !p.x || !p.out_f32 || !p.tiles || !p.ntiles || !p.err || (p.ksplit > 1 && !p.out_planes))
+        return CK_ERR_ARG;
     if (p.K % gemm::BK != 0 || p.K == 0 || p.N == 0 || (p.kx && (p.kx % gemm::BK || p.K % p.kx))) return CK_ERR_SHAPE;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.a_dense) & 15)) return CK_ERR_ARG;
     return gemm::launch_t<0, 1, 0>(p, s);

@@ -209,10 +209,15 @@ CK_DEV T warp_sum_t(T v) {
 // (`sabs` holds that sum per logit); the reference's own fold differs from the exact sum by at most
 // 7168 x 2^-53 of it, so a token is flagged only when its margin is below 16 x 2^-40 of its largest
 // sum|w x| -- in practice only exact ties take the fp64 re-route.
+// `planes` (float form): the logits arrive as L plus nplanes more partial planes of [ntok, ne]
+// (the tensor-core GEMM's K chunks 1 .. nplanes, chunk 0 in L); they are added to L in chunk order
+// -- the additions the GEMM's own epilogue makes when it keeps the chunks together -- and the sum is
+// written back to L.
 template <typename T>
 __global__ void k_route_select(const T *__restrict__ L, const float *__restrict__ sabs,
                                const float *__restrict__ bias, int32_t *__restrict__ ids, float *__restrict__ wts,
-                               uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p) {
+                               uint32_t *__restrict__ flag_list, uint32_t *__restrict__ flag_count, RouteParams p,
+                               const float *__restrict__ planes, int nplanes) {
     grid_dep_trigger_small();
     grid_dep_wait();
     constexpr bool CTA = sizeof(T) == 8;  // the fp64 form: a CTA of 256 threads per token
@@ -276,7 +281,12 @@ __global__ void k_route_select(const T *__restrict__ L, const float *__restrict_
         for (int i = 0; i < RMAX; ++i) {
             const int e = 32 * i + lane;
             const bool v = i < nreg && e < (int)p.ne;
-            const T l = v ? L[(size_t)t * p.ne + e] : NEG;
+            T l = v ? L[(size_t)t * p.ne + e] : NEG;
+            if (v && nplanes > 0) {
+                const size_t at = (size_t)t * p.ne + e, plane = (size_t)p.ntok * p.ne;
+                for (int a = 0; a < nplanes; ++a) l = l + (T)planes[a * plane + at];
+                const_cast<T *>(L)[at] = l;
+            }
             if (v) lmax = fmaxf(lmax, sabs ? sabs[(size_t)t * p.ne + e] : fabsf((float)l));
             if (p.mode == 4) {
                 pr[i] = v ? (T)1 / ((T)1 + sel_exp(-l)) : (T)0;
@@ -569,8 +579,9 @@ int launch_router_logits(const uint16_t *x, const float *w, float *L, uint32_t T
     k_router_logits<<<dim3((T + 63) / 64, (E + 63) / 64), 256, 0, s>>>(x, w, L, T, E, H);
     return (int)cudaGetLastError();
 }
-int launch_route_select(const float *L, const float *bias, int32_t *ids, float *wts, uint32_t *flag_list,
-                        uint32_t *flag_count, const RouteParams &p, cudaStream_t s) {
+int launch_route_select(float *L, const float *planes, int nplanes, const float *bias, int32_t *ids, float *wts,
+                        uint32_t *flag_list, uint32_t *flag_count, const RouteParams &p, cudaStream_t s) {
+    if (nplanes < 0 || nplanes > 7 || (nplanes && !planes)) return CK_ERR_ARG;
     if (p.ne == 0 || p.ne > 32 * RMAX || p.nsel == 0 || p.nsel > 16 || p.nsel > p.ne) return CK_ERR_SHAPE;
     if (p.mode == 4 && (p.ngroups == 0 || p.ngroups > 32 || p.ne % p.ngroups || p.topk_groups == 0 ||
                         p.topk_groups > p.ngroups || p.nsel > p.topk_groups * (p.ne / p.ngroups)))
@@ -579,7 +590,7 @@ int launch_route_select(const float *L, const float *bias, int32_t *ids, float *
     cudaMemsetAsync(flag_count, 0, sizeof(uint32_t), s);
     if (p.ntok)
         k_route_select<float><<<(p.ntok * 32 + 255) / 256, 256, 0, s>>>(L, nullptr, bias, ids, wts, flag_list,
-                                                                          flag_count, p);
+                                                                          flag_count, p, planes, nplanes);
     return (int)cudaGetLastError();
 }
 int launch_route_select_d(const double *L, const float *sabs, const float *bias, int32_t *ids, float *wts,
@@ -593,7 +604,7 @@ int launch_route_select_d(const double *L, const float *sabs, const float *bias,
     // flag_count was cleared by launch_router_logits_few, the kernel before this one
     if (p.ntok) {
         const cudaError_t e = launch_pdl(k_route_select<double>, dim3(p.ntok), dim3(256), 0, s, L, sabs, bias, ids, wts,
-                                         flag_list, flag_count, p);
+                                         flag_list, flag_count, p, (const float *)nullptr, 0);
         if (e != cudaSuccess) return (int)e;
     }
     return (int)cudaGetLastError();
