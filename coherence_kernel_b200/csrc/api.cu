@@ -25,8 +25,11 @@ inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 // The router logits GEMM gives each K-chunk accumulator a work unit of its own when its unsplit
 // units (64-token tiles x 128-expert blocks) would fill at most half the GPU's 148 SMs; beyond that
 // the short units' pipeline fills and the partial planes' traffic cost more than they save.
+inline uint32_t route_ksplit_max(const ck_moe_config *c) {  // the largest batch that splits
+    return 64u * (74u / ((c->n_experts + 127) / 128));
+}
 inline bool route_ksplit(const ck_moe_config *c, uint32_t ntok) {
-    return ntok > CK_MOE_DECODE_TOKENS && (uint64_t)((ntok + 63) / 64) * ((c->n_experts + 127) / 128) <= 74;
+    return ntok > CK_MOE_DECODE_TOKENS && ntok <= route_ksplit_max(c);
 }
 inline size_t al(size_t b) { return (b + 255) & ~(size_t)255; }
 
@@ -57,7 +60,10 @@ RouteWs route_ws(const ck_moe_config *c, uint32_t ntok, void *base) {
     w.exact = (double *)take((size_t)ntok * c->n_experts * 8);
     w.sabs = (float *)take((size_t)ntok * c->n_experts * 4);
     w.w64 = (double *)take((size_t)c->n_experts * c->hidden * 8);
-    w.planes = route_ksplit(c, ntok) ? (float *)take((size_t)7 * ntok * c->n_experts * 4) : nullptr;
+    // sized for min(ntok, the largest split batch) above the decode sizes, so that the workspace
+    // grows with ntok: one sized for a batch holds every smaller one
+    const uint32_t np = ntok > CK_MOE_DECODE_TOKENS ? (ntok < route_ksplit_max(c) ? ntok : route_ksplit_max(c)) : 0;
+    w.planes = np ? (float *)take((size_t)7 * np * c->n_experts * 4) : nullptr;
     w.total = o;
     return w;
 }

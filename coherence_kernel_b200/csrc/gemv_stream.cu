@@ -25,7 +25,8 @@
 //     memory in warp order -- a fixed order, so results are deterministic.
 // Launched with programmatic stream serialization: the next kernel in the stream may be scheduled
 // while this one drains, and every thread waits for the previous kernel (griddepcontrol.wait)
-// before its first global access, so stream order is kept.
+// before it reads x or writes y, so stream order is kept; only the producers' first stages of
+// packed weights, which no kernel of this library writes, are copied before that wait.
 // Every wait is bounded (about one second); a row group whose wait gives up writes NaN to its
 // remaining rows.
 #include "ck_common.cuh"
@@ -328,9 +329,12 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_stream(const uint8_t *__restri
             const uint32_t rg = warp, nkg = nk > rg ? (nk - rg + NRG - 1) / NRG : 0;
             uint64_t *full = bars + rg * g.nsub, *empty = bars + nst + rg * g.nsub;
             uint8_t *ring = smem + g.ring_off + rg * g.nsub * g.stage_bytes;
-            pdl_wait();
+            // the weights are never written by the kernel before this one (no kernel of this library
+            // writes packed weights): the sub-ring's first stages are filled before the wait on it,
+            // overlapping its tail
             uint32_t kk = 0;
             for (; kk < nkg; ++kk) {
+                if (kk == g.nsub) pdl_wait();
                 const uint32_t st = kk % g.nsub, ph = (kk / g.nsub) & 1u;
                 if (!mbar_wait_bounded(&empty[st], ph ^ 1u, nullptr, 0)) break;
                 const uint32_t r0 = (blockIdx.x + (kk * NRG + rg) * gridDim.x) * GR;
@@ -338,6 +342,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_stream(const uint8_t *__restri
                 mbar_arrive_expect_tx(&full[st], bytes);
                 bulk_g2s(ring + st * g.stage_bytes, qb + (uint64_t)r0 * g.row_bytes, bytes, &full[st]);
             }
+            if (kk <= g.nsub) pdl_wait();
             // the copies issued must land before the CTA exits: wait for the last min(nsub, kk)
             for (uint32_t d = 0; d < g.nsub && d < kk; ++d) {
                 const uint32_t j = kk - 1 - d;

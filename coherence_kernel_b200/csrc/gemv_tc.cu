@@ -153,15 +153,26 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
     cluster_arrive();
     const uint32_t tmem = *tmem_slot;
     pdl_launch_dependents();
-    // weights and x may be written by the kernel before this one
-    pdl_wait();
+    // x may be written by the kernel before this one, and y read by it: every warp but the weight
+    // producer waits for it here.  The packed weights are never written by the kernel before (no
+    // kernel of this library writes them), so the producer fills the first stages first and waits
+    // after, and those loads overlap the previous kernel's tail.
+    if (warp != 0) pdl_wait();
 
     if (warp == 0) {
         // ------------------------------------------------------------ weights: TMA producer
         if (lane == 0) {
             prefetch_tmap(&wmap);
             int issued = 0;
-            for (int j = 0; j < nj; ++j) {
+            const int early = nj < WST ? nj : WST;
+            for (int j = 0; j < early; ++j) {
+                mbar_arrive_expect_tx(&w_full[j], p.trows * Q4K_BYTES);
+                tma_load_2d_u8(smem + W_OFF + j * W_STAGE, &wmap, &w_full[j], (int)((sb0 + j) * Q4K_BYTES),
+                               (int)row0);
+                issued = j + 1;
+            }
+            pdl_wait();
+            for (int j = early; j < nj; ++j) {
                 const int s = j % WST;
                 if (!mbar_wait_bounded(&w_empty[s], ((j / WST) & 1) ^ 1, err, 1)) break;
                 mbar_arrive_expect_tx(&w_full[s], p.trows * Q4K_BYTES);
@@ -173,6 +184,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
             // be outstanding; after a normal run all of them have long completed)
             for (int j = issued > WST ? issued - WST : 0; j < issued; ++j)
                 mbar_wait_bounded(&w_full[j % WST], (j / WST) & 1, nullptr, 0);
+        } else {
+            pdl_wait();
         }
         __syncwarp();  // the warp reaches the CTA barrier below as a whole
     } else if (warp == 1) {

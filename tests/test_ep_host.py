@@ -75,3 +75,35 @@ def test_ep_exchange_round_trip_gloo(world, E, K, T, H):
     mp.start_processes(_worker, args=(world, _free_port(), E, K, T, H, ret), nprocs=world, join=True,
                        start_method="spawn")
     assert dict(ret) == {r: True for r in range(world)}
+
+
+def _worker_drop(rank, world, port, ret):
+    """Rank 1 leaves between steps (before the sizes exchange); rank 0's exchange must end with an
+    error within the process group's short timeout rather than wait for good."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    ids = torch.tensor([[0, 1]], dtype=torch.int32)
+    er, mask, srow, spair = ep_dispatch_counts(ids, 1, world)
+    sizes = torch.stack([srow, spair], dim=1).to(torch.int64)
+    if rank == 1:
+        ret[rank] = "left"
+        os._exit(0)  # no collective in flight: the rank leaves between steps
+    t0 = time.monotonic()
+    try:
+        dist.all_to_all_single(torch.empty_like(sizes), sizes)
+        ret[rank] = "completed"
+    except Exception:
+        ret[rank] = "raised" if time.monotonic() - t0 < 60 else "late"
+    os._exit(0)
+
+
+def test_ep_exchange_detects_a_missing_rank():
+    mgr = mp.get_context("spawn").Manager()
+    ret = mgr.dict()
+    ctx = mp.start_processes(_worker_drop, args=(2, _free_port(), ret), nprocs=2, join=False, start_method="spawn")
+    for p in ctx.processes:
+        p.join(120)
+    assert dict(ret) == {0: "raised", 1: "left"}

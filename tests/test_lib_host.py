@@ -92,3 +92,20 @@ def test_decode_step_create_and_destroy_on_the_host(cuda_lib):
     bad = _lib.DecodeConfig(7000, 16, 1e-6, workloads.MOE_DSV3.cfg())
     assert L.ck_decode_step_workspace_bytes(ctypes.byref(bad)) == 0                          # hidden mismatch
     assert L.ck_decode_step_replay(None, None) == -3
+
+
+def test_workspaces_grow_with_the_batch():
+    """A workspace sized for a batch must hold every smaller batch (callers size it once for their
+    largest): the route's and the layer's byte counts never fall as ntok grows, across the decode
+    sizes, the split-K router sizes and beyond."""
+    import ctypes
+    from coherence_kernel_b200 import _lib, workloads
+    L = _lib.load()
+    for spec in (workloads.MOE_DSV3, workloads.MOE_SMALL):
+        cfg = spec.cfg()
+        for fn in (L.ck_moe_route_workspace_bytes, L.ck_moe_workspace_bytes):
+            prev = 0
+            for n in list(range(1, 5200, 13)) + [8192, 16384]:
+                b = fn(ctypes.byref(cfg), n)
+                assert b >= prev, (spec, n)
+                prev = b
