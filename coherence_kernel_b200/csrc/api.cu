@@ -394,7 +394,7 @@ int ck_router_exact_logits(const void *x, const float *rw, const uint32_t *token
                            uint32_t n_experts, uint32_t hidden, double *out, double *router_f64, void *s) {
     if (!x || !rw || !tokens || !count || !out || !router_f64) return fail(CK_EARG, "ck_router_exact_logits");
     return fail(ck::launch_exact_logits((const uint16_t *)x, rw, tokens, count, out, router_f64, n_experts, hidden,
-                                        S(s)),
+                                        0xffffffffu, S(s)),
                 "ck_router_exact_logits");
 }
 

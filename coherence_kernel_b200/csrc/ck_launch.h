@@ -67,9 +67,10 @@ int launch_route_select(float *logits, const float *planes, int nplanes, const f
                         uint32_t *flag_list, uint32_t *flag_count, const RouteParams &p, cudaStream_t s);
 // scratch: fp64 [ntok, ne] (the exact logits of the flagged tokens)
 // out fp64 [*flag_count, ne]: the right-fold logits of the listed tokens (at most 256 experts,
-// hidden % 32 == 0); w64: scratch for the router in fp64, ne * hidden doubles
+// hidden % 32 == 0); w64: scratch for the router in fp64, ne * hidden doubles; max_count: a bound
+// on *flag_count known to the host (the batch's tokens)
 int launch_exact_logits(const uint16_t *x_bf16, const float *w, const uint32_t *flag_list, const uint32_t *flag_count,
-                        double *out, double *w64, uint32_t ne, uint32_t hidden, cudaStream_t s);
+                        double *out, double *w64, uint32_t ne, uint32_t hidden, uint32_t max_count, cudaStream_t s);
 int launch_route_exact(const uint16_t *x_bf16, const float *w, const float *bias, int32_t *ids, float *wts,
                        const uint32_t *flag_list, const uint32_t *flag_count, double *scratch, double *w64,
                        const RouteParams &p, cudaStream_t s);

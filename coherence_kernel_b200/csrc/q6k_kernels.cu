@@ -96,7 +96,7 @@ struct Geo {
     uint32_t U, tpr, slots, upt;   // units per row, threads per row slot, row slots, units per thread
     uint32_t rs, rpt;              // rows per stage, rows a thread folds per stage (rs / slots)
     uint32_t stage_alloc;          // bytes of one stage buffer (16 bytes of slack past the rows)
-    uint32_t tab_off, red_off;     // d*sc table, cross-warp partials
+    uint32_t red_off;              // cross-warp partials
 };
 
 CK_DEV void cp_async16(void *dst, const void *src) {
@@ -140,7 +140,6 @@ template <int UPT>
 __global__ void __launch_bounds__(NTHR, UPT <= 2 ? 2 : 1)
     k_q6k_stream(const uint8_t *__restrict__ qb, const float *__restrict__ x, float *__restrict__ y, Geo g) {
     extern __shared__ __align__(128) uint8_t smem[];
-    float *tab = reinterpret_cast<float *>(smem + g.tab_off);
     float *red = reinterpret_cast<float *>(smem + g.red_off);
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t slot = t / g.tpr, lt = t % g.tpr;
@@ -148,7 +147,7 @@ __global__ void __launch_bounds__(NTHR, UPT <= 2 ? 2 : 1)
 
     // this thread's units: u = lt + tpr * k; unit u = (superblock u / 16, sub = u % 16), sub = 8 ip + il
     XUnit xu[UPT];
-    uint32_t uoff[UPT], hoff[UPT], toff[UPT];
+    uint32_t uoff[UPT], hoff[UPT], soff[UPT], doff[UPT];
 #pragma unroll
     for (int k = 0; k < UPT; ++k) {
         const uint32_t u = lt + g.tpr * k;
@@ -156,7 +155,8 @@ __global__ void __launch_bounds__(NTHR, UPT <= 2 ? 2 : 1)
         const uint32_t sb = live ? u >> 4 : 0, sub = u & 15, ip = sub >> 3, il = sub & 7;
         uoff[k] = sb * Q6K_BYTES + 64 * ip + 4 * il;   // ql bytes of groups 0 / 2 (and +32: 1 / 3)
         hoff[k] = sb * Q6K_BYTES + 128 + 32 * ip + 4 * il;  // qh bytes
-        toff[k] = sb * 16 + ip * 8 + (il >> 2) * 4;
+        soff[k] = sb * Q6K_BYTES + 192 + 8 * ip + (il >> 2);  // the unit's four scales: +0, +2, +4, +6
+        doff[k] = sb * Q6K_BYTES + 208;                       // d (f16)
         const float *xs = x + sb * 256 + 128 * ip + 4 * il;
 #pragma unroll
         for (int gq = 0; gq < 4; ++gq) {
@@ -177,16 +177,6 @@ __global__ void __launch_bounds__(NTHR, UPT <= 2 ? 2 : 1)
         if (grp + gridDim.x < ngrp) cp_async_wait<1>();
         else cp_async_wait<0>();
         __syncthreads();
-        // d * sc of every (row, superblock, sub-block) of the stage, exact in fp32; ordered so a
-        // unit's four sub-block factors are one float4: [sb][ip][is][g]
-        for (uint32_t e = t; e < nr * g.nsb * 16; e += NTHR) {
-            const uint32_t i = e / (g.nsb * 16), rem = e - i * g.nsb * 16, sb = rem >> 4, kk = rem & 15;
-            const uint32_t ip = kk >> 3, is = (kk >> 2) & 1, gq = kk & 3;
-            const uint8_t *b = buf + i * g.rb + sb * Q6K_BYTES;
-            const float d = f16_bits_to_float((uint32_t)b[208] | ((uint32_t)b[209] << 8));
-            tab[i * g.nsb * 16 + rem] = d * (float)(int)(int8_t)b[192 + 8 * ip + is + 2 * gq];
-        }
-        __syncthreads();
         float acc[MAX_RPT];
 #pragma unroll
         for (int j = 0; j < MAX_RPT; ++j) acc[j] = 0.0f;
@@ -200,7 +190,12 @@ __global__ void __launch_bounds__(NTHR, UPT <= 2 ? 2 : 1)
                 if (i >= nr) break;
                 const uint8_t *row = buf + i * g.rb;
                 const uint32_t A = lds32(row + uoff[ku]), B = lds32(row + uoff[ku] + 32), H = lds32(row + hoff[ku]);
-                const float4 ds = *reinterpret_cast<const float4 *>(tab + i * g.nsb * 16 + toff[ku]);
+                // d * sc of the unit's four sub-blocks (exact in fp32): scales at +0, +2, +4, +6 of
+                // soff, d the f16 at byte 208 of the superblock (the stage carries 16 bytes of slack)
+                const uint32_t S0 = lds32(row + soff[ku]), S1 = lds32(row + soff[ku] + 4);
+                const float d = f16_bits_to_float(lds32(row + doff[ku]) & 0xFFFFu);
+                const float4 ds = make_float4(d * (float)(int)(int8_t)(S0 & 0xFFu), d * (float)(int)(int8_t)(S0 >> 16),
+                                              d * (float)(int)(int8_t)(S1 & 0xFFu), d * (float)(int)(int8_t)(S1 >> 16));
                 const uint32_t q0 = (A & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
                 const uint32_t q1 = (B & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
                 const uint32_t q2 = ((A >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
@@ -223,7 +218,7 @@ __global__ void __launch_bounds__(NTHR, UPT <= 2 ? 2 : 1)
                 acc[j] = a;
             }
         }
-        __syncthreads();  // every read of this buffer and of the table is done
+        __syncthreads();  // every read of this buffer is done
         if (grp + 2 * gridDim.x < ngrp) load_stage(g, qb, bufs[k & 1], grp + 2 * gridDim.x);
         // row sums: over the lanes of a warp that share a slot, then over the slot's warps in order
         const uint32_t wl = g.tpr < 32 ? g.tpr : 32;
@@ -278,8 +273,7 @@ bool plan(uint32_t rows, uint32_t cols, Geo &g) {
         const uint32_t cand = unit * m;
         if (cand / g.slots > (uint32_t)MAX_RPT || cand > 32 * 8) break;
         const uint32_t alloc = (cand * g.rb + 16 + 127) & ~127u;
-        const uint32_t tab = (cand * g.nsb * 16 * 4 + 127) & ~127u;
-        if (2 * alloc + tab + cand * 32 * 4 > SMEM_MAX) break;
+        if (2 * alloc + cand * 32 * 4 > SMEM_MAX) break;
         rs = cand;
         if (cand * g.rb >= 24 * 1024) break;  // enough bytes in flight per stage
     }
@@ -287,8 +281,7 @@ bool plan(uint32_t rows, uint32_t cols, Geo &g) {
     g.rs = rs;
     g.rpt = rs / g.slots;
     g.stage_alloc = (rs * g.rb + 16 + 127) & ~127u;
-    g.tab_off = 2 * g.stage_alloc;
-    g.red_off = g.tab_off + ((rs * g.nsb * 16 * 4 + 127) & ~127u);
+    g.red_off = 2 * g.stage_alloc;
     return true;
 }
 

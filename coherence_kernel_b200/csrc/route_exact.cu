@@ -50,18 +50,19 @@ CK_DEV double ref_sigmoid(double x) { return __ddiv_rn(1.0, __dadd_rn(1.0, ref_e
 //
 // Many flagged tokens (k_exact_logits): the router is first converted to fp64 (k_router_f64,
 // skipped otherwise).  A work item is 16 tokens x 64 experts on a CTA of four warps; warp q folds
-// tokens 4q .. 4q+3 and lane l experts l and l + 32, eight chains per thread.  Tiles of 32 columns
+// tokens 4q .. 4q+3 and lane l experts l and l + 32, eight chains per thread (16 x 32 and four
+// chains when the 64-expert items would leave more than half the CTAs without one).  Tiles of 32 columns
 // (the last tile first) arrive by cp.async in a ring of XT_NS stages; the router rows are read from
 // the ring with 16-byte loads at a 34-double pitch (conflict-free per quarter warp), the tile's
 // activations are converted into one of two fp64 buffers a tile ahead.  One CTA barrier per tile.
 // Few flagged tokens (a decode step, or a rank's share of a batch; k_exact_logits_few): a work
 // item is 4 tokens x 32 experts on a CTA of four warps, warp q folding token q, lane l expert l --
-// enough warps to fill the GPU, each folding one chain.  Stages of 16 columns go through a CTA-wide
+// enough warps to fill the GPU, each folding one chain.  Stages of 32 columns go through a CTA-wide
 // cp.async ring of XF_NB stages: the 32 experts' fp32 row pieces (four threads to a row, so each
 // copy instruction moves whole lines; a thread per row would keep 32 scattered sectors in flight
 // per instruction and run into the SM's limit on outstanding requests) and the four tokens'
 // activations, converted to fp64 once, two stages ahead.  The router is shared by the item's four
-// tokens through the ring (one read of it from L2 per four tokens), and each lane converts its 16
+// tokens through the ring (one read of it from L2 per four tokens), and each lane converts its 32
 // router values of the next stage while it folds the current one (converting them once per CTA
 // into shared memory instead measured slower).  It is launched without programmatic dependent
 // launch: launched early, beside the kernels before it, its CTAs were placed so that up to 51
@@ -78,12 +79,12 @@ struct XtSmem {
     double xd[2][XT_TOK][XL_J];         // converted
 };
 constexpr uint32_t XL_FEW = 128;  // at most this many flagged tokens take the few-token form
-constexpr int XF_C = 16;          // columns per stage
+constexpr int XF_C = 32;          // columns per stage
 constexpr int XF_NB = 8;          // ring stages
 constexpr int XF_W = 4;           // warps per CTA = tokens per work item
 struct XfRing {
     float4 w[XF_NB][32][XF_C / 4 + 1];  // [stage][expert][column quad], one pad quad: conflict-free per quarter warp
-    uint4 x[XF_NB][XF_W][2];            // [stage][token][8 columns]
+    uint4 x[XF_NB][XF_W][XF_C / 8];     // [stage][token][8 columns]
     double xd[XF_NB][XF_W][XF_C];       // [stage][token][column]
 };
 CK_DEV void cp_async16(void *dst, const void *src) {
@@ -121,28 +122,40 @@ __global__ void __launch_bounds__(XF_W * 32) k_exact_logits_few(const uint16_t *
     for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
         const uint32_t f0 = (item / neg) * XF_W, e = (item % neg) * 32 + lane, f = f0 + wq;
         const bool live = e < ne && f < nflag;
-        // thread i copies chunk i % 4 of router row i / 4 (rows past ne repeat the last row) and,
-        // for i < 8, half i % 2 of token i / 2's activations (tokens past nflag repeat the last one)
-        const float *wr = W + (size_t)min((item % neg) * 32 + (uint32_t)(tid / 4), ne - 1) * hidden + 4 * (tid % 4);
-        const uint16_t *xr = x + (size_t)flag_list[min(f0 + (uint32_t)(tid / 2 % XF_W), nflag - 1)] * hidden +
-                             8 * (tid % 2);
-        // stage s holds columns 16 (nst-1-s) .. +15 (the fold runs from the last column down)
+        // a stage's router piece is 32 rows of XF_C / 4 16-byte chunks: thread i copies chunk
+        // (i + 128 k) % CPR of row (i + 128 k) / CPR (rows past ne repeat the last row); threads below
+        // XF_W * XPR copy chunk i % XPR of token i / XPR's activations (tokens past nflag repeat the
+        // last one)
+        constexpr int CPR = XF_C / 4, CPT = 32 * CPR / (XF_W * 32), XPR = XF_C / 8;
+        const float *wr[CPT];
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+            const uint32_t i = (uint32_t)(tid + XF_W * 32 * k);
+            wr[k] = W + (size_t)min((item % neg) * 32 + i / CPR, ne - 1) * hidden + 4 * (i % CPR);
+        }
+        const uint16_t *xr = x + (size_t)flag_list[min(f0 + (uint32_t)(tid / XPR % XF_W), nflag - 1)] * hidden +
+                             8 * (tid % XPR);
+        // stage s holds columns XF_C (nst-1-s) .. + XF_C - 1 (the fold runs from the last column down)
         auto issue = [&](int s) {
             if (s < nst) {
                 const int j = XF_C * (nst - 1 - s), b = s % XF_NB;
-                cp_async16(&r.w[b][tid / 4][tid % 4], wr + j);
-                if (tid < 2 * XF_W) cp_async16(&r.x[b][tid / 2][tid % 2], xr + j);
+#pragma unroll
+                for (int k = 0; k < CPT; ++k) {
+                    const int i = tid + XF_W * 32 * k;
+                    cp_async16(&r.w[b][i / CPR][i % CPR], wr[k] + j);
+                }
+                if (tid < XF_W * XPR) cp_async16(&r.x[b][tid / XPR][tid % XPR], xr + j);
             }
             cp_async_commit();  // an empty group past the end keeps the wait count uniform
         };
-        auto convert_x = [&](int s) {  // the stage's 64 activations, one per thread of warps 0-1
+        auto convert_x = [&](int s) {  // the stage's XF_C * XF_W activations, one per thread
             if (s < nst && tid < XF_C * XF_W) {
                 const int b = s % XF_NB, t = tid / XF_C, c = tid % XF_C;
                 const uint16_t h = reinterpret_cast<const uint16_t *>(&r.x[b][t][0])[c];
                 r.xd[b][t][c] = (double)bf16_bits_to_float(h);
             }
         };
-        auto load_w = [&](int s, double (&wv)[XF_C]) {  // the lane's 16 router values, in fp64
+        auto load_w = [&](int s, double (&wv)[XF_C]) {  // the lane's XF_C router values, in fp64
             const int b = s % XF_NB;
 #pragma unroll
             for (int c = 0; c < XF_C / 4; ++c) {
@@ -189,26 +202,24 @@ __global__ void __launch_bounds__(XF_W * 32) k_exact_logits_few(const uint16_t *
     }
 }
 
-__global__ void __launch_bounds__(XT_THREADS) k_exact_logits(const uint16_t *__restrict__ x, const double *__restrict__ W,
-                                                             const uint32_t *__restrict__ flag_list,
-                                                             const uint32_t *__restrict__ flag_count,
-                                                             double *__restrict__ out, uint32_t ne, uint32_t hidden) {
-    grid_dep_trigger_small();
-    grid_dep_wait();
-    extern __shared__ __align__(16) uint8_t xt_smem[];
-    XtSmem &S = *reinterpret_cast<XtSmem *>(xt_smem);
-    const uint32_t nflag = *flag_count;
-    if (nflag <= XL_FEW) return;  // k_exact_logits_few takes them
+// One work item set of the tiled form: NE2 experts per lane (XT_TOK tokens x 32 NE2 experts per
+// item).  NE2 = 2 shares each activation load between two experts; NE2 = 1 halves the items' size,
+// for batches whose items would leave most SMs idle.
+template <int NE2>
+CK_DEV void exact_tiled(const uint16_t *__restrict__ x, const double *__restrict__ W,
+                        const uint32_t *__restrict__ flag_list, uint32_t nflag, double *__restrict__ out, uint32_t ne,
+                        uint32_t hidden, XtSmem &S) {
+    constexpr int EXP = 32 * NE2, RPT = EXP / 8;  // experts per item; router rows each thread copies from
     const int tid = threadIdx.x, lane = tid & 31, q = tid >> 5;
-    const uint32_t ntg = (nflag + XT_TOK - 1) / XT_TOK, neg = (ne + XT_EXP - 1) / XT_EXP;
+    const uint32_t ntg = (nflag + XT_TOK - 1) / XT_TOK, neg = (ne + EXP - 1) / EXP;
     const int ntile = (int)(hidden / XL_J);
     for (uint32_t item = blockIdx.x; item < ntg * neg; item += gridDim.x) {
-        const uint32_t f0 = (item / neg) * XT_TOK, e0 = (item % neg) * XT_EXP;
-        // this thread's 16-byte pieces of a tile: eight of router rows (16 per row; rows past ne
+        const uint32_t f0 = (item / neg) * XT_TOK, e0 = (item % neg) * EXP;
+        // this thread's 16-byte pieces of a tile: RPT of router rows (16 per row; rows past ne
         // repeat the last row: read, never written) and, for threads 0-63, a quarter of a token row
-        const double *wsrc[8];
+        const double *wsrc[RPT];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < RPT; ++k) {
             const uint32_t e = min(e0 + (uint32_t)(tid / 16 + 8 * k), ne - 1);
             wsrc[k] = W + (size_t)e * hidden + 2 * (tid % 16);
         }
@@ -218,7 +229,7 @@ __global__ void __launch_bounds__(XT_THREADS) k_exact_logits(const uint16_t *__r
             if (tile < ntile) {
                 const int slot = tile % XT_NS, j0 = (int)hidden - XL_J * (tile + 1);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) cp_async16(&S.w[slot][tid / 16 + 8 * k][2 * (tid % 16)], wsrc[k] + j0);
+                for (int k = 0; k < RPT; ++k) cp_async16(&S.w[slot][tid / 16 + 8 * k][2 * (tid % 16)], wsrc[k] + j0);
                 if (tid < 4 * XT_TOK) cp_async16(&S.x[slot][tid / 4][8 * (tid % 4)], xsrc + j0);
             }
             cp_async_commit();
@@ -238,9 +249,11 @@ __global__ void __launch_bounds__(XT_THREADS) k_exact_logits(const uint16_t *__r
         cp_async_wait<XT_NS - 2>();  // tile 0 has landed
         __syncthreads();
         convert(0);
-        double a[4][2];
+        double a[4][NE2];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) a[t][0] = a[t][1] = 0.0;
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+            for (int c = 0; c < NE2; ++c) a[t][c] = 0.0;
         for (int tile = 0; tile < ntile; ++tile) {
             cp_async_wait<XT_NS - 3>();  // tiles up to tile + 1 have landed
             __syncthreads();             // ... for every thread; tile - 1 is folded, buffer tile & 1 converted
@@ -248,31 +261,34 @@ __global__ void __launch_bounds__(XT_THREADS) k_exact_logits(const uint16_t *__r
             convert(tile + 1);
             const int slot = tile % XT_NS, b = tile & 1;
             // columns jj + 1, then jj: descending j; the next pair's operands load while this one folds
-            double2 wa = *reinterpret_cast<const double2 *>(&S.w[slot][lane][XL_J - 2]);
-            double2 wb = *reinterpret_cast<const double2 *>(&S.w[slot][lane + 32][XL_J - 2]);
-            double2 xx[4];
+            double2 w[NE2], xx[4];
+#pragma unroll
+            for (int c = 0; c < NE2; ++c) w[c] = *reinterpret_cast<const double2 *>(&S.w[slot][lane + 32 * c][XL_J - 2]);
 #pragma unroll
             for (int t = 0; t < 4; ++t) xx[t] = *reinterpret_cast<const double2 *>(&S.xd[b][4 * q + t][XL_J - 2]);
 #pragma unroll
             for (int jj = XL_J - 2; jj >= 0; jj -= 2) {
-                double2 wa2 = wa, wb2 = wb, xx2[4];
+                double2 w2[NE2], xx2[4];
+#pragma unroll
+                for (int c = 0; c < NE2; ++c) w2[c] = w[c];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) xx2[t] = xx[t];
                 if (jj >= 2) {
-                    wa2 = *reinterpret_cast<const double2 *>(&S.w[slot][lane][jj - 2]);
-                    wb2 = *reinterpret_cast<const double2 *>(&S.w[slot][lane + 32][jj - 2]);
+#pragma unroll
+                    for (int c = 0; c < NE2; ++c)
+                        w2[c] = *reinterpret_cast<const double2 *>(&S.w[slot][lane + 32 * c][jj - 2]);
 #pragma unroll
                     for (int t = 0; t < 4; ++t) xx2[t] = *reinterpret_cast<const double2 *>(&S.xd[b][4 * q + t][jj - 2]);
                 }
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
-                    a[t][0] = __fma_rn(wa.y, xx[t].y, a[t][0]);
-                    a[t][1] = __fma_rn(wb.y, xx[t].y, a[t][1]);
-                    a[t][0] = __fma_rn(wa.x, xx[t].x, a[t][0]);
-                    a[t][1] = __fma_rn(wb.x, xx[t].x, a[t][1]);
+#pragma unroll
+                    for (int c = 0; c < NE2; ++c) a[t][c] = __fma_rn(w[c].y, xx[t].y, a[t][c]);
+#pragma unroll
+                    for (int c = 0; c < NE2; ++c) a[t][c] = __fma_rn(w[c].x, xx[t].x, a[t][c]);
                 }
-                wa = wa2;
-                wb = wb2;
+#pragma unroll
+                for (int c = 0; c < NE2; ++c) w[c] = w2[c];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) xx[t] = xx2[t];
             }
@@ -283,12 +299,30 @@ __global__ void __launch_bounds__(XT_THREADS) k_exact_logits(const uint16_t *__r
             const uint32_t f = f0 + 4 * q + t;
             if (f >= nflag) continue;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            for (int c = 0; c < NE2; ++c) {
                 const uint32_t e = e0 + lane + 32 * c;
                 if (e < ne) out[(size_t)f * ne + e] = a[t][c];
             }
         }
     }
+}
+
+__global__ void __launch_bounds__(XT_THREADS, 1) k_exact_logits(const uint16_t *__restrict__ x, const double *__restrict__ W,
+                                                             const uint32_t *__restrict__ flag_list,
+                                                             const uint32_t *__restrict__ flag_count,
+                                                             double *__restrict__ out, uint32_t ne, uint32_t hidden) {
+    grid_dep_trigger_small();
+    grid_dep_wait();
+    extern __shared__ __align__(16) uint8_t xt_smem[];
+    XtSmem &S = *reinterpret_cast<XtSmem *>(xt_smem);
+    const uint32_t nflag = *flag_count;
+    if (nflag <= XL_FEW) return;  // k_exact_logits_few takes them
+    // 64-expert items while they fill more than half the CTAs, else 32-expert items (twice as many)
+    const uint32_t items64 = (nflag + XT_TOK - 1) / XT_TOK * ((ne + 63) / 64);
+    if (2 * items64 <= gridDim.x)
+        exact_tiled<1>(x, W, flag_list, nflag, out, ne, hidden, S);
+    else
+        exact_tiled<2>(x, W, flag_list, nflag, out, ne, hidden, S);
 }
 
 // (value, index) maximum over the warp: the larger value, the lower index on a tie -- the
@@ -451,10 +485,10 @@ __global__ void __launch_bounds__(256) k_exact_select(const double *__restrict__
     }
 }
 
-// The reference's right-fold logits of the listed tokens: out[f * ne + e] for f < *count; w64 is
-// scratch for the router in fp64 (ne * hidden doubles).
+// The reference's right-fold logits of the listed tokens: out[f * ne + e] for f < *count <= max_count;
+// w64 is scratch for the router in fp64 (ne * hidden doubles).
 int launch_exact_logits(const uint16_t *x, const float *w, const uint32_t *flag_list, const uint32_t *flag_count,
-                        double *out, double *w64, uint32_t ne, uint32_t hidden, cudaStream_t s) {
+                        double *out, double *w64, uint32_t ne, uint32_t hidden, uint32_t max_count, cudaStream_t s) {
     if (ne == 0 || ne > 256 || hidden == 0 || hidden % XL_J != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
         (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(w64) & 15))
         return CK_ERR_SHAPE;
@@ -471,15 +505,18 @@ int launch_exact_logits(const uint16_t *x, const float *w, const uint32_t *flag_
         if (e != cudaSuccess) return (int)e;
         attr_mark(attrs);
     }
-    cudaError_t e = launch_pdl(k_router_f64, dim3(nsm), dim3(256), 0, s, reinterpret_cast<const float4 *>(w),
-                               reinterpret_cast<double2 *>(w64), (size_t)ne * hidden / 4, flag_count);
-    // both forms are launched; each returns at once unless the flagged count is its own.  The tiled
-    // form runs one CTA per SM (shared-memory bandwidth is its bound) over its work items.
+    // both forms are launched (the tiled one, with the router's fp64 copy, only where the count can
+    // exceed XL_FEW); each returns at once unless the flagged count is its own.  The tiled form runs
+    // one CTA per SM (shared-memory bandwidth is its bound) over its work items.
+    const bool tiled = max_count > XL_FEW;
+    cudaError_t e = tiled ? launch_pdl(k_router_f64, dim3(nsm), dim3(256), 0, s, reinterpret_cast<const float4 *>(w),
+                                       reinterpret_cast<double2 *>(w64), (size_t)ne * hidden / 4, flag_count)
+                          : cudaSuccess;
     if (e == cudaSuccess) {
         k_exact_logits_few<<<2 * nsm, XF_W * 32, sizeof(XfRing), s>>>(x, w, flag_list, flag_count, out, ne, hidden);
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess)
+    if (e == cudaSuccess && tiled)
         e = launch_pdl(k_exact_logits, dim3(nsm), dim3(XT_THREADS), sizeof(XtSmem), s, x, (const double *)w64,
                        flag_list, flag_count, out, ne, hidden);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
@@ -489,7 +526,7 @@ int launch_route_exact(const uint16_t *x, const float *w, const float *bias, int
                        const uint32_t *flag_list, const uint32_t *flag_count, double *scratch, double *w64,
                        const RouteParams &p, cudaStream_t s) {
     if (p.nsel > 16 || (p.mode == 4 && p.ngroups > 32)) return CK_ERR_SHAPE;
-    int rc = launch_exact_logits(x, w, flag_list, flag_count, scratch, w64, p.ne, p.hidden, s);
+    int rc = launch_exact_logits(x, w, flag_list, flag_count, scratch, w64, p.ne, p.hidden, p.ntok, s);
     if (rc) return rc;
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
