@@ -157,6 +157,13 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
     nb = R * C // 256 * 144 + 4 * (R + C)
     out["q4k_matvec_7168"] = {"us": round(us, 2), "roofline": _roof("hbm", nb / us / 1e3, hbm, "GB/s")}
     dense_us = us
+    # a decode step's Q, K and V projections read the same activations: three 7168^2 matvecs in
+    # one launch (ck_q4k_matvec_f32_group)
+    y3 = [torch.empty(R, device=dev) for _ in range(3)]
+    us3 = _graph_us(torch, lambda i: ops.q4k_matvec_group([q4[(3 * i + j) % 16] for j in range(3)], x, R, C, outs=y3),
+                    64, 16)
+    out["q4k_matvec_7168_group3"] = {"us": round(us3, 2), "us_per_matvec": round(us3 / 3, 2),
+                                     "roofline": _roof("hbm", 3 * nb / us3 / 1e3, hbm, "GB/s")}
     # the sibling format: Q6_K decode matvec at the same 7168 x 7168 and at 4096 x 4096
     for R in (7168, 4096):
         q6 = [t(synth.make_q6k(np.random.default_rng([6, i]), R * R)) for i in range(16)]
@@ -253,8 +260,9 @@ def sub_benchmarks(torch, dev, hbm, tc_burst):
         o = torch.empty((bsz, sp.hidden), dtype=torch.bfloat16, device=dev)
 
         def step(k):
-            for j in range(4):
-                ops.q4k_matvec(q4[(4 * k + j) % 16], x, 7168, 7168, out=y)
+            # Q, K, V from the same activations in one launch, then O from V, as a decode step runs them
+            qkv = ops.q4k_matvec_group([q4[(4 * k + j) % 16] for j in range(3)], x, 7168, 7168, outs=y3)
+            ops.q4k_matvec(q4[(4 * k + 3) % 16], qkv[2], 7168, 7168, out=y)
             return lay(xx, out=o)
         for k in range(3):
             step(k)
@@ -395,6 +403,7 @@ def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, 
     q4 = [t(synth.make_q4k(np.random.default_rng([2, i]), R * C)) for i in range(16)]
     xv = t(np.random.default_rng(3).standard_normal(C).astype(np.float32))
     yv = torch.empty(R, device=dev)
+    yv3 = [torch.empty(R, device=dev) for _ in range(3)]
     dense_b = R * C // 256 * 144
     sweep = {}
     parity = None
@@ -411,8 +420,9 @@ def decode_sweep_ep(torch, dist, layer_cls, spec, w, experts, rank, world, dev, 
         o = torch.empty((bsz, spec.hidden), dtype=torch.bfloat16, device=dev)
 
         def step(k):
-            for j in range(4):
-                ops.q4k_matvec(q4[(4 * k + j) % 16], xv, R, C, out=yv)
+            # Q, K, V from the same activations in one launch, then O from V, as a decode step runs them
+            qkv = ops.q4k_matvec_group([q4[(4 * k + j) % 16] for j in range(3)], xv, R, C, outs=yv3)
+            ops.q4k_matvec(q4[(4 * k + 3) % 16], qkv[2], R, C, out=yv)
             return lay(xb, out=o)
         for k in range(3):
             step(k)

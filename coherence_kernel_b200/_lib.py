@@ -41,6 +41,7 @@ SIGNATURES = {
     "ck_q8_0_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_q4k_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),
     "ck_matvec_ordered_f32": (_i32, [_i32, _p, _p, _p, _u32, _u32, _p]),
+    "ck_q4k_matvec_f32_group": (_i32, [_u32, _p, _p, _p, _u32, _u32, _p]),
     "ck_q4k_matmul_batch_f32": (_i32, [_p, _p, _p, _u32, _u32, _u32, _p]),
     "ck_q6k_dequant_f32": (_i32, [_p, _p, _u64, _u64, _p]),
     "ck_q6k_matvec_f32": (_i32, [_p, _p, _p, _u32, _u32, _p]),

@@ -175,6 +175,15 @@ int ck_q4k_matvec_f32(const void *qb, const float *x, float *y, uint32_t rows, u
         return fail(CK_EARG, "ck_q4k_matvec_f32");
     return fail(ck::launch_q4k_matvec((const uint8_t *)qb, x, y, rows, cols, 1, S(s)), "ck_q4k_matvec_f32");
 }
+int ck_q4k_matvec_f32_group(uint32_t n, const void *const *qb, const float *x, float *const *y, uint32_t rows,
+                            uint32_t cols, void *s) {
+    if (!qb || !x || !y || n == 0 || n > 4 || (reinterpret_cast<uintptr_t>(x) & 15))
+        return fail(CK_EARG, "ck_q4k_matvec_f32_group");
+    for (uint32_t g = 0; g < n; ++g)
+        if (!qb[g] || !y[g] || (reinterpret_cast<uintptr_t>(qb[g]) & 15)) return fail(CK_EARG, "ck_q4k_matvec_f32_group");
+    return fail(ck::launch_q4k_matvec_group(n, reinterpret_cast<const uint8_t *const *>(qb), x, y, rows, cols, 1, S(s)),
+                "ck_q4k_matvec_f32_group");
+}
 int ck_q4k_matmul_batch_f32(const void *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
                             void *s) {
     if (!qb || !x || !y || ntok == 0 || (reinterpret_cast<uintptr_t>(qb) & 15) ||

@@ -16,6 +16,8 @@ int launch_q4k_dequant(const uint8_t *qb, float *w, uint64_t off, uint64_t n, cu
 int launch_q4k_dequant_bf16(const uint8_t *qb, void *w, uint64_t off, uint64_t n, cudaStream_t s);
 int launch_matvec_ordered(int kind, const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols,
                           cudaStream_t s);
+int launch_q4k_matvec_group(uint32_t ng, const uint8_t *const *qb, const float *x, float *const *y, uint32_t rows,
+                            uint32_t cols, uint32_t ntok, cudaStream_t s);
 int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
                       cudaStream_t s);
 int launch_q80_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
@@ -35,6 +37,9 @@ int launch_gemv_stream(int kind, const uint8_t *qb, const float *x, float *y, ui
 // tensor-core Q4_K decode matvec (gemv_tc.cu): cols % 256 == 0, weights and x 16-byte aligned
 bool gemv_tc_ok(const void *qb, const float *x, uint32_t rows, uint32_t cols);
 int launch_gemv_tc(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
+// up to 4 matrices of one shape against the same x in one launch (each y as its single launch)
+int launch_gemv_tc_group(uint32_t ng, const uint8_t *const *qb, const float *x, float *const *y, uint32_t rows,
+                         uint32_t cols, cudaStream_t s);
 int launch_f16_matvec(const uint16_t *w, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s);
 int launch_scale(const float *x, float *y, float a, uint32_t n, cudaStream_t s);
 int launch_axpy(const float *x, float *y, float a, uint32_t n, cudaStream_t s);

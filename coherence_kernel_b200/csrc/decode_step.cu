@@ -155,9 +155,10 @@ int ck_decode_step_run(ck_decode_step *s, float *h_dev, float *q_dev, float *k_d
     const unsigned eb = (unsigned)((n + 255) / 256);
     k_rmsnorm<<<ntok, NORM_THREADS, 0, st>>>(h_dev, s->g_attn, s->w.a, nullptr, H, s->cfg.eps);
     int rc = (int)cudaGetLastError();
-    if (!rc) rc = ck::launch_q4k_matvec((const uint8_t *)s->wq, s->w.a, q_dev, H, H, ntok, st);
-    if (!rc) rc = ck::launch_q4k_matvec((const uint8_t *)s->wk, s->w.a, k_dev, H, H, ntok, st);
-    if (!rc) rc = ck::launch_q4k_matvec((const uint8_t *)s->wv, s->w.a, v_dev, H, H, ntok, st);
+    // Q, K and V read the same a: one launch for the three where the tensor-core matvec applies
+    const uint8_t *wqkv[3] = {(const uint8_t *)s->wq, (const uint8_t *)s->wk, (const uint8_t *)s->wv};
+    float *yqkv[3] = {q_dev, k_dev, v_dev};
+    if (!rc) rc = ck::launch_q4k_matvec_group(3, wqkv, s->w.a, yqkv, H, H, ntok, st);
     if (!rc) rc = ck::launch_q4k_matvec((const uint8_t *)s->wo, v_dev, s->w.o, H, H, ntok, st);
     if (rc) return rc;
     k_add_f32<<<eb, 256, 0, st>>>(h_dev, s->w.o, n);

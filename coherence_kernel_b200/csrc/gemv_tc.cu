@@ -96,15 +96,20 @@ CK_DEV void mbar_arrive_peer(uint64_t *local, uint32_t rank) {
                  : "memory");
 }
 
+constexpr uint32_t MAX_GROUP = 4;  // matrices of one shape sharing x in one launch
 struct Params {
     const float *x;
-    float *y;
+    float *y[MAX_GROUP];       // y of matrix g (maps wmap0 .. wmap3)
     uint32_t rows, cols, nsb;  // nsb: superblocks per row
     uint32_t csize;            // CTAs per cluster (K split)
     uint32_t trows;            // rows per tile (<= ROWS; the MMA's rows past it are discarded)
+    uint32_t tiles;            // tiles per matrix
 };
 
-__global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUtensorMap wmap, Params p) {
+__global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUtensorMap wmap0,
+                                                     const __grid_constant__ CUtensorMap wmap1,
+                                                     const __grid_constant__ CUtensorMap wmap2,
+                                                     const __grid_constant__ CUtensorMap wmap3, Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + BAR_OFF);
@@ -119,8 +124,11 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
     float *red = reinterpret_cast<float *>(smem + RED_OFF);
     float *xs = reinterpret_cast<float *>(smem + XS_OFF);  // per slot: X_s[8], scale_s[8]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t q = cluster_rank(), tile = blockIdx.x / p.csize;
+    // cluster blockIdx / csize is tile `tile` of matrix `mi`
+    const uint32_t q = cluster_rank(), mi = blockIdx.x / p.csize / p.tiles, tile = blockIdx.x / p.csize % p.tiles;
     const uint32_t row0 = tile * p.trows;
+    const CUtensorMap *wmap = mi == 0 ? &wmap0 : mi == 1 ? &wmap1 : mi == 2 ? &wmap2 : &wmap3;
+    float *__restrict__ y = mi == 0 ? p.y[0] : mi == 1 ? p.y[1] : mi == 2 ? p.y[2] : p.y[3];
     // this CTA's superblocks [sb0, sb1)
     const uint32_t sb0 = (uint32_t)((uint64_t)p.nsb * q / p.csize), sb1 = (uint32_t)((uint64_t)p.nsb * (q + 1) / p.csize);
     const int nj = (int)(sb1 - sb0);
@@ -162,12 +170,12 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
     if (warp == 0) {
         // ------------------------------------------------------------ weights: TMA producer
         if (lane == 0) {
-            prefetch_tmap(&wmap);
+            prefetch_tmap(wmap);
             int issued = 0;
             const int early = nj < WST ? nj : WST;
             for (int j = 0; j < early; ++j) {
                 mbar_arrive_expect_tx(&w_full[j], p.trows * Q4K_BYTES);
-                tma_load_2d_u8(smem + W_OFF + j * W_STAGE, &wmap, &w_full[j], (int)((sb0 + j) * Q4K_BYTES),
+                tma_load_2d_u8(smem + W_OFF + j * W_STAGE, wmap, &w_full[j], (int)((sb0 + j) * Q4K_BYTES),
                                (int)row0);
                 issued = j + 1;
             }
@@ -176,7 +184,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
                 const int s = j % WST;
                 if (!mbar_wait_bounded(&w_empty[s], ((j / WST) & 1) ^ 1, err, 1)) break;
                 mbar_arrive_expect_tx(&w_full[s], p.trows * Q4K_BYTES);
-                tma_load_2d_u8(smem + W_OFF + s * W_STAGE, &wmap, &w_full[s], (int)((sb0 + j) * Q4K_BYTES),
+                tma_load_2d_u8(smem + W_OFF + s * W_STAGE, wmap, &w_full[s], (int)((sb0 + j) * Q4K_BYTES),
                                (int)row0);
                 issued = j + 1;
             }
@@ -357,7 +365,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_gemv_tc(const __grid_constant__ CUt
                     bad |= inbox_err[c - 1] != 0;
                 }
             }
-            if (r < p.trows && row < p.rows) p.y[row] = bad ? __int_as_float(0x7FC00000) : v;
+            if (r < p.trows && row < p.rows) y[row] = bad ? __int_as_float(0x7FC00000) : v;
         }
     }
     if (warp == 1) {
@@ -399,21 +407,31 @@ bool gemv_tc_ok(const void *qb, const float *x, uint32_t rows, uint32_t cols) {
 }
 
 namespace gtc {
-static int launch(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t trows,
-                  uint32_t csize, cudaStream_t s) {
-    if (trows == 0 || trows > ROWS || csize == 0 || csize > MAX_CLUSTER) return CK_ERR_ARG;
+// ng matrices qb[0 .. ng) of one shape, all against x, in one launch: every matrix's tiles and K
+// split are those of its own single launch (so each y is bit-identical to it), one after another in
+// the grid
+static int launch(uint32_t ng, const uint8_t *const *qb, const float *x, float *const *y, uint32_t rows,
+                  uint32_t cols, uint32_t trows, uint32_t csize, cudaStream_t s) {
+    if (trows == 0 || trows > ROWS || csize == 0 || csize > MAX_CLUSTER || ng == 0 || ng > MAX_GROUP)
+        return CK_ERR_ARG;
     EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return CK_ERR_NODEV;
     const uint32_t nsb = cols / 256, row_bytes = nsb * Q4K_BYTES;
-    CUtensorMap map;
-    cuuint64_t dims[2] = {row_bytes, rows};
-    cuuint64_t strides[1] = {row_bytes};
-    cuuint32_t box[2] = {Q4K_BYTES, trows};
-    cuuint32_t estr[2] = {1, 1};
-    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(qb), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return CK_ERR_ARG;
+    CUtensorMap maps[MAX_GROUP];
+    for (uint32_t g = 0; g < MAX_GROUP; ++g) {
+        if (g >= ng) {
+            maps[g] = maps[0];  // never read
+            continue;
+        }
+        cuuint64_t dims[2] = {row_bytes, rows};
+        cuuint64_t strides[1] = {row_bytes};
+        cuuint32_t box[2] = {Q4K_BYTES, trows};
+        cuuint32_t estr[2] = {1, 1};
+        if (enc(&maps[g], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(qb[g]), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return CK_ERR_ARG;
+    }
     const uint32_t tiles = (rows + trows - 1) / trows;
     static unsigned long long set = 0;
     if (attr_pending(set)) {
@@ -422,7 +440,15 @@ static int launch(const uint8_t *qb, const float *x, float *y, uint32_t rows, ui
         if (e != cudaSuccess) return (int)e;
         attr_mark(set);
     }
-    gtc::Params p = {x, y, rows, cols, nsb, csize, trows};
+    gtc::Params p = {};
+    p.x = x;
+    for (uint32_t g = 0; g < MAX_GROUP; ++g) p.y[g] = y[g < ng ? g : 0];
+    p.rows = rows;
+    p.cols = cols;
+    p.nsb = nsb;
+    p.csize = csize;
+    p.trows = trows;
+    p.tiles = tiles;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = csize;
@@ -431,25 +457,31 @@ static int launch(const uint8_t *qb, const float *x, float *y, uint32_t rows, ui
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles * csize);
+    cfg.gridDim = dim3(ng * tiles * csize);
     cfg.blockDim = dim3(gtc::NTHR);
     cfg.dynamicSmemBytes = gtc::SMEM;
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gtc::k_gemv_tc, map, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gtc::k_gemv_tc, maps[0], maps[1], maps[2], maps[3], p);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 }  // namespace gtc
 
 int launch_gemv_tc(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, cudaStream_t s) {
-    if (!gemv_tc_ok(qb, x, rows, cols)) return CK_ERR_SHAPE;
+    return launch_gemv_tc_group(1, &qb, x, &y, rows, cols, s);
+}
+
+int launch_gemv_tc_group(uint32_t ng, const uint8_t *const *qb, const float *x, float *const *y, uint32_t rows,
+                         uint32_t cols, cudaStream_t s) {
+    for (uint32_t g = 0; g < ng; ++g)
+        if (!gemv_tc_ok(qb[g], x, rows, cols)) return CK_ERR_SHAPE;
     int dev = 0, nsm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     uint32_t trows, csize;
     gtc::plan(rows, cols / 256, (uint32_t)nsm, trows, csize);
-    return gtc::launch(qb, x, y, rows, cols, trows, csize, s);
+    return gtc::launch(ng, qb, x, y, rows, cols, trows, csize, s);
 }
 
 }  // namespace ck

@@ -287,6 +287,22 @@ int launch_matvec_ordered(int kind, const uint8_t *qb, const float *x, float *y,
         k_matvec_ordered<12><<<nblk(rows, 128), 128, 0, s>>>(qb, x, y, rows, cols);
     return (int)cudaGetLastError();
 }
+// ng matrices of one shape against the same x: one tensor-core launch where a single one would take
+// the tensor-core matvec (each y bit-identical to its single launch), else one launch each
+int launch_q4k_matvec_group(uint32_t ng, const uint8_t *const *qb, const float *x, float *const *y, uint32_t rows,
+                            uint32_t cols, uint32_t ntok, cudaStream_t s) {
+    bool tc = ntok == 1 && ng >= 1 && ng <= 4 && cols % 64 == 0;
+    for (uint32_t g = 0; tc && g < ng; ++g)
+        tc = gemv_tc_ok(qb[g], x, rows, cols) &&
+             (!gemv_stream_ok(qb[g], x, cols) || (uint64_t)rows * (cols / 256) * Q4K_BYTES >= (12ull << 20));
+    if (tc) return launch_gemv_tc_group(ng, qb, x, y, rows, cols, s);
+    for (uint32_t g = 0; g < ng; ++g) {
+        const int rc = launch_q4k_matvec(qb[g], x, y[g], rows, cols, ntok, s);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
 int launch_q4k_matvec(const uint8_t *qb, const float *x, float *y, uint32_t rows, uint32_t cols, uint32_t ntok,
                       cudaStream_t s) {
     if (cols % 64 != 0) return CK_ERR_SHAPE;

@@ -74,6 +74,23 @@ def q4k_matvec(qb, x, rows, cols, out=None):
     return y
 
 
+def q4k_matvec_group(qbs, x, rows, cols, outs=None):
+    """Up to four Q4_K matvecs of one shape on the same x, in one launch where the tensor-core
+    kernel applies (ck_q4k_matvec_f32_group); returns the list of y."""
+    if not 1 <= len(qbs) <= 4:
+        raise ValueError("one to four matrices")
+    for qb in qbs:
+        _dev(qb, "qb", torch.uint8, q4k_nbytes(rows * cols))
+    _dev(x, "x", torch.float32, cols)
+    ys = list(outs) if outs is not None else [torch.empty(rows, dtype=torch.float32, device=x.device) for _ in qbs]
+    n = len(qbs)
+    qarr = (ctypes.c_void_p * n)(*[qb.data_ptr() for qb in qbs])
+    yarr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+    _lib.check(_lib.load().ck_q4k_matvec_f32_group(n, qarr, _ptr(x), yarr, rows, cols, _stream()),
+               "ck_q4k_matvec_f32_group")
+    return ys
+
+
 def q6k_nbytes(n_weights: int) -> int:
     return (n_weights + 255) // 256 * 210
 

@@ -66,6 +66,12 @@ int ck_q6k_matvec_part_f32(const void *qb_dev, const float *x_dev, float *part_d
                            uint32_t parts, void *stream);
 /* Batched matvec over ntok tokens, fp32 (replaces form_q4k_matmul_batch_f32,
  * qk-matmul-batch.fk:206-217): y[t*rows + r] = sum_j W[r, j] x[t*cols + j].  cols % 64 == 0. */
+/* 1 to 4 Q4_K matrices of one shape against the same x (a decode step's Q/K/V projections):
+ * y_list[g] = qb_list[g] . x.  qb_list and y_list are host arrays of device pointers.  Where one such
+ * matvec takes the tensor-core kernel, all of them run in one launch, each y bit-identical to its
+ * own ck_q4k_matvec_f32; otherwise they run one after another. */
+int ck_q4k_matvec_f32_group(uint32_t n, const void *const *qb_list, const float *x_dev, float *const *y_list,
+                            uint32_t rows, uint32_t cols, void *stream);
 int ck_q4k_matmul_batch_f32(const void *qb_dev, const float *x_dev, float *y_dev, uint32_t rows, uint32_t cols,
                             uint32_t ntok, void *stream);
 

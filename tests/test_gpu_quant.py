@@ -192,3 +192,16 @@ def test_bounded_wait_gives_up_and_reports():
     f = np.load(os.path.join(G, "ref_fixtures.npz"))
     w = ops.q8_0_dequant(dev(f["q80"]), 0, 96).cpu().numpy()
     assert np.array_equal(w, f["w8"].astype(np.float32))
+
+
+@pytest.mark.parametrize("rows,cols,n", [(7168, 7168, 3), (7168, 7168, 4), (4096, 11008, 2), (1024, 2048, 3)])
+def test_q4k_matvec_group_equals_single_calls(rows, cols, n):
+    """ck_q4k_matvec_f32_group: several matrices against one x in one launch (tensor-core shapes) or
+    one after another (small ones); every y bit-identical to its own ck_q4k_matvec_f32."""
+    rng = np.random.default_rng(rows + cols + n)
+    qs = [torch.from_numpy(synth.make_q4k(rng, rows * cols)).cuda() for _ in range(n)]
+    x = torch.from_numpy(rng.standard_normal(cols).astype(np.float32)).cuda()
+    ys = ops.q4k_matvec_group(qs, x, rows, cols)
+    torch.cuda.synchronize()
+    for q, y in zip(qs, ys):
+        assert torch.equal(y, ops.q4k_matvec(q, x, rows, cols))
