@@ -103,6 +103,15 @@ struct Cfg {
 struct Tile {
     int g, xrow, orow, ntok;
 };
+// one lane of a converged warp issues the MMAs: a tcgen05.mma from a lone diverged thread issues
+// several times slower
+CK_DEV bool elect_lane() {
+    uint32_t pred = 0;
+    asm volatile("{\n .reg .b32 %%rx;\n .reg .pred %%px;\n elect.sync %%rx|%%px, %1;\n selp.u32 %0, 1, 0, %%px;\n}"
+                 : "=r"(pred)
+                 : "r"(0xffffffffu));
+    return pred != 0;
+}
 // A tile longer than the largest token tile is cut to BN tokens by every role alike (the MMA
 // thread also records the error); the tile builders never make one.
 CK_DEV Tile load_tile(const int4 *tiles, int i) {
@@ -299,7 +308,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // The whole warp runs the loop: lane 0 takes the (bounded) barrier waits and broadcasts
+        // their outcome, and one elected lane of the converged warp issues the MMAs and commits.
+        {
             // running ring positions and phases (no division in the loop); the B operand's
             // descriptor is the stage's base descriptor plus 2 per 16-wide K slice (32 bytes)
             int sb = 0, sa = 0, ut = 0;
@@ -311,7 +322,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t atm0 = tmem_base + (uint32_t)C::A_TOFF;              // first A stage (TMEM)
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++ut) {
                 const Tile t = load_tile(p.tiles, u / ks / nrt);
-                if (p.tiles[u / ks / nrt].w > BN) atomicCAS(p.err, 0, 9);
+                if (lane == 0 && p.tiles[u / ks / nrt].w > BN) atomicCAS(p.err, 0, 9);
                 int kb0, kb1;
                 krange(u, kb0, kb1);
                 int nmma = ((t.ntok + 15) / 16) * 16;
@@ -320,45 +331,58 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t idesc = idesc_bf16(BM, nmma);
                 const int ab = ut % C::NBUF;
                 const uint32_t aph = (uint32_t)(ut / C::NBUF) & 1u;
-                if (!mbar_wait_bounded(&acc_empty[ab], aph ^ 1u, p.err, 2)) { ok = false; break; }
+                int w_ok = 1;
+                if (lane == 0) w_ok = mbar_wait_bounded(&acc_empty[ab], aph ^ 1u, p.err, 2);
+                if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if ((!DENSE && !mbar_wait_bounded(&a_full[sa], pha, p.err, 3)) ||
-                        !mbar_wait_bounded(&b_full[sb], phb, p.err, 4)) {
+                    int k_ok = 1;
+                    if (lane == 0)
+                        k_ok = (DENSE || mbar_wait_bounded(&a_full[sa], pha, p.err, 3)) &&
+                               mbar_wait_bounded(&b_full[sb], phb, p.err, 4);
+                    if (!__shfl_sync(0xffffffffu, k_ok, 0)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t bd = bdesc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
-                    if constexpr (DENSE) {
-                        // K chunk kb / chunk accumulates into its own accumulator
-                        const uint32_t dd = d0 + (uint32_t)((kb / chunk) * C::DENSE_TILE);
-                        const int kfirst = kb % chunk;
-                        const uint64_t ad = adesc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
+                    if (elect_lane()) {
+                        if constexpr (DENSE) {
+                            // K chunk kb / chunk accumulates into its own accumulator
+                            const uint32_t dd = d0 + (uint32_t)((kb / chunk) * C::DENSE_TILE);
+                            const int kfirst = kb % chunk;
+                            const uint64_t ad = adesc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)
-                            umma_bf16(dd, ad + 2 * k, bd + 2 * k, idesc, (kfirst | k) != 0);
-                    } else {
-                        const uint32_t at = atm0 + (uint32_t)(sa * C::A_TCOLS);
+                            for (int k = 0; k < BK / 16; ++k)
+                                umma_bf16(dd, ad + 2 * k, bd + 2 * k, idesc, (kfirst | k) != 0);
+                        } else {
+                            const uint32_t at = atm0 + (uint32_t)(sa * C::A_TCOLS);
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k) {
-                            const uint32_t acc = (kb | k) != 0;
-                            umma_bf16_ts(d0, at + 8 * k, bd + 2 * k, idesc, acc);
-                            if (DUAL) umma_bf16_ts(d0 + BN, at + 32 + 8 * k, bd + 2 * k, idesc, acc);
+                            for (int k = 0; k < BK / 16; ++k) {
+                                const uint32_t acc = (kb | k) != 0;
+                                umma_bf16_ts(d0, at + 8 * k, bd + 2 * k, idesc, acc);
+                                if (DUAL) umma_bf16_ts(d0 + BN, at + 32 + 8 * k, bd + 2 * k, idesc, acc);
+                            }
+                            umma_commit(&a_empty[sa]);
                         }
-                        umma_commit(&a_empty[sa]);
+                        umma_commit(&b_empty[sb]);
+                    }
+                    __syncwarp();
+                    if constexpr (!DENSE) {
                         if (++sa == C::A_ST) { sa = 0; pha ^= 1u; }
                     }
-                    umma_commit(&b_empty[sb]);
                     if (++sb == C::B_ST) { sb = 0; phb ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit(&acc_full[ab]);
+                if (elect_lane()) umma_commit(&acc_full[ab]);
+                __syncwarp();
             }
-            // every MMA this thread issued completes before TMEM is released
-            umma_commit(done_bar);
-            mbar_wait_bounded(done_bar, 0, nullptr, 0);
+            // every MMA this warp issued completes before TMEM is released
+            if (elect_lane()) umma_commit(done_bar);
+            __syncwarp();
+            if (lane == 0) mbar_wait_bounded(done_bar, 0, nullptr, 0);
+            __syncwarp();
         }
     } else if (warp < W_EPI0 && !DENSE) {
         // ------------------------------------------------------------ dequant producers

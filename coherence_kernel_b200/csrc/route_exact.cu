@@ -58,7 +58,7 @@ CK_DEV double ref_sigmoid(double x) { return __ddiv_rn(1.0, __dadd_rn(1.0, ref_e
 // Few flagged tokens (a decode step, or a rank's share of a batch; k_exact_logits_few): a work
 // item is 4 tokens x 32 experts on a CTA of four warps, warp q folding token q, lane l expert l --
 // enough warps to fill the GPU, each folding one chain.  Stages of 32 columns go through a CTA-wide
-// cp.async ring of XF_NB stages: the 32 experts' fp32 row pieces (four threads to a row, so each
+// cp.async ring of XF_NB stages: the 32 experts' fp32 row pieces (eight threads to a piece, so each
 // copy instruction moves whole lines; a thread per row would keep 32 scattered sectors in flight
 // per instruction and run into the SM's limit on outstanding requests) and the four tokens'
 // activations, converted to fp64 once, two stages ahead.  The router is shared by the item's four
