@@ -73,6 +73,7 @@ SIGNATURES = {
                                   _u32, _i32, _p, _p]),
     "ck_moe_expert_gemm_bounded": (_i32, [_i32, _p, _p, _p, _p, _u64, _u32, _u32, _p, _u32, _p, _u32, _p, _p, _p,
                                           _u32, _u32, _u32, _i32, _u32, _p, _p]),
+    "ck_moe_expert_gemm_rows": (_i32, [_p, _u64, _u32, _p, _u32, _p, _u32, _p, _p, _u32, _u32, _u32, _i32, _p, _p]),
     "ck_moe_combine": (_i32, [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _i32, _p, _p, _p]),
     "ck_token_tiles": (_i32, [_p, _p, _u32, _p]),
     "ck_token_tiles_n": (_i32, [_p, _p, _u32, _u32, _p]),
@@ -90,6 +91,7 @@ SIGNATURES = {
     "ck_ep_peer_signal": (_i32, [_p, _i32, _p]),
     "ck_ep_peer_wait": (_i32, [_p, _i32, _u64, _p]),
     "ck_ep_peer_return": (_i32, [_p, _p, _p, _p, _p, _p]),
+    "ck_ep_peer_return_rows": (_i32, [_p, _p, _p, _p, _p, _p]),
     "ck_ep_group_create": (_p, [ctypes.POINTER(MoeConfig), _u32, _p, _u32]),
     "ck_ep_group_load": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "ck_ep_group_forward": (_i32, [_p, _p, _u32, _p, _p, _p, _p, _p]),

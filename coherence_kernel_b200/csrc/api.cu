@@ -455,6 +455,29 @@ int ck_moe_expert_gemm_bounded(int dual, const void *w0, const void *w1, const v
     return fail(ck::launch_gemm_q4k(p, S(s)), "ck_moe_expert_gemm");
 }
 
+int ck_moe_expert_gemm_rows(const void *w0, uint64_t w_stride, uint32_t n_routed, const void *x, uint32_t x_rows,
+                            const unsigned long long *row_dst, uint32_t out_rows, const void *tiles,
+                            const int32_t *ntiles, uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow,
+                            int *err, void *s) {
+    if (!row_dst) return fail(CK_ERR_ARG, "ck_moe_expert_gemm_rows: row_dst is null");
+    ck::GemmParams p = {};
+    p.w0 = (const uint8_t *)w0;
+    p.w_stride = w_stride;
+    p.x = x;
+    p.x_rows = x_rows;
+    p.row_dst = row_dst;
+    p.out_rows = out_rows;
+    p.tiles = (const int4 *)tiles;
+    p.ntiles = ntiles;
+    p.max_tiles = max_tiles;
+    p.n_routed = n_routed;
+    p.N = n;
+    p.K = k;
+    p.xrow_is_orow = xrow_is_orow;
+    p.err = err;
+    return fail(ck::launch_gemm_q4k(p, S(s)), "ck_moe_expert_gemm_rows");
+}
+
 int ck_moe_combine(const void *y, const int32_t *ids, const float *wts, const int32_t *pair_pos, uint32_t ntok,
                    uint32_t nsel, uint32_t n_shared, uint32_t hidden, int order_by_expert, void *out, float *out_f32,
                    void *s) {

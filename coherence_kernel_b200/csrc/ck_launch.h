@@ -137,6 +137,10 @@ struct GemmParams {
     // a bound on the tokens of every tile (0: none known); 1..8 runs the few-token grouped matvec
     // (moe_gemv.cu) where its shape rules hold
     uint32_t max_tile_tok;
+    // single form only: output row o is stored at the bf16 row whose address is row_dst[o] instead of
+    // at out + o * N -- rows may sit in another GPU's memory (the expert-parallel return written by
+    // the down projection's epilogue); every address 16-byte aligned, N % 8 == 0
+    const unsigned long long *row_dst;
 };
 int launch_gemm_q4k(const GemmParams &p, cudaStream_t s);
 bool gemv_moe_ok(const GemmParams &p);

@@ -14,7 +14,10 @@
 //   k_ep_wait            the rank's flags[s] >= step for every s, bounded; a timeout sets err
 //   ... the receiver regroups its W * cap rows by local expert and runs the expert GEMMs ...
 //   k_ep_return          every (row, slot) pair the rank computed is stored into its source's return
-//                        buffer at (token, slot), followed by a second signal / wait
+//                        buffer at (token, slot), followed by a second signal / wait -- or, when the
+//                        down projection runs on the grouped GEMM, k_ep_return_rows gives that GEMM
+//                        each output row's address in its source's return buffer and the GEMM's
+//                        epilogue stores the rows there itself (ck_moe_expert_gemm_rows)
 //
 // The host never waits and no size crosses to the host, so a forward can be captured in a CUDA
 // graph.  Single buffering is safe: a rank writes step i+1 rows into a peer only after the return
@@ -138,6 +141,24 @@ __global__ void k_ep_return(ck_ep_peers P, const uint4 *__restrict__ y2, const i
     }
 }
 
+// The destinations of the down projection's rows when its epilogue writes the return itself: for
+// every (received row, slot) pair with a local expert, row_dst[its permute position] = the address
+// of row token * nsel + slot in its source's return buffer (k_ep_return's mapping).
+__global__ void k_ep_return_rows(ck_ep_peers P, const int32_t *__restrict__ pair_pos2,
+                                 const int32_t *__restrict__ ids_own, const int32_t *__restrict__ tok_own,
+                                 unsigned long long *__restrict__ row_dst) {
+    const uint32_t K = P.nsel;
+    const size_t npairs = (size_t)P.world * P.cap * K;
+    for (size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x; q < npairs; q += (size_t)gridDim.x * blockDim.x) {
+        if (ids_own[q] < 0) continue;
+        const size_t row = q / K;
+        const uint32_t k = (uint32_t)(q - row * K), s = (uint32_t)(row / P.cap);
+        const int32_t t = tok_own[row];
+        row_dst[pair_pos2[q]] = reinterpret_cast<unsigned long long>(P.ret_y[s]) +
+                                ((unsigned long long)t * K + k) * P.hidden * 2ull;
+    }
+}
+
 inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
 int check(const ck_ep_peers *P) {
@@ -224,6 +245,16 @@ int ck_ep_peer_return(const ck_ep_peers *P, const void *y2_bf16_dev, const int32
     const size_t npairs = (size_t)P->world * P->cap * P->nsel;
     k_ep_return<<<grid_for(npairs), 256, 0, S(s)>>>(*P, reinterpret_cast<const uint4 *>(y2_bf16_dev), pair_pos2_dev,
                                                    ids_own_dev, tok_own_dev);
+    return (int)cudaGetLastError();
+}
+
+int ck_ep_peer_return_rows(const ck_ep_peers *P, const int32_t *pair_pos2_dev, const int32_t *ids_own_dev,
+                           const int32_t *tok_own_dev, unsigned long long *row_dst_dev, void *s) {
+    if (int rc = check(P)) return rc;
+    if (!pair_pos2_dev || !ids_own_dev || !tok_own_dev || !row_dst_dev) return CK_EARG;
+    const size_t npairs = (size_t)P->world * P->cap * P->nsel;
+    k_ep_return_rows<<<grid_for((npairs + 31) / 32), 256, 0, S(s)>>>(*P, pair_pos2_dev, ids_own_dev, tok_own_dev,
+                                                                     row_dst_dev);
     return (int)cudaGetLastError();
 }
 

@@ -485,6 +485,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(p.out);
         uint8_t *epi_stage = smem + C::EPI_OFF + (warp - W_EPI0) * C::EPI_STAGE;
         const bool vec_out = !DENSE && p.N % 8 == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+        // the bf16 row of output row o: out + o N, or the address row_dst[o] holds
+        auto out_row = [&](uint32_t o) -> __nv_bfloat16 * {
+            return p.row_dst ? reinterpret_cast<__nv_bfloat16 *>(p.row_dst[o]) : out + (uint64_t)o * p.N;
+        };
         // lane j holds the route weight of token cb*32 + j of the current chunk (shuffled out
         // below); the next chunk's weight is loaded one chunk ahead, the first before the wait
         auto route_w = [&](const Tile &t, int cb) -> float {
@@ -546,7 +550,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const int tl = q * 8 + (lane >> 2), seg = lane & 3;
                         const uint4 o = *reinterpret_cast<const uint4 *>(epi_stage + q * 512 + lane * 16);
                         if (cb * 32 + tl < t.ntok)
-                            *reinterpret_cast<uint4 *>(out + (uint64_t)(t.orow + cb * 32 + tl) * p.N + n0 + 32 * sp + 8 * seg) = o;
+                            *reinterpret_cast<uint4 *>(out_row((uint32_t)(t.orow + cb * 32 + tl)) + n0 + 32 * sp + 8 * seg) = o;
                     }
                     __syncwarp();
                 } else {
@@ -564,7 +568,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 (kc == 0 ? p.out_f32 : p.out_planes + (uint64_t)(kc - 1) * p.out_rows * p.N)
                                     [(uint64_t)(t.orow + tok) * p.N + row] = val;
                             else
-                                out[(uint64_t)(t.orow + tok) * p.N + row] = __float2bfloat16_rn(val);
+                                out_row((uint32_t)(t.orow + tok))[row] = __float2bfloat16_rn(val);
                         }
                     }
                 }
@@ -677,7 +681,8 @@ static int launch_t(const GemmParams &p, cudaStream_t s) {
 }  // namespace gemm
 
 int launch_gemm_q4k(const GemmParams &p, cudaStream_t s) {
-    if (!p.w0 || !p.x || !p.out || !p.tiles || !p.ntiles || !p.err) return CK_ERR_ARG;
+    if (!p.w0 || !p.x || !(p.out || p.row_dst) || !p.tiles || !p.ntiles || !p.err) return CK_ERR_ARG;
+    if (p.row_dst && (p.dual || p.N % 8 || p.max_tile_tok)) return CK_ERR_ARG;
     if (p.K % gemm::BK != 0 || p.N == 0 || p.K == 0 || ((uint64_t)p.N * p.K) % 256 != 0) return CK_ERR_SHAPE;
     if (p.dual && !p.w1) return CK_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.w0) & 15)) return CK_ERR_ARG;

@@ -15,7 +15,9 @@ Each rank owns one device arena, which every peer maps through CUDA IPC:
 
 A forward issues, on one stream and with no host wait: the route, the dispatch plan, the shared
 expert (side stream), the dispatch stores, a barrier, the regroup of all world * cap received rows by
-local expert (unused rows carry expert -1), the expert GEMMs, the return stores, a barrier and the
+local expert (unused rows carry expert -1), the expert GEMMs, the return stores (from the down
+projection's own epilogue when it runs on the grouped GEMM: every output row is stored straight into
+its source's return buffer, so the return crosses NVLink while the GEMM runs), a barrier and the
 combine.  It can therefore be captured in a CUDA graph and replayed.  The (token, slot) rows reach the
 combine in the reference's order, computed by the same kernels as on one GPU, so the output equals
 the single-GPU layer's bit for bit whenever both take the same expert-GEMM form (the few-token
@@ -110,8 +112,13 @@ class PeerExpertParallelMoE:
         self.perm_ws2 = torch.empty(_align(L.ck_moe_permute_workspace_bytes(R, K, self.el)), dtype=torch.uint8,
                                     device=dev)
         self.h2 = torch.empty((P, I), dtype=torch.bfloat16, device=dev)
-        self.y2 = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
         self.bound = min(R, FEW_TOKENS) if R <= DECODE_TOKENS else 0
+        if self.bound:
+            # decode-sized receives: the few-token matvec writes y2, a return kernel sends its rows
+            self.y2 = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
+        else:
+            # the grouped GEMM's epilogue stores each row in its source's return buffer itself
+            self.row_dst = torch.empty(P, dtype=torch.int64, device=dev)
         self.side = torch.cuda.Stream(device=dev)
         # the arena, mapped by every peer
         self.lay = arena_layout(W, T, K, H, sp.n_shared)
@@ -217,6 +224,9 @@ class PeerExpertParallelMoE:
                                     H, int(sp.mode == 4), _ptr(self.xp2), _ptr(self.row_w2), _ptr(self.pair_pos2),
                                     _ptr(self.counts2), _ptr(self.tiles2), _ptr(self.ntiles2), _ptr(self.perm_ws2),
                                     st), "regroup")
+        if not self.bound:
+            _lib.check(L.ck_ep_peer_return_rows(pe, _ptr(self.pair_pos2), self.own["recv_ids"], self.own["recv_tok"],
+                                                _ptr(self.row_dst), st), "ck_ep_peer_return_rows")
         mark("regroup")
         err = ctypes.c_void_p(self.peers.err)
         _lib.check(L.ck_moe_expert_gemm_bounded(1, _ptr(self.w[0]), _ptr(self.w[1]), None, None, sp.matrix_bytes,
@@ -224,14 +234,22 @@ class PeerExpertParallelMoE:
                                                  _ptr(self.row_w2), _ptr(self.tiles2), _ptr(self.ntiles2), self.mt2, I,
                                                  H, 0, self.bound, err, st), "expert gate/up")
         mark("gate_up")
-        _lib.check(L.ck_moe_expert_gemm_bounded(0, _ptr(self.w[2]), None, None, None, sp.matrix_bytes, self.el, 0,
-                                                 _ptr(self.h2), R * K, _ptr(self.y2), R * K, None, _ptr(self.tiles2),
-                                                 _ptr(self.ntiles2), self.mt2, H, I, 1, self.bound, err, st),
-                   "expert down")
-        mark("down")
-        mark("experts")
-        _lib.check(L.ck_ep_peer_return(pe, _ptr(self.y2), _ptr(self.pair_pos2), self.own["recv_ids"],
-                                       self.own["recv_tok"], st), "ck_ep_peer_return")
+        if self.bound:
+            _lib.check(L.ck_moe_expert_gemm_bounded(0, _ptr(self.w[2]), None, None, None, sp.matrix_bytes, self.el,
+                                                     0, _ptr(self.h2), R * K, _ptr(self.y2), R * K, None,
+                                                     _ptr(self.tiles2), _ptr(self.ntiles2), self.mt2, H, I, 1,
+                                                     self.bound, err, st), "expert down")
+            mark("down")
+            mark("experts")
+            _lib.check(L.ck_ep_peer_return(pe, _ptr(self.y2), _ptr(self.pair_pos2), self.own["recv_ids"],
+                                           self.own["recv_tok"], st), "ck_ep_peer_return")
+        else:
+            # down projection and return in one kernel: each output row goes over NVLink to its source
+            _lib.check(L.ck_moe_expert_gemm_rows(_ptr(self.w[2]), sp.matrix_bytes, self.el, _ptr(self.h2), R * K,
+                                                  _ptr(self.row_dst), R * K, _ptr(self.tiles2), _ptr(self.ntiles2),
+                                                  self.mt2, H, I, 1, err, st), "expert down + return")
+            mark("down")
+            mark("experts")
         _lib.check(L.ck_ep_peer_signal(pe, 1, st), "ck_ep_peer_signal")
         _lib.check(L.ck_ep_peer_wait(pe, 1, WAIT_NS, st), "ck_ep_peer_wait")
         mark("return")

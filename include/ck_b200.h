@@ -192,6 +192,17 @@ int ck_moe_expert_gemm_bounded(int dual, const void *w0_dev, const void *w1_dev,
                                const float *row_w_dev, const void *tiles_dev, const int32_t *ntiles_dev,
                                uint32_t max_tiles, uint32_t n, uint32_t k, int xrow_is_orow,
                                uint32_t max_tile_tokens, int *err_dev, void *stream);
+/* The single-matrix grouped GEMM of ck_moe_expert_gemm_bounded (dual = 0, the grouped-GEMM form only)
+ * with output row o stored at the bf16 row whose device address is row_dst_dev[o] rather than in a
+ * contiguous output: the rows may lie in other GPUs' memory mapped into this process.  No counterpart
+ * in the reference (its MoE runs on one device): the expert-parallel layer's down projection writes
+ * each (token, slot) row straight into the source rank's return buffer (row_dst from
+ * ck_ep_peer_return_rows), so the return crosses NVLink while the GEMM runs.  n % 8 == 0 and every
+ * address 16-byte aligned; out_rows bounds o. */
+int ck_moe_expert_gemm_rows(const void *w0_dev, uint64_t w_stride, uint32_t n_routed, const void *x_bf16_dev,
+                            uint32_t x_rows, const unsigned long long *row_dst_dev, uint32_t out_rows,
+                            const void *tiles_dev, const int32_t *ntiles_dev, uint32_t max_tiles, uint32_t n,
+                            uint32_t k, int xrow_is_orow, int *err_dev, void *stream);
 int ck_moe_combine(const void *y_bf16_dev, const int32_t *ids_dev, const float *wts_dev, const int32_t *pair_pos_dev,
                    uint32_t ntok, uint32_t nsel, uint32_t n_shared, uint32_t hidden, int order_by_expert,
                    void *out_bf16_dev, float *out_f32_dev, void *stream);
@@ -261,7 +272,8 @@ void ck_decode_step_destroy(ck_decode_step *step);
  * region `rank` of its destination; the unused rows of that region get expert -1), signal / wait
  * (which = 0), the receiver's ck_moe_permute over world * cap rows and expert GEMMs,
  * ck_ep_peer_return (every computed (row, slot) pair into its source's return buffer at row
- * token * nsel + slot), signal / wait (which = 1), ck_moe_combine.  No host synchronization: the
+ * token * nsel + slot; or ck_ep_peer_return_rows before a down projection that stores its rows there
+ * itself), signal / wait (which = 1), ck_moe_combine.  No host synchronization: the
  * step count is a device value, so a forward can be captured in a CUDA graph.  Every wait is
  * bounded; a timeout sets the error word (20 dispatch, 21 return) and the step's outputs are not
  * valid.  All ranks must run the same sequence of forwards. */
@@ -293,6 +305,12 @@ int ck_ep_peer_signal(const ck_ep_peers *peers, int which, void *stream);
 int ck_ep_peer_wait(const ck_ep_peers *peers, int which, uint64_t limit_ns, void *stream);
 int ck_ep_peer_return(const ck_ep_peers *peers, const void *y2_bf16_dev, const int32_t *pair_pos2_dev,
                       const int32_t *ids_own_dev, const int32_t *tok_own_dev, void *stream);
+/* In place of ck_ep_peer_return when the down projection runs on the grouped GEMM: row_dst_dev
+ * (world * cap * nsel entries, indexed by the permute's pair positions) receives, for every pair
+ * with a local expert, the address of its row token * nsel + slot in its source's return buffer;
+ * ck_moe_expert_gemm_rows over those rows then does the return from its epilogue. */
+int ck_ep_peer_return_rows(const ck_ep_peers *peers, const int32_t *pair_pos2_dev, const int32_t *ids_own_dev,
+                           const int32_t *tok_own_dev, unsigned long long *row_dst_dev, void *stream);
 
 /* ---- one process, several GPUs (no counterpart in the reference): the same expert-parallel layer for
  * a host that owns the box's GPUs itself (the reference runtime with this carrier is one).  A group

@@ -56,3 +56,39 @@ def test_gemm_matches_oracle_fold_exactly_enough():
 def test_prefill_shape_sampled(m):
     rows, cols = workloads.Q4K_PREFILL
     run(rows, cols, m, seed=m, sample_rows=np.unique(np.linspace(0, rows - 1, 48).astype(int)))
+
+
+@pytest.mark.parametrize("rows,cols,ntok", [(1024, 2048, 300), (256, 512, 17), (512, 1408, 200)])
+def test_gemm_rows_scattered_equal_contiguous(rows, cols, ntok):
+    """ck_moe_expert_gemm_rows (output row o stored at the address row_dst[o], the expert-parallel
+    down projection that writes the return itself) gives, row for row, exactly the bits of the
+    contiguous grouped GEMM, with the rows scattered in a shuffled order and nothing else written."""
+    import ctypes
+
+    from coherence_kernel_b200 import _lib
+    from coherence_kernel_b200.ops import _ptr, _stream
+    L = _lib.load()
+    rng = np.random.default_rng(rows + ntok)
+    q = torch.from_numpy(synth.make_q4k(rng, rows * cols)).cuda()
+    x = torch.from_numpy(synth.make_bf16(rng, (ntok, cols)).view(np.int16)).cuda()
+    mt = ntok // 16 + 2
+    tiles = torch.empty((mt, 4), dtype=torch.int32, device="cuda")
+    nt = torch.empty(1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check(L.ck_token_tiles(_ptr(tiles), _ptr(nt), ntok, _stream()), "ck_token_tiles")
+    ref = torch.empty((ntok, rows), dtype=torch.int16, device="cuda")
+    _lib.check(L.ck_moe_expert_gemm_bounded(0, _ptr(q), None, None, None, 0, 1, 0, _ptr(x), ntok, _ptr(ref), ntok,
+                                            None, _ptr(tiles), _ptr(nt), mt, rows, cols, 0, 0, _ptr(err), _stream()),
+               "ck_moe_expert_gemm_bounded")
+    perm = torch.randperm(ntok, generator=torch.Generator().manual_seed(ntok)).cuda()
+    dst = torch.full((ntok + 3, rows), 0x7ABC, dtype=torch.int16, device="cuda")
+    row_dst = (dst.data_ptr() + perm.to(torch.int64) * rows * 2).contiguous()
+    _lib.check(L.ck_moe_expert_gemm_rows(_ptr(q), 0, 1, _ptr(x), ntok, _ptr(row_dst), ntok, _ptr(tiles), _ptr(nt), mt,
+                                         rows, cols, 0, _ptr(err), _stream()), "ck_moe_expert_gemm_rows")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(dst[perm], ref)
+    assert bool((dst[ntok:] == 0x7ABC).all())
+    # the entry refuses a missing row table
+    assert L.ck_moe_expert_gemm_rows(_ptr(q), 0, 1, _ptr(x), ntok, None, ntok, _ptr(tiles), _ptr(nt), mt, rows,
+                                     cols, 0, _ptr(err), _stream()) != 0
