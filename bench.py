@@ -622,6 +622,32 @@ def port_reference(spec, args):
             "sample": f"{nthreads} tokens of the layer per step on the oracle, one per host thread"}
 
 
+def bind_near_gpu(local_rank):
+    """Run this rank on the CPUs nearest its GPU (NVML's CPU affinity for the device) so that its
+    pinned host buffers, allocated afterwards, sit on that GPU's NUMA node: with every rank copying at
+    once, buffers on the far socket throttle the host<->device copies of the end-to-end loop.  Only
+    the process's CPU affinity changes; no GPU setting is touched.  Returns the CPU count bound to,
+    or None where NVML cannot tell."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[local_rank]) if vis else local_rank
+            h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+            cpus = {64 * i + b for i, wd in enumerate(words) for b in range(64) if (int(wd) >> b) & 1}
+            cpus &= os.sched_getaffinity(0)
+            if not cpus:
+                return None
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:
+        return None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -644,6 +670,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    bound_cpus = bind_near_gpu(local)
 
     import torch
     import torch.distributed as dist
@@ -881,7 +908,8 @@ def main():
         # exchange (1) and gathers the dispatch rows (1) in place of the source permute, regroups on
         # the receiver (permute 3), restores the pair order (1), and runs the shared expert's token
         # tiles + 2 GEMMs per shared expert on a side stream
-        # over peer memory: begin, route 8, plan, dispatch, signal, wait, regroup 3, GEMM 2, return,
+        # over peer memory: begin, route 8, plan, dispatch, signal, wait, regroup 3, GEMM 2, return (or
+        # the down GEMM's row table when that GEMM stores the return itself),
         # signal, wait, combine, + the shared expert's token tiles and 2 GEMMs per shared expert
         launches_per_step = (14 if world == 1 else 17 + 1 + 2 * spec.n_shared if args.exchange == "nccl"
                              else 22 + 1 + 2 * spec.n_shared)
@@ -891,7 +919,9 @@ def main():
                 "data": "synthetic",
                 "config": {"workload": WORKLOAD, "tokens": T_all, "tokens_per_gpu": T,
                            "experts_per_gpu": el, "parallelism": f"ep{world}" if world > 1 else "single",
-                           "l2": "weights 6.37 GB >> 126 MB L2 (no flush needed)"},
+                           "l2": "weights 6.37 GB >> 126 MB L2 (no flush needed)",
+                           "host_binding": (f"each rank on the {bound_cpus} CPUs nearest its GPU (NVML affinity)"
+                                            if bound_cpus else "none")},
                 "weight_stream_gbs": round(weight_bytes / (ms_step / 1e3) / 1e9, 1),
                 "algorithmic_tflops": round(T_all * spec.flops_per_token() / (ms_step / 1e3) / 1e12, 1),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
