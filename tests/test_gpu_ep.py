@@ -142,3 +142,76 @@ def test_ep_dispatch_plan_matches_host_rules(world, E, K, T):
     assert torch.equal(send_tok[:S], tok)
     assert torch.equal(meta[:S], torch.cat([me, mw.view(torch.int32)], dim=1))
     assert torch.equal(ret_pos, ep_return_positions(ids, el))
+
+
+@pytest.mark.parametrize("cap,K,H,I", [(96, 4, 1024, 512), (40, 8, 7168, 2048)])
+def test_fused_return_equals_return_kernel(cap, K, H, I):
+    """On one GPU, with both 'ranks' of a two-rank peer table in local memory: the down projection
+    that stores its rows through ck_ep_peer_return_rows' table (ck_moe_expert_gemm_rows) fills the
+    return buffers with exactly the bits of the contiguous down projection followed by
+    ck_ep_peer_return -- the same rows at the same (token, slot) places, nothing else written."""
+    import ctypes
+
+    from coherence_kernel_b200 import _lib, synth
+    from coherence_kernel_b200.ep_peer import EpPeers
+    from coherence_kernel_b200.ops import _ptr, _stream
+    L, W = _lib.load(), 2
+    g = torch.Generator().manual_seed(cap * K)
+    rows = W * cap
+    # received rows: each source's rows carry distinct tokens; about half the slots have a local expert
+    ids_own = torch.where(torch.rand(rows, K, generator=g) < 0.5, 0, -1).to(torch.int32)
+    tok_own = torch.cat([torch.randperm(cap, generator=g) for _ in range(W)]).to(torch.int32)
+    valid = (ids_own.reshape(-1) >= 0).nonzero().reshape(-1)
+    npairs = int(valid.numel())
+    pair_pos2 = torch.full((rows * K,), -1, dtype=torch.int32)
+    pair_pos2[valid] = torch.randperm(npairs, generator=g).to(torch.int32)
+    ids_own, tok_own, pair_pos2 = ids_own.cuda(), tok_own.cuda(), pair_pos2.cuda()
+    rng = np.random.default_rng(cap + K)
+    w = torch.from_numpy(synth.make_q4k(rng, H * I)).cuda()
+    h2 = torch.from_numpy(synth.make_bf16(rng, (npairs, I)).view(np.int16)).cuda()
+    mt = npairs // 16 + 2
+    tiles = torch.empty((mt, 4), dtype=torch.int32, device="cuda")
+    nt = torch.empty(1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = _stream()
+    _lib.check(L.ck_token_tiles(_ptr(tiles), _ptr(nt), npairs, st), "ck_token_tiles")
+    keep = []  # buffers the peer table points at
+
+    def table(ret):
+        pe = EpPeers()
+        pe.world, pe.rank, pe.cap, pe.nsel, pe.hidden = W, 0, cap, K, H
+        for d in range(W):
+            for name, n, dt in (("recv_x", cap * H, torch.int16), ("recv_ids", cap * K, torch.int32),
+                                ("recv_w", cap * K, torch.float32), ("recv_tok", cap, torch.int32),
+                                ("dflag", 1, torch.int64), ("rflag", 1, torch.int64)):
+                b = torch.zeros(n, dtype=dt, device="cuda")
+                keep.append(b)
+                getattr(pe, name)[d] = b.data_ptr()
+            pe.ret_y[d] = ret[d].data_ptr()
+        for name in ("my_dflags", "my_rflags", "ctr", "err"):
+            b = torch.zeros(W, dtype=torch.int64, device="cuda")
+            keep.append(b)
+            setattr(pe, name, b.data_ptr())
+        return pe
+
+    # the return kernel after the contiguous down projection
+    ret_a = [torch.zeros((cap * K, H), dtype=torch.int16, device="cuda") for _ in range(W)]
+    y2 = torch.empty((npairs, H), dtype=torch.int16, device="cuda")
+    _lib.check(L.ck_moe_expert_gemm_bounded(0, _ptr(w), None, None, None, 0, 1, 0, _ptr(h2), npairs, _ptr(y2), npairs,
+                                            None, _ptr(tiles), _ptr(nt), mt, H, I, 0, 0, _ptr(err), st), "down")
+    pa = table(ret_a)
+    _lib.check(L.ck_ep_peer_return(ctypes.byref(pa), _ptr(y2), _ptr(pair_pos2), _ptr(ids_own), _ptr(tok_own), st),
+               "ck_ep_peer_return")
+    # the down projection storing its rows itself
+    ret_b = [torch.zeros((cap * K, H), dtype=torch.int16, device="cuda") for _ in range(W)]
+    pb = table(ret_b)
+    row_dst = torch.zeros(rows * K, dtype=torch.int64, device="cuda")
+    _lib.check(L.ck_ep_peer_return_rows(ctypes.byref(pb), _ptr(pair_pos2), _ptr(ids_own), _ptr(tok_own),
+                                        _ptr(row_dst), st), "ck_ep_peer_return_rows")
+    _lib.check(L.ck_moe_expert_gemm_rows(_ptr(w), 0, 1, _ptr(h2), npairs, _ptr(row_dst), npairs, _ptr(tiles), _ptr(nt),
+                                         mt, H, I, 0, _ptr(err), st), "ck_moe_expert_gemm_rows")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for d in range(W):
+        assert torch.equal(ret_a[d], ret_b[d])
+    assert int(sum((r != 0).any(dim=1).sum() for r in ret_a)) == npairs  # every pair row landed once
