@@ -207,11 +207,21 @@ int member_forward(ck_ep_group *g, uint32_t d, uint32_t T, int phase) {
         if (!rc)
             rc = ck_moe_expert_gemm_bounded(1, m.wg, m.wu, nullptr, nullptr, mb, g->el, 0, m.xp2, R * K, m.h2, R * K,
                                             m.row_w2, m.tiles2, m.ntiles2, m.mt2, I, H, 0, bound, pe->err, s);
-        if (!rc)
-            rc = ck_moe_expert_gemm_bounded(0, m.wd, nullptr, nullptr, nullptr, mb, g->el, 0, m.h2, R * K, m.y2, R * K,
-                                            nullptr, m.tiles2, m.ntiles2, m.mt2, H, I, 1, bound, pe->err, s);
-        if (!rc)
-            rc = ck_ep_peer_return(pe, m.y2, m.pair_pos2, rids, (const int32_t *)(m.arena + m.a_recv_tok), s);
+        const int32_t *rtok = (const int32_t *)(m.arena + m.a_recv_tok);
+        if (bound) {
+            if (!rc)
+                rc = ck_moe_expert_gemm_bounded(0, m.wd, nullptr, nullptr, nullptr, mb, g->el, 0, m.h2, R * K, m.y2,
+                                                R * K, nullptr, m.tiles2, m.ntiles2, m.mt2, H, I, 1, bound, pe->err, s);
+            if (!rc) rc = ck_ep_peer_return(pe, m.y2, m.pair_pos2, rids, rtok, s);
+        } else {
+            // the down projection stores every row in its source's return buffer itself; the row
+            // table (8 bytes a pair) lives in the y2 block, which it does not otherwise need
+            unsigned long long *row_dst = reinterpret_cast<unsigned long long *>(m.y2);
+            if (!rc) rc = ck_ep_peer_return_rows(pe, m.pair_pos2, rids, rtok, row_dst, s);
+            if (!rc)
+                rc = ck_moe_expert_gemm_rows(m.wd, mb, g->el, m.h2, R * K, row_dst, R * K, m.tiles2, m.ntiles2, m.mt2,
+                                             H, I, 1, pe->err, s);
+        }
         if (!rc) rc = ck_ep_peer_signal(pe, 1, s);
         return rc;
     }
