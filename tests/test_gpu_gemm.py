@@ -58,7 +58,7 @@ def test_prefill_shape_sampled(m):
     run(rows, cols, m, seed=m, sample_rows=np.unique(np.linspace(0, rows - 1, 48).astype(int)))
 
 
-@pytest.mark.parametrize("rows,cols,ntok", [(1024, 2048, 300), (256, 512, 17), (512, 1408, 200)])
+@pytest.mark.parametrize("rows,cols,ntok", [(1024, 2048, 300), (256, 512, 17), (512, 1408, 200), (200, 512, 33)])
 def test_gemm_rows_scattered_equal_contiguous(rows, cols, ntok):
     """ck_moe_expert_gemm_rows (output row o stored at the address row_dst[o], the expert-parallel
     down projection that writes the return itself) gives, row for row, exactly the bits of the
