@@ -112,7 +112,9 @@ def test_expert_parallel_matches_single_gpu(name, world, ntok, transport):
     assert verdict == "ok", info
 
 
-@pytest.mark.parametrize("world,E,K,T", [(2, 16, 4, 300), (8, 256, 8, 1500), (4, 64, 8, 2048), (3, 48, 6, 1025)])
+@pytest.mark.parametrize("world,E,K,T", [(2, 16, 4, 300), (8, 256, 8, 1500), (4, 64, 8, 2048), (3, 48, 6, 1025),
+                                         (2, 256, 8, 4096), (4, 256, 8, 2048), (8, 256, 8, 1024), (8, 256, 8, 16),
+                                         (8, 256, 8, 1)])
 def test_ep_dispatch_plan_matches_host_rules(world, E, K, T):
     """The device plan (one CTA) equals the host rules the gloo test exercises: pairs per expert,
     rows and pairs per rank, the dispatch rows in (rank, token) order with their metadata, and the
